@@ -1,0 +1,102 @@
+/* tokmix.h -- C ABI of libtokmix.so, the sm_100a (B200) prefill token-mixer kernels.
+ *
+ * Two entry points replace the two kernel extensions the reference's plugin modules bind:
+ *
+ *   tokmix_fa2_fwd      replaces  flash_attention_2_forward(q, k, v, sm_scale, causal)
+ *                       kernels_optimized/flash_attention_2.cu:1121-1258, bound at
+ *                       kernels_optimized/flash_attention_2.py:139-140 (kernel_fn)
+ *   tokmix_gdn_prefill  replaces  qwen35moe_gdn_prefill_bf16tc(q, k, v, g, beta, state, scale)
+ *                       kernels_optimized/qwen35moe_gdn_prefill.cu:1203-1264, bound at
+ *                       kernels_optimized/qwen35moe_gdn_prefill.py:149-161 (kernel_fn)
+ *
+ * Conventions (all entry points):
+ *   - every pointer argument except `status` and the cu_seqlens host copy is DEVICE memory of
+ *     the current device; the library allocates and frees no device memory (TMEM is allocated
+ *     and released inside each kernel);
+ *   - work is enqueued on `stream` (a cudaStream_t; NULL = legacy default stream) and the call
+ *     returns without synchronising;
+ *   - the return value is TOKMIX_OK or one of the TOKMIX_ERR_* codes; the text of the last
+ *     error of the calling thread is returned by tokmix_last_error();
+ *   - `status` (optional, device memory, one uint32 initialised to 0 by the caller) receives
+ *     the kernels' device-side status bits: every pipeline wait inside a kernel is bounded, and
+ *     a wait that runs out sets a TOKMIX_DEV_* bit here and ends the kernel early instead of
+ *     hanging the GPU.  The caller reads it after synchronising.
+ */
+#ifndef TOKMIX_H_
+#define TOKMIX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* return codes */
+#define TOKMIX_OK 0
+#define TOKMIX_ERR_INVALID_ARGUMENT 1 /* shape / pointer / alignment argument rejected */
+#define TOKMIX_ERR_UNSUPPORTED 2      /* valid request this build has no kernel for */
+#define TOKMIX_ERR_LAUNCH 3           /* the CUDA launch itself failed */
+#define TOKMIX_ERR_DEVICE 4           /* wrong device (needs compute capability 10.0) */
+
+/* device status bits written into *status by the kernels */
+#define TOKMIX_DEV_TIMEOUT_TMA 0x1u
+#define TOKMIX_DEV_TIMEOUT_MMA 0x2u
+#define TOKMIX_DEV_TIMEOUT_PIPE 0x4u
+#define TOKMIX_DEV_BAD_ARGS 0x8u
+
+/* tensor layouts for attention */
+#define TOKMIX_LAYOUT_BHSD 0 /* [batch, heads, seq, head_dim]  (the reference's contract) */
+#define TOKMIX_LAYOUT_BSHD 1 /* [batch, seq, heads, head_dim] */
+
+/* element types */
+#define TOKMIX_DTYPE_BF16 0
+#define TOKMIX_DTYPE_FP32 1
+
+/* Causal / non-causal attention forward, bf16 in and out, fp32 softmax and accumulation.
+ *
+ *   o = softmax(q k^T * sm_scale + mask) v
+ *
+ * q, o: [batch, heads_q, seqlen_q, head_dim] (BHSD) or [batch, seqlen_q, heads_q, head_dim] (BSHD)
+ * k, v: same layout with heads_kv and seqlen_kv.  Contiguous; base pointers 16-byte aligned.
+ * heads_q must be a multiple of heads_kv; query head h reads key/value head h / (heads_q/heads_kv).
+ * head_dim in {64, 128}.  causal != 0 masks key j for query i when j > i (top-left aligned, as
+ * torch's scaled_dot_product_attention(is_causal=True)).
+ * Replaces flash_attention_2_forward (kernels_optimized/flash_attention_2.cu:1121-1258), which
+ * supported only BHSD, heads_q == heads_kv and head_dim == 128. */
+int tokmix_fa2_fwd(const void* q, const void* k, const void* v, void* o, int batch, int heads_q, int heads_kv,
+                   int seqlen_q, int seqlen_kv, int head_dim, int layout, int causal, float sm_scale,
+                   uint32_t* status, void* stream);
+
+/* Gated-delta-rule (GDN) prefill, chunked on the tensor cores.
+ *
+ * Token layout: q, k [total_tokens, heads_k, 128]; v, out [total_tokens, heads_v, 128];
+ * g, beta [total_tokens, heads_v] fp32 (g is the log decay, beta the write strength).
+ * A batch [B, T, ...] is the same memory with total_tokens = B*T and B sequences of T tokens.
+ * Sequence n covers tokens [cu_seqlens[n], cu_seqlens[n+1]).
+ * State layout: initial_state / final_state [num_seqs, heads_v, 128 (v), 128 (k)] fp32
+ * (initial_state may be NULL for a zero initial state; final_state may alias initial_state).
+ * Value head h reads key head h % heads_k (as kernels/qwen35moe_gdn_prefill.cu:48).
+ * io_dtype is the type of q, k, v and out: TOKMIX_DTYPE_BF16 (the only one this build runs).
+ *
+ * cu_seqlens_dev:   device int32 [num_seqs + 1]
+ * seq_order_dev:    device int32 [num_seqs], the order in which sequences are scheduled
+ *                   (longest first balances the GPU); may be NULL for 0..num_seqs-1.
+ * Replaces qwen35moe_gdn_prefill_bf16tc (kernels_optimized/qwen35moe_gdn_prefill.cu:1203-1264),
+ * which supported only fp32 I/O, a batch of equal lengths, heads_k=16, heads_v=32. */
+int tokmix_gdn_prefill(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                       const float* initial_state, void* out, float* final_state, const int32_t* cu_seqlens_dev,
+                       const int32_t* seq_order_dev, int num_seqs, int total_tokens, int heads_k, int heads_v,
+                       int head_dim_k, int head_dim_v, float scale, int io_dtype, uint32_t* status, void* stream);
+
+/* Text of the last error reported on the calling thread ("" if none). */
+const char* tokmix_last_error(void);
+
+/* Library version string, e.g. "tokmix 0.1.0 sm_100a". */
+const char* tokmix_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TOKMIX_H_ */

@@ -1,0 +1,768 @@
+// gdn_prefill.cu -- chunked gated-delta-rule prefill for sm_100a (B200).
+//
+// Reference path replaced: kernels_optimized/qwen35moe_gdn_prefill.cu:683-1161 (precompute +
+// chunk-scan kernels) behind qwen35moe_gdn_prefill_bf16tc (:1203-1264).  Maths: the fp32
+// recurrence kernels/qwen35moe_gdn_prefill.cu:55-99 (value head h reads key head h % Hk,
+// state layout [v][k], output computed with the updated state).
+//
+// Chunked form used here (C = 64 tokens, in-chunk cumulative log decay G_t, incoming state S0):
+//   L_ts  = beta_t exp(G_t - G_s) (k_t . k_s)          s < t
+//   T     = (I + L)^-1 diag(beta)                      (unit-lower inverse, fp32, blocked 16x16)
+//   W     = T diag(e^G) K                              (tensor core)
+//   Delta = T V - W S0^T                               (tensor core; T split into bf16 hi + lo)
+//   O     = scale (diag(e^G) Q S0^T + P Delta),  P_ts = exp(G_t - G_s)(q_t . k_s), s <= t
+//   S     = e^{G_C} S0 + (diag(e^{G_C - G}) Delta)^T K (tensor core; Delta' split hi + lo)
+// Every contraction is an M=128 tcgen05 MMA because the CTA keeps the VALUE dimension on the
+// 128 TMEM lanes ("transposed" products: Delta^T, O^T, S with lane = value row; W^T with
+// lane = key row).  The fp32 master state never leaves TMEM between chunks; a bf16 copy in
+// shared memory is the MMA operand for the next chunk.
+//
+// One CTA processes one (sequence, value head) unit, all its chunks in order.  Warp roles:
+//   warps 0-3   state chain: Delta pass (Delta -> bf16 operands in TMEM), state pass (S ->
+//               bf16 shared copy, pre-scale by the next chunk's decay), initial/final state
+//   warps 4-7   operands: decay prefix sums, QK/KK read-out (P tile, e^G-scaled Q, L rows),
+//               W pass (W^T -> -W bf16 tile), output pass (O^T -> global)
+//   warps 8-11  blocked triangular solve -> T (hi/lo) and T diag(e^G) tiles
+//   warp 12     TMA producer (stacked Q/K chunk tile, V chunk tile)
+//   warp 13     TMEM owner and MMA issuer; it polls the hand-off barriers and issues the next
+//               ready MMA group, critical-path groups first, so the state chain never waits
+//               behind the next chunk's preparation.
+// Hand-off barriers are two-slot arrays indexed by chunk parity.  All waits are bounded.
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "host_common.h"
+#include "sm100.cuh"
+
+namespace tokmix {
+namespace gdn {
+
+constexpr int kC = 64;     // tokens per chunk
+constexpr int kD = 128;    // head dim (keys and values)
+constexpr int kThreads = 448;
+constexpr int kWarpTma = 12;
+constexpr int kWarpMma = 13;
+
+// TMEM columns
+constexpr uint32_t kColS = 0;      // state S[v][k] fp32, 128 cols
+constexpr uint32_t kColX0 = 128;   // Delta^T fp32 (64 cols) then bf16 A operands (96 cols), 2 slots
+constexpr uint32_t kColX1 = 224;
+constexpr uint32_t kColO = 320;    // O^T fp32, 64 cols
+constexpr uint32_t kColW = 384;    // W^T fp32 (lane = key row), 64 cols
+constexpr uint32_t kColQK = 448;   // lanes 0-63: Q K^T, lanes 64-127: K K^T, 64 cols
+
+// shared memory layout (bytes, 1024-aligned tiles)
+constexpr int kSlotBytes = 32768;                  // stacked [Q;K] chunk tile: 2 boxes of 128 rows x 128 B
+constexpr int kOffSlot0 = 0;
+constexpr int kOffSlot1 = kSlotBytes;
+constexpr int kOffV = 2 * kSlotBytes;              // V chunk tile: 2 boxes of 64 rows x 128 B
+constexpr int kOffP0 = kOffV + 16384;              // P tiles [t][s] bf16, 2 slots
+constexpr int kOffP1 = kOffP0 + 8192;
+constexpr int kOffThi = kOffP1 + 8192;             // T hi [t][s]
+constexpr int kOffTlo = kOffThi + 8192;            // T lo
+constexpr int kOffTG = kOffTlo + 8192;             // T diag(e^G)
+constexpr int kOffWneg = kOffTG + 8192;            // -W as [k][t], 128 rows x 128 B
+constexpr int kOffS0 = kOffWneg + 16384;           // bf16 state copies [v][k]: 2 boxes of 128 rows x 128 B
+constexpr int kOffS1 = kOffS0 + 32768;
+constexpr int kOffScratch = kOffS1 + 32768;        // solve scratch fp32 [64][kScStride]
+constexpr int kScStride = 68;
+constexpr int kOffParams = kOffScratch + 64 * kScStride * 4;
+constexpr int kParamsBytes = 1280;
+constexpr int kSmemBytes = kOffParams + 2 * kParamsBytes;  // + 2 parameter slots
+
+struct ChunkParams {
+  float beta[kC];         // write strength (0 for tokens past the sequence end)
+  float g2[kC];           // in-chunk inclusive prefix sum of g, in log2 units
+  float eg[kC];           // exp(G_t)
+  float egr[kC];          // exp(G_C - G_t) (0 past the end)
+  float gamma_c;          // exp(G_C)
+  int n_valid;
+  int pad[62];
+};
+static_assert(sizeof(ChunkParams) == kParamsBytes, "params slot size");
+
+struct Params {
+  const float* g;
+  const float* beta;
+  const float* state_in;
+  float* state_out;
+  __nv_bfloat16* out;
+  const int32_t* cu_seqlens;
+  const int32_t* seq_order;
+  int hk, hv;
+  float scale;
+  uint32_t* status;
+};
+
+struct Barriers {
+  uint64_t in_full[2], v_full[2], slot_free[2], v_free[2];
+  uint64_t qk_done[2], qk_read[2], g_ready[2], prep1[2];
+  uint64_t w_done[2], wneg[2], delta[2], da_done[2];
+  uint64_t snew[2], s_ready[2], o_done[2], o_free[2];
+};
+
+__device__ __forceinline__ bool wait_c(uint64_t* bars, int c, uint32_t* status, uint32_t code) {
+  return mbar_wait(&bars[c & 1], (c >> 1) & 1, status, code);
+}
+__device__ __forceinline__ bool test_c(uint64_t* bars, int c) { return mbar_test(&bars[c & 1], (c >> 1) & 1); }
+
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// write 64 bf16 values (packed as 32 uint32) as row `row` of a 128-byte-swizzled tile
+__device__ __forceinline__ void store_row_sw128(uint8_t* tile, int row, const uint32_t (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4 val = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    *reinterpret_cast<uint4*>(tile + row * 128 + ((j ^ (row & 7)) << 4)) = val;
+  }
+}
+
+__device__ __forceinline__ float bf16_lo_part(float x, uint32_t& hi_bits) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(x);
+  hi_bits = __bfloat16_as_ushort(h);
+  return x - __bfloat162float(h);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gdn_prefill_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ Barriers bars;
+  __shared__ uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_shared;
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int unit = blockIdx.x;
+  const int order = unit / p.hv;
+  const int h = unit - order * p.hv;
+  const int seq = p.seq_order ? p.seq_order[order] : order;
+  const int kh = h % p.hk;
+  const int tok0 = p.cu_seqlens[seq];
+  const int len = p.cu_seqlens[seq + 1] - tok0;
+  const int nchunks = len > 0 ? (len + kC - 1) / kC : 0;
+  ChunkParams* params = reinterpret_cast<ChunkParams*>(smem + kOffParams);
+  float* scratch = reinterpret_cast<float*>(smem + kOffScratch);
+  const size_t state_off = (static_cast<size_t>(seq) * p.hv + h) * kD * kD;
+
+  if (threadIdx.x == 0) {
+    uint64_t* all = reinterpret_cast<uint64_t*>(&bars);
+    for (int i = 0; i < static_cast<int>(sizeof(Barriers) / 8); ++i) mbar_init(&all[i], 1);
+    mbar_init(&drain_bar, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.qk_read[i], 128);
+      mbar_init(&bars.g_ready[i], 32);
+      mbar_init(&bars.prep1[i], 128);
+      mbar_init(&bars.wneg[i], 128);
+      mbar_init(&bars.da_done[i], 128);
+      mbar_init(&bars.s_ready[i], 128);
+      mbar_init(&bars.o_free[i], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(&tmem_base_shared, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base_shared;
+
+  if (nchunks == 0) {
+    // empty sequence: final state = initial state
+    if (warp < 4) {
+      const int v = threadIdx.x;
+      for (int kk = 0; kk < kD; kk += 4) {
+        float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (p.state_in) val = *reinterpret_cast<const float4*>(p.state_in + state_off + v * kD + kk);
+        *reinterpret_cast<float4*>(p.state_out + state_off + v * kD + kk) = val;
+      }
+    }
+  } else if (warp < 4) {
+    // =========================================================== state chain (lane = value row)
+    const int v = threadIdx.x;
+    const uint32_t lane_base = tmem_addr(tbase, warp * 32, 0);
+    bool ok = true;
+    // --- initial state: bf16 copy -> S slot 0, TMEM S <- gamma_C(0) * S0
+    ok = wait_c(bars.g_ready, 0, p.status, kDevTimeoutPipe);
+    if (ok) {
+      const float gam = params[0].gamma_c;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sv[64];
+#pragma unroll
+        for (int j = 0; j < 64; j += 4) {
+          float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (p.state_in) val = *reinterpret_cast<const float4*>(p.state_in + state_off + v * kD + half * 64 + j);
+          sv[j] = __float_as_uint(val.x);
+          sv[j + 1] = __float_as_uint(val.y);
+          sv[j + 2] = __float_as_uint(val.z);
+          sv[j + 3] = __float_as_uint(val.w);
+        }
+        uint32_t packed[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) packed[j] = pack_bf16x2(__uint_as_float(sv[2 * j]), __uint_as_float(sv[2 * j + 1]));
+        store_row_sw128(smem + kOffS0 + half * 16384, v, packed);
+#pragma unroll
+        for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
+        tmem_st32(lane_base + kColS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_st32(lane_base + kColS + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      }
+      fence_async_smem();
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars.s_ready[0]);
+    }
+    for (int c = 0; ok && c < nchunks; ++c) {
+      const ChunkParams& pc = params[c & 1];
+      const uint32_t colx = (c & 1) ? kColX1 : kColX0;
+      // --- Delta pass
+      if (!wait_c(bars.delta, c, p.status, kDevTimeoutMma)) { ok = false; break; }
+      tc_fence_after();
+      {
+        uint32_t d[64];
+        tmem_ld64(lane_base + colx, d);
+        uint32_t pk[32], hi[32], lo[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float d0 = __uint_as_float(d[2 * j]);
+          const float d1 = __uint_as_float(d[2 * j + 1]);
+          pk[j] = pack_bf16x2(d0, d1);
+          const float e0 = d0 * pc.egr[2 * j];
+          const float e1 = d1 * pc.egr[2 * j + 1];
+          uint32_t h0, h1;
+          const float l0 = bf16_lo_part(e0, h0);
+          const float l1 = bf16_lo_part(e1, h1);
+          hi[j] = h0 | (h1 << 16);
+          lo[j] = pack_bf16x2(l0, l1);
+        }
+        tmem_st32(lane_base + colx, pk);
+        tmem_st32(lane_base + colx + 32, hi);
+        tmem_st32(lane_base + colx + 64, lo);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      mbar_arrive(&bars.da_done[c & 1]);
+      // --- state pass
+      if (!wait_c(bars.snew, c, p.status, kDevTimeoutMma)) { ok = false; break; }
+      tc_fence_after();
+      const bool last = (c == nchunks - 1);
+      float gam = 1.0f;
+      if (!last) {
+        if (!wait_c(bars.g_ready, c + 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
+        gam = params[(c + 1) & 1].gamma_c;
+      }
+      uint8_t* sdst = smem + (((c + 1) & 1) ? kOffS1 : kOffS0);
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sv[64];
+        tmem_ld64(lane_base + kColS + half * 64, sv);
+        if (last) {
+          float* dst = p.state_out + state_off + v * kD + half * 64;
+#pragma unroll
+          for (int j = 0; j < 64; j += 4)
+            *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
+                                                              __uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3]));
+        } else {
+          uint32_t packed[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            packed[j] = pack_bf16x2(__uint_as_float(sv[2 * j]), __uint_as_float(sv[2 * j + 1]));
+          store_row_sw128(sdst + half * 16384, v, packed);
+#pragma unroll
+          for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
+          tmem_st32(lane_base + kColS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_st32(lane_base + kColS + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        }
+      }
+      if (!last) {
+        fence_async_smem();
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bars.s_ready[(c + 1) & 1]);
+      }
+    }
+  } else if (warp < 8) {
+    // =========================================================== operand warps
+    const int r = threadIdx.x - 128;  // TMEM lane / row owned by this thread
+    const uint32_t lane_base = tmem_addr(tbase, (warp & 3) * 32, 0);
+    bool ok = true;
+    for (int c = 0; ok && c < nchunks; ++c) {
+      ChunkParams& pc = params[c & 1];
+      // --- (1) decay prefix sums for chunk c (warp 4)
+      if (warp == 4) {
+        if (c >= 2 && !wait_c(bars.da_done, c - 2, p.status, kDevTimeoutPipe)) { ok = false; break; }
+        const int n_valid = min(kC, len - c * kC);
+        const int t0 = 2 * lane, t1 = 2 * lane + 1;
+        const size_t base = static_cast<size_t>(tok0 + c * kC);
+        const float ga = t0 < n_valid ? p.g[(base + t0) * p.hv + h] : 0.0f;
+        const float gb = t1 < n_valid ? p.g[(base + t1) * p.hv + h] : 0.0f;
+        const float ba = t0 < n_valid ? p.beta[(base + t0) * p.hv + h] : 0.0f;
+        const float bb = t1 < n_valid ? p.beta[(base + t1) * p.hv + h] : 0.0f;
+        float incl = ga + gb;  // inclusive scan of pair sums
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const float o = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += o;
+        }
+        const float G0 = incl - gb;
+        const float G1 = incl;
+        const float GC = __shfl_sync(0xffffffffu, incl, 31);
+        constexpr float kLog2e = 1.4426950408889634f;
+        pc.beta[t0] = ba;
+        pc.beta[t1] = bb;
+        pc.g2[t0] = G0 * kLog2e;
+        pc.g2[t1] = G1 * kLog2e;
+        pc.eg[t0] = t0 < n_valid ? expf(G0) : 0.0f;
+        pc.eg[t1] = t1 < n_valid ? expf(G1) : 0.0f;
+        pc.egr[t0] = t0 < n_valid ? expf(GC - G0) : 0.0f;
+        pc.egr[t1] = t1 < n_valid ? expf(GC - G1) : 0.0f;
+        if (lane == 0) {
+          pc.gamma_c = expf(GC);
+          pc.n_valid = n_valid;
+        }
+        __syncwarp();
+        mbar_arrive(&bars.g_ready[c & 1]);
+      }
+      // --- (2) QK / KK read-out: P tile, e^G-scaled Q (in place), L rows -> scratch
+      if (!wait_c(bars.qk_done, c, p.status, kDevTimeoutMma)) { ok = false; break; }
+      if (!wait_c(bars.g_ready, c, p.status, kDevTimeoutPipe)) { ok = false; break; }
+      if (c >= 1 && !wait_c(bars.prep1, c - 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
+      if (c >= 2 && !wait_c(bars.o_done, c - 2, p.status, kDevTimeoutMma)) { ok = false; break; }
+      tc_fence_after();
+      {
+        uint32_t row[64];
+        tmem_ld64(lane_base + kColQK, row);
+        if (r < 64) {
+          const int t = r;
+          const float gt = pc.g2[t];
+          uint32_t packed[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int s0 = 2 * j, s1 = 2 * j + 1;
+            const float p0 = s0 <= t ? __uint_as_float(row[s0]) * ex2_approx(gt - pc.g2[s0]) : 0.0f;
+            const float p1 = s1 <= t ? __uint_as_float(row[s1]) * ex2_approx(gt - pc.g2[s1]) : 0.0f;
+            packed[j] = pack_bf16x2(p0, p1);
+          }
+          store_row_sw128(smem + ((c & 1) ? kOffP1 : kOffP0), t, packed);
+          // Q row t lives in rows 0..63 of the stacked slot, 2 boxes of 64 columns
+          uint8_t* slot = smem + ((c & 1) ? kOffSlot1 : kOffSlot0);
+          const float eg = pc.eg[t];
+#pragma unroll
+          for (int bx = 0; bx < 2; ++bx) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              uint4* ptr = reinterpret_cast<uint4*>(slot + bx * 16384 + t * 128 + ((j ^ (t & 7)) << 4));
+              uint4 val = *ptr;
+              uint32_t* w = reinterpret_cast<uint32_t*>(&val);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                __nv_bfloat162 b2 = *reinterpret_cast<__nv_bfloat162*>(&w[e]);
+                const float2 f = __bfloat1622float2(b2);
+                w[e] = pack_bf16x2(f.x * eg, f.y * eg);
+              }
+              *ptr = val;
+            }
+          }
+        } else {
+          const int t = r - 64;
+          const float gt = pc.g2[t];
+          const float bt = pc.beta[t];
+          float* dst = scratch + t * kScStride;
+#pragma unroll
+          for (int s = 0; s < 64; s += 4) {
+            float4 val;
+            val.x = s + 0 < t ? bt * ex2_approx(gt - pc.g2[s + 0]) * __uint_as_float(row[s + 0]) : 0.0f;
+            val.y = s + 1 < t ? bt * ex2_approx(gt - pc.g2[s + 1]) * __uint_as_float(row[s + 1]) : 0.0f;
+            val.z = s + 2 < t ? bt * ex2_approx(gt - pc.g2[s + 2]) * __uint_as_float(row[s + 2]) : 0.0f;
+            val.w = s + 3 < t ? bt * ex2_approx(gt - pc.g2[s + 3]) * __uint_as_float(row[s + 3]) : 0.0f;
+            *reinterpret_cast<float4*>(dst + s) = val;
+          }
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars.qk_read[c & 1]);
+      // --- (3) W pass: W^T (lane = key row k) -> -W as [k][t] bf16
+      if (!wait_c(bars.w_done, c, p.status, kDevTimeoutMma)) { ok = false; break; }
+      if (c >= 1 && !wait_c(bars.delta, c - 1, p.status, kDevTimeoutMma)) { ok = false; break; }
+      tc_fence_after();
+      {
+        uint32_t row[64];
+        tmem_ld64(lane_base + kColW, row);
+        uint32_t packed[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          packed[j] = pack_bf16x2(-__uint_as_float(row[2 * j]), -__uint_as_float(row[2 * j + 1]));
+        store_row_sw128(smem + kOffWneg, r, packed);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars.wneg[c & 1]);
+      // --- (4) output pass of the previous chunk
+      if (c >= 1) {
+        if (!wait_c(bars.o_done, c - 1, p.status, kDevTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const int cp = c - 1;
+        const int nv = min(kC, len - cp * kC);
+        uint32_t row[64];
+        tmem_ld64(lane_base + kColO, row);
+        __nv_bfloat16* dst = p.out + (static_cast<size_t>(tok0 + cp * kC) * p.hv + h) * kD + r;
+        const size_t tstride = static_cast<size_t>(p.hv) * kD;
+#pragma unroll
+        for (int t = 0; t < kC; ++t)
+          if (t < nv) dst[t * tstride] = __float2bfloat16_rn(__uint_as_float(row[t]) * p.scale);
+        tc_fence_before();
+        mbar_arrive(&bars.o_free[cp & 1]);
+      }
+    }
+    if (ok) {
+      const int cp = nchunks - 1;
+      if (wait_c(bars.o_done, cp, p.status, kDevTimeoutMma)) {
+        tc_fence_after();
+        const int nv = min(kC, len - cp * kC);
+        uint32_t row[64];
+        tmem_ld64(lane_base + kColO, row);
+        __nv_bfloat16* dst = p.out + (static_cast<size_t>(tok0 + cp * kC) * p.hv + h) * kD + r;
+        const size_t tstride = static_cast<size_t>(p.hv) * kD;
+#pragma unroll
+        for (int t = 0; t < kC; ++t)
+          if (t < nv) dst[t * tstride] = __float2bfloat16_rn(__uint_as_float(row[t]) * p.scale);
+      }
+    }
+  } else if (warp < 12) {
+    // =========================================================== blocked triangular solve
+    // scratch[t][s] (t > s) holds L; the unit-lower inverse That[t][s] (t > s) is written
+    // transposed into scratch[s][t].  Diagonal blocks D_i = (I + L_ii)^-1 first, then the
+    // off-diagonal blocks by distance: That_ij = -D_i * sum_{k=j}^{i-1} L_ik That_kj.
+    const int tid = threadIdx.x - 256;
+    float* tmp = reinterpret_cast<float*>(smem + kOffTG);  // X temporaries, reuses the T^G tile
+    auto Lv = [&](int t, int s) -> float { return scratch[t * kScStride + s]; };
+    auto Tv = [&](int t, int s) -> float {  // That[t][s], any t, s
+      return t == s ? 1.0f : (t > s ? scratch[s * kScStride + t] : 0.0f);
+    };
+    bool ok = true;
+    for (int c = 0; ok && c < nchunks; ++c) {
+      bool ready = wait_c(bars.qk_read, c, p.status, kDevTimeoutPipe);
+      if (ready && c >= 1) ready = wait_c(bars.w_done, c - 1, p.status, kDevTimeoutMma);
+      // the four warps leave together or not at all (they meet at named barriers below)
+      if (!named_sync_and(1, 128, ready)) { ok = false; break; }
+      const ChunkParams& pc = params[c & 1];
+      // step 1: diagonal 16x16 blocks, one column per thread (threads 0..63)
+      if (tid < 64) {
+        const int blk = tid >> 4, col = tid & 15, o = blk * 16;
+        float x[16];
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+          if (rr < col) {
+            x[rr] = 0.0f;
+          } else if (rr == col) {
+            x[rr] = 1.0f;
+          } else {
+            float acc = 0.0f;
+#pragma unroll
+            for (int s = 0; s < rr; ++s) acc = fmaf(Lv(o + rr, o + s), x[s], acc);
+            x[rr] = -acc;
+          }
+        }
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr)
+          if (rr > col) scratch[(o + col) * kScStride + o + rr] = x[rr];
+      }
+      named_sync(1, 128);
+      // steps 2-4: block distance 1, 2, 3
+#pragma unroll 1
+      for (int dist = 1; dist <= 3; ++dist) {
+        const int nblk = 4 - dist;  // blocks (i, j = i - dist), i = dist..3
+        const int nelem = nblk * 256;
+        // X = sum_{k=j}^{i-1} L_ik That_kj   (16x16 each)
+        for (int e = tid; e < nelem; e += 128) {
+          const int bi = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
+          const int i = dist + bi, j = i - dist;
+          float acc = 0.0f;
+          for (int kb = j; kb < i; ++kb) {
+#pragma unroll
+            for (int s = 0; s < 16; ++s) acc = fmaf(Lv(16 * i + rr, 16 * kb + s), Tv(16 * kb + s, 16 * j + cc), acc);
+          }
+          tmp[e] = acc;
+        }
+        named_sync(1, 128);
+        // That_ij = -D_i X
+        for (int e = tid; e < nelem; e += 128) {
+          const int bi = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
+          const int i = dist + bi, j = i - dist;
+          float acc = tmp[e];  // D_i has a unit diagonal
+#pragma unroll
+          for (int s = 0; s < 16; ++s)
+            if (s < rr) acc = fmaf(scratch[(16 * i + s) * kScStride + 16 * i + rr], tmp[(bi << 8) + (s << 4) + cc], acc);
+          scratch[(16 * j + cc) * kScStride + 16 * i + rr] = -acc;
+        }
+        named_sync(1, 128);
+      }
+      // step 5: T = That diag(beta) (hi/lo) and T diag(e^G) as bf16 [t][s] tiles
+      {
+        const int t = tid & 63;
+        uint32_t a[32], b[32];
+        if (tid < 64) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float v0 = Tv(t, 2 * j) * pc.beta[2 * j];
+            const float v1 = Tv(t, 2 * j + 1) * pc.beta[2 * j + 1];
+            uint32_t h0, h1;
+            const float l0 = bf16_lo_part(v0, h0);
+            const float l1 = bf16_lo_part(v1, h1);
+            a[j] = h0 | (h1 << 16);
+            b[j] = pack_bf16x2(l0, l1);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            a[j] = pack_bf16x2(Tv(t, 2 * j) * pc.beta[2 * j] * pc.eg[2 * j],
+                               Tv(t, 2 * j + 1) * pc.beta[2 * j + 1] * pc.eg[2 * j + 1]);
+        }
+        named_sync(1, 128);  // tmp (aliasing the T^G tile) is dead from here on
+        if (tid < 64) {
+          store_row_sw128(smem + kOffThi, t, a);
+          store_row_sw128(smem + kOffTlo, t, b);
+        } else {
+          store_row_sw128(smem + kOffTG, t, a);
+        }
+      }
+      fence_async_smem();
+      mbar_arrive(&bars.prep1[c & 1]);
+    }
+  } else if (warp == kWarpTma) {
+    // =========================================================== TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&map_q);
+      tma_prefetch_desc(&map_k);
+      tma_prefetch_desc(&map_v);
+      int issued = 0;
+      for (int c = 0; c < nchunks; ++c) {
+        const int row = tok0 + c * kC;
+        if (c >= 2 && !wait_c(bars.slot_free, c - 2, p.status, kDevTimeoutPipe)) break;
+        uint8_t* slot = smem + ((c & 1) ? kOffSlot1 : kOffSlot0);
+        mbar_arrive_expect_tx(&bars.in_full[c & 1], kSlotBytes);
+        for (int bx = 0; bx < 2; ++bx) {
+          tma_load_3d(slot + bx * 16384, &map_q, &bars.in_full[c & 1], bx * 64, kh, row);
+          tma_load_3d(slot + bx * 16384 + 8192, &map_k, &bars.in_full[c & 1], bx * 64, kh, row);
+        }
+        if (c >= 1 && !wait_c(bars.v_free, c - 1, p.status, kDevTimeoutPipe)) break;
+        mbar_arrive_expect_tx(&bars.v_full[c & 1], 16384);
+        for (int bx = 0; bx < 2; ++bx)
+          tma_load_3d(smem + kOffV + bx * 8192, &map_v, &bars.v_full[c & 1], bx * 64, h, row);
+        issued = c + 1;
+      }
+      // before the CTA retires, let the last loads land (bounded; a no-op on the normal path)
+      for (int c = max(0, issued - 2); c < issued; ++c) {
+        wait_c(bars.in_full, c, nullptr, 0);
+        wait_c(bars.v_full, c, nullptr, 0);
+      }
+    }
+  } else {
+    // =========================================================== MMA issuer (polling)
+    if (lane == 0 && nchunks > 0) {
+      const uint32_t id_qk = make_idesc(128, 64, 1, 0, 0);    // [Q;K] K^T
+      const uint32_t id_w = make_idesc(128, 64, 1, 1, 0);     // W^T = K^T (T^G)^T, A MN-major
+      const uint32_t id_vt = make_idesc(128, 64, 1, 1, 0);    // Delta^T = V^T T^T, A MN-major
+      const uint32_t id_sw = make_idesc(128, 64, 1, 0, 1);    // Delta^T += S (-W)^T, B MN-major
+      const uint32_t id_upd = make_idesc(128, 128, 1, 0, 1);  // S += Delta'^T K, A TMEM, B MN-major
+      const uint32_t id_sq = make_idesc(128, 64, 1, 0, 0);    // O^T = S Qt^T
+      const uint32_t id_dp = make_idesc(128, 64, 1, 0, 0);    // O^T += Delta^T P^T, A TMEM
+      const uint32_t a_thi = smem_u32(smem + kOffThi), a_tlo = smem_u32(smem + kOffTlo);
+      const uint32_t a_tg = smem_u32(smem + kOffTG), a_v = smem_u32(smem + kOffV);
+      const uint32_t a_wneg = smem_u32(smem + kOffWneg);
+      int n1 = 0, n2 = 0, n3 = 0, n4 = 0, n5 = 0;
+      const int N = nchunks;
+      unsigned long long idle_since = 0;
+      while (n5 < N) {
+        bool issued = false;
+        if (n4 < n3 && n4 <= n5 && test_c(bars.da_done, n4)) {
+          // T4: S += Delta'_hi^T K + Delta'_lo^T K
+          const int c = n4;
+          tc_fence_after();
+          const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
+          const uint32_t colx = (c & 1) ? kColX1 : kColX0;
+#pragma unroll
+          for (int part = 0; part < 2; ++part)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16_ts(tbase + kColS, tbase + colx + 32 + 32 * part + 8 * kk,
+                           make_sdesc_sw128(slot + 8192 + kk * 2048, 16384, 1024), id_upd, 1u);
+          umma_commit(&bars.snew[c & 1]);
+          ++n4;
+          issued = true;
+        } else if (n3 < n2 && n3 == n4 && test_c(bars.wneg, n3) && test_c(bars.s_ready, n3)) {
+          // T3: Delta^T += S (-W)^T
+          const int c = n3;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + ((c & 1) ? kOffS1 : kOffS0));
+          const uint32_t colx = (c & 1) ? kColX1 : kColX0;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16_ss(tbase + colx, make_sdesc_sw128(sa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                         make_sdesc_sw128(a_wneg + kk * 2048, 16384, 1024), id_sw, 1u);
+          umma_commit(&bars.delta[c & 1]);
+          ++n3;
+          issued = true;
+        } else if (n5 < n4 && test_c(bars.qk_read, n5) && (n5 == 0 || test_c(bars.o_free, n5 - 1))) {
+          // T5: O^T = S Qt^T + Delta^T P^T
+          const int c = n5;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + ((c & 1) ? kOffS1 : kOffS0));
+          const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
+          const uint32_t pa = smem_u32(smem + ((c & 1) ? kOffP1 : kOffP0));
+          const uint32_t colx = (c & 1) ? kColX1 : kColX0;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16_ss(tbase + kColO, make_sdesc_sw128(sa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                         make_sdesc_sw128(slot + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), id_sq,
+                         kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16_ts(tbase + kColO, tbase + colx + 8 * kk, make_sdesc_sw128(pa + kk * 32, 16, 1024), id_dp, 1u);
+          umma_commit(&bars.o_done[c & 1]);
+          umma_commit(&bars.slot_free[c & 1]);
+          ++n5;
+          issued = true;
+        } else if (n2 < n1 && n2 < n4 + 2 && n2 < n5 + 2 && test_c(bars.prep1, n2) && test_c(bars.v_full, n2) &&
+                   (n2 == 0 || test_c(bars.wneg, n2 - 1))) {
+          // T2: W^T = K^T (T^G)^T ; Delta^T = V^T T_hi^T + V^T T_lo^T
+          const int c = n2;
+          tc_fence_after();
+          const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
+          const uint32_t colx = (c & 1) ? kColX1 : kColX0;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16_ss(tbase + kColW, make_sdesc_sw128(slot + 8192 + kk * 2048, 16384, 1024),
+                         make_sdesc_sw128(a_tg + kk * 32, 16, 1024), id_w, kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16_ss(tbase + colx, make_sdesc_sw128(a_v + kk * 2048, 8192, 1024),
+                         make_sdesc_sw128(a_thi + kk * 32, 16, 1024), id_vt, kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16_ss(tbase + colx, make_sdesc_sw128(a_v + kk * 2048, 8192, 1024),
+                         make_sdesc_sw128(a_tlo + kk * 32, 16, 1024), id_vt, 1u);
+          umma_commit(&bars.w_done[c & 1]);
+          umma_commit(&bars.v_free[c & 1]);
+          ++n2;
+          issued = true;
+        } else if (n1 < N && n1 <= n2 + 1 && n1 < n5 + 2 && test_c(bars.in_full, n1) &&
+                   (n1 == 0 || test_c(bars.qk_read, n1 - 1))) {
+          // T1: [Q;K] K^T
+          const int c = n1;
+          tc_fence_after();
+          const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_bf16_ss(tbase + kColQK, make_sdesc_sw128(slot + off, 16, 1024),
+                         make_sdesc_sw128(slot + 8192 + off, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&bars.qk_done[c & 1]);
+          ++n1;
+          issued = true;
+        }
+        if (issued) {
+          idle_since = 0;
+        } else {
+          const unsigned long long now = global_timer_ns();
+          if (idle_since == 0) {
+            idle_since = now;
+          } else if (now - idle_since > kWaitTimeoutNs ||
+                     *reinterpret_cast<volatile uint32_t*>(p.status) != 0u) {
+            record_status(p.status, kDevTimeoutPipe);
+            break;
+          }
+        }
+      }
+      // every MMA issued by this thread completes before TMEM is released (bounded)
+      umma_commit(&drain_bar);
+      mbar_wait(&drain_bar, 0, nullptr, 0);
+    }
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+}  // namespace gdn
+}  // namespace tokmix
+
+extern "C" int tokmix_gdn_prefill(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                                  const float* initial_state, void* out, float* final_state,
+                                  const int32_t* cu_seqlens_dev, const int32_t* seq_order_dev, int num_seqs,
+                                  int total_tokens, int heads_k, int heads_v, int head_dim_k, int head_dim_v,
+                                  float scale, int io_dtype, uint32_t* status, void* stream) {
+  using namespace tokmix;
+  using namespace tokmix::gdn;
+  if (!q || !k || !v || !g || !beta || !out || !final_state || !cu_seqlens_dev)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: null pointer argument");
+  if (num_seqs < 0 || total_tokens < 0 || heads_k <= 0 || heads_v <= 0)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: negative or zero size");
+  if (heads_v % heads_k != 0)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: heads_v (%d) must be a multiple of heads_k (%d)",
+                heads_v, heads_k);
+  if (head_dim_k != kD || head_dim_v != kD)
+    return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_gdn_prefill: head dims must be 128 (got %d, %d)", head_dim_k,
+                head_dim_v);
+  if (io_dtype != TOKMIX_DTYPE_BF16)
+    return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_gdn_prefill: only bf16 q/k/v/out are supported by the kernel");
+  if (!std::isfinite(scale)) return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: scale must be finite");
+  if (status == nullptr)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: a device status word is required");
+  for (const void* ptr : {q, k, v, static_cast<const void*>(initial_state), static_cast<const void*>(final_state)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+      return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: tensors must be 16-byte aligned");
+  if (num_seqs == 0) return TOKMIX_OK;
+  if (const int rc = check_device()) return rc;
+  const long long units = static_cast<long long>(num_seqs) * heads_v;
+  if (units > 0x7FFFFFFFll) return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_gdn_prefill: too many (sequence, head) units");
+
+  // 3-D tensor maps over (dim, head, token); box = 64 columns x 1 head x 64 tokens.
+  const uint64_t rows = static_cast<uint64_t>(total_tokens > 0 ? total_tokens : 1);
+  CUtensorMap mq, mk, mv;
+  {
+    uint64_t dims_k[3] = {kD, static_cast<uint64_t>(heads_k), rows};
+    uint64_t strides_k[2] = {kD * 2, static_cast<uint64_t>(heads_k) * kD * 2};
+    uint64_t dims_v[3] = {kD, static_cast<uint64_t>(heads_v), rows};
+    uint64_t strides_v[2] = {kD * 2, static_cast<uint64_t>(heads_v) * kD * 2};
+    uint32_t box[3] = {64, 1, 64};
+    if (!encode_tiled(&mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, dims_k, strides_k, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tiled(&mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, k, dims_k, strides_k, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tiled(&mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, v, dims_v, strides_v, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+      return TOKMIX_ERR_INVALID_ARGUMENT;
+  }
+  Params p{};
+  p.g = g;
+  p.beta = beta;
+  p.state_in = initial_state;
+  p.state_out = final_state;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.cu_seqlens = cu_seqlens_dev;
+  p.seq_order = seq_order_dev;
+  p.hk = heads_k;
+  p.hv = heads_v;
+  p.scale = scale;
+  p.status = status;
+  const int smem_bytes = kSmemBytes + 1024;
+  if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_prefill_kernel), smem_bytes))
+    return check_launch("tokmix_gdn_prefill: cudaFuncSetAttribute");
+  gdn_prefill_kernel<<<static_cast<unsigned>(units), kThreads, smem_bytes, static_cast<cudaStream_t>(stream)>>>(
+      mq, mk, mv, p);
+  return check_launch("tokmix_gdn_prefill");
+}

@@ -1,0 +1,201 @@
+"""qwen35moe_gdn_prefill plugin module -- drop-in for the reference's
+``kernels_optimized/qwen35moe_gdn_prefill.py`` (module contract of ``kernels/__init__.py:3-8``):
+
+    KERNEL_TYPE, kernel_fn(q, k, v, g, beta, state, scale=None) -> [out, final_state],
+    get_inputs, get_flops, get_bytes
+
+``kernel_fn`` runs the sm_100a chunked kernel in libtokmix.so (``tokmix_gdn_prefill``); there is
+no fallback.  Argument meaning follows the reference (``kernels/qwen35moe_gdn_prefill.py:107-151``):
+q, k [B,T,Hk,128]; v [B,T,Hv,128]; g (log decay), beta [B,T,Hv]; state [B,Hv,128(v),128(k)];
+value head h reads key head h % Hk; default scale 128**-0.5; returns [out like v, final_state fp32].
+
+Extensions over the reference module:
+* q/k/v may be bf16 (the kernel's native type; out is then bf16).  The reference's fp32 contract
+  is accepted too: fp32 q/k/v are rounded to bf16 on the device before the kernel runs and the
+  output is returned as fp32.
+* ``cu_seqlens`` (keyword): variable-length sequences packed along T with q.shape[0] == 1 and
+  one initial state per sequence (state [N,Hv,128,128]); ``state=None`` means zero states.
+* any Hk dividing Hv (the reference fixes Hk=16, Hv=32).
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import _lib
+
+KERNEL_TYPE = "qwen35moe_gdn_prefill"
+D = 128
+H_K = 16
+H_V = 32
+_CHECK_STATUS = os.environ.get("TOKMIX_CHECK_STATUS", "0") == "1"
+
+_meta_cache: dict = {}
+
+
+def _device_meta(lengths: tuple[int, ...], device: torch.device):
+    """cu_seqlens (int32) and the longest-first scheduling order, uploaded once per shape."""
+    key = (lengths, device)
+    hit = _meta_cache.get(key)
+    if hit is None:
+        cu = [0]
+        for n in lengths:
+            cu.append(cu[-1] + n)
+        order = sorted(range(len(lengths)), key=lambda i: -lengths[i])
+        cu_t = torch.tensor(cu, dtype=torch.int32).to(device)
+        order_t = torch.tensor(order, dtype=torch.int32).to(device) if len(set(lengths)) > 1 else None
+        hit = (cu_t, order_t)
+        if len(_meta_cache) > 256:
+            _meta_cache.clear()
+        _meta_cache[key] = hit
+    return hit
+
+
+def _validate(q, k, v, g, beta, state, cu_seqlens):
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("q/k/v must be [batch, tokens, heads, dim]")
+    if g.ndim != 3 or beta.ndim != 3:
+        raise ValueError("g/beta must be [batch, tokens, H_v]")
+    if q.shape[-1] != D or k.shape[-1] != D or v.shape[-1] != D:
+        raise ValueError("head dimension must be 128")
+    if q.shape != k.shape:
+        raise ValueError("q and k shapes must match")
+    hk, hv = q.shape[2], v.shape[2]
+    if hv % hk != 0:
+        raise ValueError("H_v must be a multiple of H_k")
+    if v.shape[:2] != q.shape[:2] or g.shape != q.shape[:2] + (hv,) or beta.shape != g.shape:
+        raise ValueError("inconsistent token/head shapes")
+    tensors = [q, k, v, g, beta] + ([state] if state is not None else [])
+    if any(not t.is_cuda for t in tensors):
+        raise ValueError("all tensors must be CUDA tensors")
+    if any(t.device != q.device for t in tensors):
+        raise ValueError("all tensors must be on the same device")
+    if q.dtype not in (torch.bfloat16, torch.float32) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q/k/v must all be bfloat16 or all be float32")
+    if cu_seqlens is None:
+        nseq = q.shape[0]
+    else:
+        if q.shape[0] != 1:
+            raise ValueError("with cu_seqlens, q/k/v/g/beta must have batch dimension 1")
+        nseq = len(cu_seqlens) - 1
+        if nseq < 1:
+            raise ValueError("cu_seqlens needs at least two entries")
+    if state is not None and tuple(state.shape) != (nseq, hv, D, D):
+        raise ValueError(f"state shape must be [{nseq}, {hv}, 128, 128]")
+    return nseq, hk, hv
+
+
+def _lengths(cu_seqlens, total: int) -> tuple[int, ...]:
+    if isinstance(cu_seqlens, torch.Tensor):
+        cu = [int(x) for x in cu_seqlens.detach().to("cpu").tolist()]
+    else:
+        cu = [int(x) for x in cu_seqlens]
+    if cu[0] != 0 or any(b < a for a, b in zip(cu, cu[1:])) or cu[-1] != total:
+        raise ValueError("cu_seqlens must start at 0, be non-decreasing and end at the token count")
+    return tuple(b - a for a, b in zip(cu, cu[1:]))
+
+
+def kernel_fn(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    g: torch.Tensor,
+    beta: torch.Tensor,
+    state: torch.Tensor | None,
+    scale: float | None = None,
+    *,
+    cu_seqlens=None,
+) -> list[torch.Tensor]:
+    nseq, hk, hv = _validate(q, k, v, g, beta, state, cu_seqlens)
+    if scale is None:
+        scale = D ** -0.5
+    dev = q.device
+    io_dtype = q.dtype
+    B, T = q.shape[0], q.shape[1]
+    total = B * T
+    if cu_seqlens is None:
+        lengths = (T,) * B
+    else:
+        lengths = _lengths(cu_seqlens, T)
+    if total == 0:
+        out = torch.empty(v.shape, dtype=io_dtype, device=dev)
+        fs = state.to(torch.float32).clone() if state is not None else torch.zeros((nseq, hv, D, D), device=dev)
+        return [out, fs]
+    cu_t, order_t = _device_meta(lengths, dev)
+    qb = q.to(torch.bfloat16).contiguous()
+    kb = k.to(torch.bfloat16).contiguous()
+    vb = v.to(torch.bfloat16).contiguous()
+    gf = g.to(torch.float32).contiguous()
+    bf = beta.to(torch.float32).contiguous()
+    st = state.to(torch.float32).contiguous() if state is not None else None
+    out = torch.empty(vb.shape, dtype=torch.bfloat16, device=dev)
+    final_state = torch.empty((nseq, hv, D, D), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    word = _lib.status_word(dev)
+    with torch.cuda.device(dev):
+        rc = lib.tokmix_gdn_prefill(
+            qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
+            st.data_ptr() if st is not None else None, out.data_ptr(), final_state.data_ptr(),
+            cu_t.data_ptr(), order_t.data_ptr() if order_t is not None else None,
+            nseq, total, hk, hv, D, D, float(scale), _lib.DTYPE_BF16, word.data_ptr(), _lib.stream_ptr(dev))
+    _lib.check(rc, "qwen35moe_gdn_prefill")
+    if _CHECK_STATUS:
+        _lib.raise_on_device_status(word, "qwen35moe_gdn_prefill")
+    if io_dtype != torch.bfloat16:
+        out = out.to(io_dtype)
+    return [out, final_state]
+
+
+def check_device_status(device: torch.device | None = None) -> None:
+    """Synchronise and raise if any kernel on `device` reported a device-side timeout."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    _lib.raise_on_device_status(_lib.status_word(dev), "qwen35moe_gdn_prefill")
+
+
+def filled(shape, scale: float, bias: float, dtype=torch.float32, device="cuda") -> torch.Tensor:
+    """The reference's deterministic fixture ``((i mod 251) - 125) * scale + bias``
+    (``kernels/qwen35moe_gdn_prefill.py:158-164``)."""
+    n = 1
+    for dim in shape:
+        n *= dim
+    x = torch.arange(n, device=device, dtype=torch.float32)
+    x = ((x % 251) - 125.0) * scale + bias
+    return x.reshape(shape).to(dtype)
+
+
+def get_inputs(batch: int = 1, seq_len: int = 4096, dtype: torch.dtype = torch.float32, seed: int = 42,
+               device: str = "cuda") -> dict:
+    """The reference's fixture (``kernels/qwen35moe_gdn_prefill.py:154-174``; seed ignored)."""
+    del seed
+    return {
+        "q": filled((batch, seq_len, H_K, D), 0.001, 0.0, dtype, device),
+        "k": filled((batch, seq_len, H_K, D), 0.001, 0.0, dtype, device),
+        "v": filled((batch, seq_len, H_V, D), 0.001, 0.0, dtype, device),
+        "g": filled((batch, seq_len, H_V), 0.0001, -0.01, torch.float32, device),
+        "beta": filled((batch, seq_len, H_V), 0.0001, 0.5, torch.float32, device),
+        "state": filled((batch, H_V, D, D), 0.0001, 0.0, torch.float32, device),
+        "scale": D ** -0.5,
+    }
+
+
+def get_flops(batch: int = 1, seq_len: int = 4096) -> int:
+    """Reference formula (recurrent count), ``kernels_optimized/qwen35moe_gdn_prefill.py:170-171``."""
+    return 4 * batch * H_V * seq_len * D * D
+
+
+def get_bytes(batch: int = 1, seq_len: int = 4096, element_size: int = 4) -> int:
+    """Reference formula, ``kernels_optimized/qwen35moe_gdn_prefill.py:174-179`` (one element
+    size for every tensor)."""
+    qk = 2 * batch * seq_len * H_K * D
+    vo = 2 * batch * seq_len * H_V * D
+    gb = 2 * batch * seq_len * H_V
+    st = 2 * batch * H_V * D * D
+    return (qk + vo + gb + st) * element_size
+
+
+def algorithmic_bytes(tokens: int, n_seqs: int, hk: int = H_K, hv: int = H_V, io_bytes: int = 2) -> int:
+    """Bytes the bf16-I/O kernel must move at minimum: q, k, v read and o written in `io_bytes`
+    per element, g and beta read in fp32, one fp32 state read and written per (sequence, head)."""
+    return (tokens * (2 * hk + 2 * hv) * D * io_bytes + tokens * 2 * hv * 4 + n_seqs * hv * D * D * 4 * 2)

@@ -1,0 +1,94 @@
+"""libtokmix.so: it loads, exports every entry point include/tokmix.h declares, and rejects bad
+arguments through its status codes without touching a GPU (CPU-only checks)."""
+
+import ctypes
+import pathlib
+import re
+import subprocess
+
+import pytest
+
+from kernel_opt_agent_b200 import _lib
+
+HEADER = pathlib.Path(__file__).resolve().parents[1] / "include" / "tokmix.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tokmix_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    syms = declared_symbols()
+    assert syms, "no declarations parsed"
+    for s in syms:
+        assert hasattr(lib, s), s
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True).stdout
+    exported = set(re.findall(r" T (tokmix_\w+)", out))
+    assert set(syms) <= exported
+    assert set(_lib.SIGNATURES) == set(syms)
+
+
+def test_version():
+    assert _lib.version().startswith("tokmix ") and "sm_100a" in _lib.version()
+
+
+def test_fa2_rejects_bad_arguments():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    # null pointer (non-empty problem)
+    rc = lib.tokmix_fa2_fwd(None, p, p, p, 1, 8, 8, 128, 128, 128, 0, 1, 0.1, None, None)
+    assert rc == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "null" in _lib.last_error()
+    # heads_q not a multiple of heads_kv
+    rc = lib.tokmix_fa2_fwd(p, p, p, p, 1, 6, 4, 128, 128, 128, 0, 1, 0.1, None, None)
+    assert rc == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "multiple" in _lib.last_error()
+    # bad layout / scale / alignment
+    assert lib.tokmix_fa2_fwd(p, p, p, p, 1, 8, 8, 128, 128, 128, 7, 1, 0.1, None, None) == 1
+    assert lib.tokmix_fa2_fwd(p, p, p, p, 1, 8, 8, 128, 128, 128, 0, 1, -1.0, None, None) == 1
+    odd = ctypes.c_void_p(18)
+    assert lib.tokmix_fa2_fwd(odd, p, p, p, 1, 8, 8, 128, 128, 128, 0, 1, 0.1, None, None) == 1
+    # empty problem is a no-op success
+    assert lib.tokmix_fa2_fwd(p, p, p, p, 0, 8, 8, 128, 128, 128, 0, 1, 0.1, None, None) == 0
+
+
+def test_gdn_rejects_bad_arguments():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    # every call below is rejected (or is a no-op) before anything is launched
+    args = [p, p, p, p, p, None, p, p, p, None, 1, 64, 16, 32, 128, 128, 0.08, 0, p, None]
+    bad = list(args)
+    bad[0] = None
+    assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "null" in _lib.last_error()
+    bad = list(args)
+    bad[13] = 24  # heads_v not a multiple of heads_k
+    assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    bad = list(args)
+    bad[14] = 64  # head dim
+    assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_UNSUPPORTED
+    bad = list(args)
+    bad[17] = 1  # fp32 io
+    assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_UNSUPPORTED
+    bad = list(args)
+    bad[18] = None  # status word required
+    assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    bad = list(args)
+    bad[10] = 0  # no sequences: no-op
+    assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_OK
+
+
+def test_python_wrappers_raise_valueerror_on_cpu_tensors():
+    import torch
+
+    from kernel_opt_agent_b200 import flash_attention_2 as fa2
+    from kernel_opt_agent_b200 import qwen35moe_gdn_prefill as gdn
+
+    q = torch.zeros(1, 2, 8, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        fa2.kernel_fn(q, q, q)
+    x = torch.zeros(1, 4, 16, 128)
+    y = torch.zeros(1, 4, 32, 128)
+    gb = torch.zeros(1, 4, 32)
+    with pytest.raises(ValueError):
+        gdn.kernel_fn(x, x, y, gb, gb, torch.zeros(1, 32, 128, 128))

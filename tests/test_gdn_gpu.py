@@ -1,0 +1,154 @@
+"""GDN prefill parity on a B200: the sm_100a chunked kernel (through the C ABI) against the
+fp32 recurrence oracle."""
+
+import json
+import pathlib
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from kernel_opt_agent_b200 import qwen35moe_gdn_prefill as gdn
+from kernel_opt_agent_b200.kernel_configs import KERNEL_CONFIGS
+from kernel_opt_agent_b200.kernel_configs import qwen35moe_gdn_prefill as gcfg
+from tests.golden import make_golden as golden
+
+pytestmark = pytest.mark.gpu
+GOLDEN = pathlib.Path(__file__).resolve().parent / "golden"
+OUT_TOL = dict(atol=2e-2, rtol=2e-2)     # bf16 output
+STATE_TOL = dict(atol=1e-4, rtol=1e-3)   # fp32 final state
+
+
+def _np(x):
+    return None if x is None else x.float().cpu().numpy()
+
+
+def _oracle(inp, threads):
+    return oracle.gdn_recurrent(_np(inp["q"]), _np(inp["k"]), _np(inp["v"]), _np(inp["g"]), _np(inp["beta"]),
+                                _np(inp.get("state")), inp.get("scale"), cu_seqlens=_np(inp.get("cu_seqlens")),
+                                nthreads=threads)
+
+
+def _check(inp, threads, out_tol=OUT_TOL, state_tol=STATE_TOL):
+    out, fs = gdn.kernel_fn(**inp)
+    gdn.check_device_status(out.device)
+    o_ref, s_ref = _oracle(inp, threads)
+    got_o, got_s = _np(out), _np(fs)
+    assert np.isfinite(got_o).all() and np.isfinite(got_s).all()
+    np.testing.assert_allclose(got_o, o_ref, **out_tol)
+    np.testing.assert_allclose(got_s, s_ref.reshape(got_s.shape), **state_tol)
+    return out, fs
+
+
+@pytest.mark.parametrize("b,t,hk,hv,state_std", [
+    (1, 1, 16, 32, 0.0),
+    (1, 2, 2, 4, 0.02),
+    (1, 63, 2, 4, 0.0),
+    (1, 64, 2, 4, 0.02),
+    (2, 65, 2, 4, 0.02),
+    (1, 128, 1, 1, 0.0),
+    (1, 200, 16, 32, 0.02),
+    (3, 129, 4, 8, 0.02),
+])
+def test_gdn_matches_oracle(cuda_device, oracle_threads, b, t, hk, hv, state_std):
+    inp = gcfg.baseline_inputs(b, t, seed=t + hk, state_std=state_std, hk=hk, hv=hv)
+    _check(inp, oracle_threads)
+
+
+def test_gdn_varlen_with_empty_and_tail_sequences(cuda_device, oracle_threads):
+    inp = gcfg.baseline_inputs(1, 0, lengths=[1, 63, 64, 65, 200, 0, 129], seed=5, state_std=0.02)
+    _check(inp, oracle_threads)
+
+
+def test_gdn_reference_fixture_fp32_io(cuda_device, oracle_threads):
+    """The reference's own fixture and fp32 interface, at its own tolerance."""
+    cfg = KERNEL_CONFIGS["qwen35moe_gdn_prefill"]
+    tol = cfg["tolerances"][torch.float32]
+    for t in (2048, 2113):
+        inp = gcfg.fixture_inputs(1, t, torch.float32, "cuda")
+        out, fs = gdn.kernel_fn(**inp)
+        assert out.dtype == torch.float32
+        o_ref, s_ref = _oracle(inp, oracle_threads)
+        np.testing.assert_allclose(_np(out), o_ref, **tol)
+        np.testing.assert_allclose(_np(fs), s_ref, **tol)
+
+
+def test_gdn_stability_cases(cuda_device, oracle_threads):
+    cfg = KERNEL_CONFIGS["qwen35moe_gdn_prefill"]
+    for name, inp in cfg["numerical_stability_cases"]({"batch": 1, "seq_len": 300, "dist": "baseline"},
+                                                       torch.bfloat16, "cuda"):
+        out, fs = gdn.kernel_fn(**inp)
+        o_ref, s_ref = _oracle(inp, oracle_threads)
+        # the reference relaxes its tolerance x10 for these cases (tools/bench.py:557-609)
+        np.testing.assert_allclose(_np(out), o_ref, atol=2e-2, rtol=2e-2, err_msg=name)
+        np.testing.assert_allclose(_np(fs), s_ref, atol=1e-3, rtol=1e-2, err_msg=name)
+
+
+def test_gdn_strong_negative_gate_strict(cuda_device, oracle_threads):
+    inp = gcfg.baseline_inputs(1, 64, seed=3)
+    gen = torch.Generator().manual_seed(4)
+    inp["g"] = (torch.rand(inp["g"].shape, generator=gen) * 17.0 - 25.0).cuda()
+    _check(inp, oracle_threads)
+
+
+@pytest.mark.skipif(not (GOLDEN / "gdn_golden_meta.json").exists(), reason="GDN golden vectors not generated")
+@pytest.mark.parametrize("name", sorted(golden.GDN_CASES))
+def test_gdn_matches_reference_kernel_golden(cuda_device, name):
+    meta = json.loads((GOLDEN / "gdn_golden_meta.json").read_text())
+    case = golden.GDN_CASES[name]
+    q, k, v, g, beta, st = (x.cuda() for x in golden.gdn_inputs(case))
+    io = torch.float32 if case["kind"] == "fixture" else torch.bfloat16
+    out, fs = gdn.kernel_fn(q.to(io), k.to(io), v.to(io), g, beta, st)
+    ref = np.load(GOLDEN / f"{name}.npz")
+    tol_o = dict(atol=2e-3, rtol=2e-1) if case["kind"] == "fixture" else OUT_TOL
+    tol_s = dict(atol=2e-3, rtol=2e-1) if case["kind"] == "fixture" else STATE_TOL
+    np.testing.assert_allclose(_np(out)[:, :, meta["out_heads"]], ref["out"], **tol_o)
+    np.testing.assert_allclose(_np(fs)[:, meta["state_heads"]], ref["final_state"], **tol_s)
+
+
+def test_gdn_config1_full(cuda_device, oracle_threads):
+    """B=1, T=2048, Hk=16, Hv=32, zero state: every output and the fp32 final state."""
+    inp = gcfg.baseline_inputs(1, 2048, seed=0)
+    _check(inp, oracle_threads)
+
+
+def test_gdn_state_continuation_is_exact(cuda_device):
+    """Chunk-aligned split with the state handed over equals the one-shot run bit for bit."""
+    inp = gcfg.baseline_inputs(1, 640, seed=8, state_std=0.02)
+    out, fs = gdn.kernel_fn(**inp)
+    a = {k: (v[:, :256] if k in ("q", "k", "v", "g", "beta") else v) for k, v in inp.items()}
+    oa, sa = gdn.kernel_fn(**a)
+    b = {k: (v[:, 256:] if k in ("q", "k", "v", "g", "beta") else v) for k, v in inp.items()}
+    b["state"] = sa
+    ob, sb = gdn.kernel_fn(**b)
+    assert torch.equal(torch.cat([oa, ob], dim=1), out)
+    assert torch.equal(sb, fs)
+
+
+def test_gdn_deterministic(cuda_device):
+    inp = gcfg.baseline_inputs(2, 700, seed=11, state_std=0.02)
+    r = [gdn.kernel_fn(**inp) for _ in range(3)]
+    for o, s in r[1:]:
+        assert torch.equal(o, r[0][0]) and torch.equal(s, r[0][1])
+
+
+def test_gdn_varlen_full_size(cuda_device, oracle_threads):
+    """8 sequences, lengths ~U[1024, 32768], per-sequence initial state N(0, 0.02): the two
+    shortest sequences against the oracle, every sequence against its own one-sequence run."""
+    lengths = gcfg.varlen_lengths(8, seed=0)
+    inp = gcfg.baseline_inputs(1, 0, lengths=lengths, seed=0, state_std=0.02)
+    out, fs = gdn.kernel_fn(**inp)
+    gdn.check_device_status(cuda_device)
+    cu = np.cumsum([0] + lengths)
+    order = np.argsort(lengths)
+    for n in range(8):
+        a, b = int(cu[n]), int(cu[n + 1])
+        one = {k: (v[:, a:b] if k in ("q", "k", "v", "g", "beta") else v) for k, v in inp.items() if k != "cu_seqlens"}
+        one["state"] = inp["state"][n:n + 1]
+        o1, s1 = gdn.kernel_fn(**one)
+        assert torch.equal(o1, out[:, a:b]) and torch.equal(s1[0], fs[n]), n
+        if n in order[:2]:
+            o_ref, s_ref = _oracle({**one}, oracle_threads)
+            np.testing.assert_allclose(_np(o1), o_ref, **OUT_TOL)
+            np.testing.assert_allclose(_np(s1), s_ref, **STATE_TOL)
