@@ -1,0 +1,422 @@
+"""Benchmark of the B200 prefill token mixers (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+    torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
+
+Workloads (synthetic data from fixed seeds, shapes of the B200 configs):
+  gdn_b1_t2048   (default, headline)  GDN prefill B=1 T=2048 Hk=16 Hv=32 d=128, chunk 64, bf16 q/k/v/o,
+                 fp32 g/beta/state, zero initial state.  Weak scaling: every rank runs its own batch.
+  fa2_b4_s8192   FA2 causal GQA forward B=4 Hq=32 Hkv=8 S=8192 D=128 bf16.  Strong scaling: the
+                 8 key/value heads (with their 4 query heads each) are split across ranks.
+  gdn_varlen     GDN prefill, 8 sequences of U[1024, 32768] tokens packed with cu_seqlens,
+                 per-sequence initial state N(0, 0.02).  Strong scaling over head groups.
+The headline line also carries the other two workloads under "also" (same run, same timing rules).
+
+Timing: W untimed warm-up steps, then K timed steps bracketed by a barrier and
+torch.cuda.synchronize(); each step is timed with CUDA events on the launching stream and the
+L2 cache (126 MB) is flushed by writing a 256 MB buffer between steps when the step's inputs fit
+in L2.  The step time is the max over ranks.  `e2e` repeats the headline step through the public
+plugin call from pinned host buffers, host->device copies of the inputs and device->host copies
+of the outputs inside the timed region.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from kernel_opt_agent_b200 import flash_attention_2 as fa2  # noqa: E402
+from kernel_opt_agent_b200 import qwen35moe_gdn_prefill as gdn  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+D = 128
+HK, HV = 16, 32
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of each workload's
+# kernel from one ncu capture; see profiles/*.md for the commands and the raw figures.
+NCU_TRAFFIC_BYTES = {}
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ----------------------------------------------------------------------------- input generation
+def gdn_inputs(device, tokens_per_seq, seed, lengths=None, state_std=0.0, hk=HK, hv=HV, head_slice=None):
+    """GDN workload drawn on the device from a seeded generator (q, k L2-normalised, v ~ N(0,1),
+    g = -softplus(N(0,1)), beta = sigmoid(N(0,1)))."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    T = int(sum(lengths)) if lengths is not None else tokens_per_seq
+    nseq = len(lengths) if lengths is not None else 1
+    q = torch.randn(1, T, hk, D, device=device, generator=gen)
+    k = torch.randn(1, T, hk, D, device=device, generator=gen)
+    q = (q / q.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    v = torch.randn(1, T, hv, D, device=device, generator=gen).to(torch.bfloat16)
+    g = -torch.nn.functional.softplus(torch.randn(1, T, hv, device=device, generator=gen))
+    beta = torch.sigmoid(torch.randn(1, T, hv, device=device, generator=gen))
+    state = torch.randn(nseq, hv, D, D, device=device, generator=gen) * state_std
+    inp = {"q": q, "k": k, "v": v, "g": g, "beta": beta, "state": state, "scale": D ** -0.5}
+    if head_slice is not None:
+        # key heads [a, b) and the value heads that read them (h % hk in [a, b)), kept in an order
+        # where local value head i reads local key head i % (b - a)
+        a, b = head_slice
+        vh = [h for r in range(hv // hk) for h in range(r * hk + a, r * hk + b)]
+        inp["q"], inp["k"] = inp["q"][:, :, a:b].contiguous(), inp["k"][:, :, a:b].contiguous()
+        for key in ("v", "g", "beta"):
+            inp[key] = inp[key][:, :, vh].contiguous()
+        inp["state"] = inp["state"][:, vh].contiguous()
+    if lengths is not None:
+        cu = [0]
+        for n in lengths:
+            cu.append(cu[-1] + int(n))
+        inp["cu_seqlens"] = torch.tensor(cu, dtype=torch.int32)
+    return inp
+
+
+def varlen_lengths(n=8, lo=1024, hi=32768, seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    return [int(x) for x in torch.randint(lo, hi + 1, (n,), generator=gen)]
+
+
+def fa2_inputs(device, batch, hq, hkv, s, d, seed, kv_slice=None):
+    gen = torch.Generator(device=device).manual_seed(seed)
+    a, b = kv_slice if kv_slice is not None else (0, hkv)
+    group = hq // hkv
+    # draw the full tensors (same values on every rank), keep this rank's head slice
+    q = torch.randn(batch, hq, s, d, device=device, generator=gen, dtype=torch.bfloat16)[:, a * group:b * group]
+    k = torch.randn(batch, hkv, s, d, device=device, generator=gen, dtype=torch.bfloat16)[:, a:b]
+    v = torch.randn(batch, hkv, s, d, device=device, generator=gen, dtype=torch.bfloat16)[:, a:b]
+    return {"q": q.contiguous(), "k": k.contiguous(), "v": v.contiguous(), "causal": True,
+            "sm_scale": 1.0 / math.sqrt(d)}
+
+
+def input_bytes(inp) -> int:
+    return sum(t.numel() * t.element_size() for t in inp.values() if isinstance(t, torch.Tensor) and t.is_cuda)
+
+
+# ----------------------------------------------------------------------------- timing helpers
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while GPU work runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", ",".join(str(g) for g in gpus)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons, n = [], [], set(), 0
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            n += 1
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": n}
+
+
+def max_over_ranks(x: float, device) -> float:
+    if dist.is_available() and dist.is_initialized():
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return x
+
+
+def barrier():
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+
+
+def time_steps(step_fn, steps, warmup, device, flush: bool):
+    """Runs warmup + steps; returns (max-over-ranks total seconds of the K timed steps, per-step ms list)."""
+    flush_buf = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device) if flush else None
+    stream = torch.cuda.current_stream(device)
+    for _ in range(warmup):
+        if flush_buf is not None:
+            flush_buf.fill_(1)
+        step_fn()
+    torch.cuda.synchronize(device)
+    barrier()
+    torch.cuda.synchronize(device)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        if flush_buf is not None:
+            flush_buf.fill_(i & 0xFF)
+        starts[i].record(stream)
+        step_fn()
+        ends[i].record(stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    torch.cuda.synchronize(device)
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_s = sum(per) / 1e3
+    return max_over_ranks(total_s, device), per
+
+
+# ----------------------------------------------------------------------------- workloads
+def run_gdn_batch(device, rank, world, steps, warmup, batch=1):
+    inp = gdn_inputs(device, 2048, seed=1000 + rank, lengths=[2048] * batch if batch > 1 else None)
+    tokens = 2048 * batch * world
+    total_s, per = time_steps(lambda: gdn.kernel_fn(**inp), steps, warmup, device,
+                              flush=input_bytes(inp) < L2_BYTES)
+    gdn.check_device_status(device)
+    algo = gdn.algorithmic_bytes(2048 * batch, batch)
+    ms = total_s / steps * 1e3
+    return {"tokens_per_step": tokens, "ms": ms, "value": tokens * steps / total_s / 1e6, "unit": "Mtok/s",
+            "kernel_ms_local": statistics.mean(per), "algo_bytes": algo, "inp": inp}
+
+
+def headline_config(world: int) -> dict:
+    return {"workload": "gdn_b1_t2048", "batch_per_rank": 1, "seq_len": 2048, "hk": HK, "hv": HV, "head_dim": D,
+            "chunk": 64, "io": "bf16 q/k/v/o, fp32 g/beta/state", "initial_state": "zero",
+            "parallelism": f"dp{world} (one batch per rank)", "l2": "flushed between timed steps (256 MB write)"}
+
+
+HEADLINE_METRIC = "GDN prefill Mtok/s"
+
+
+def run_gdn_varlen(device, rank, world, steps, warmup):
+    lengths = varlen_lengths()
+    per_rank = HK // world
+    a, b = rank * per_rank, (rank + 1) * per_rank
+    inp = gdn_inputs(device, 0, seed=7, lengths=lengths, state_std=0.02, head_slice=(a, b))
+    tokens = sum(lengths)
+    total_s, per = time_steps(lambda: gdn.kernel_fn(**inp), steps, warmup, device,
+                              flush=input_bytes(inp) < L2_BYTES)
+    gdn.check_device_status(device)
+    algo = gdn.algorithmic_bytes(tokens, len(lengths), hk=b - a, hv=2 * (b - a))
+    return {"tokens_per_step": tokens, "ms": total_s / steps * 1e3, "value": tokens * steps / total_s / 1e6,
+            "unit": "Mtok/s", "kernel_ms_local": statistics.mean(per), "algo_bytes": algo,
+            "config": {"workload": "gdn_varlen", "n_seqs": 8, "lengths": lengths, "total_tokens": tokens,
+                       "hk": HK, "hv": HV, "head_dim": D, "chunk": 64, "initial_state": "N(0,0.02)",
+                       "shard": f"key heads {HK // world}/rank"}}
+
+
+def run_fa2(device, rank, world, steps, warmup, batch=4):
+    B, HQ, HKV, S, DD = batch, 32, 8, 8192, 128
+    per_rank = HKV // world
+    a, b = rank * per_rank, (rank + 1) * per_rank
+    inp = fa2_inputs(device, B, HQ, HKV, S, DD, seed=3, kv_slice=(a, b))
+    flops_total = fa2.get_flops(B, HQ, S, DD, causal=True)
+    total_s, per = time_steps(lambda: fa2.kernel_fn(**inp), steps, warmup, device,
+                              flush=input_bytes(inp) < L2_BYTES)
+    fa2.check_device_status(device)
+    local_flops = fa2.get_flops(B, (b - a) * (HQ // HKV), S, DD, causal=True)
+    return {"ms": total_s / steps * 1e3, "value": flops_total * steps / total_s / 1e12, "unit": "TFLOP/s",
+            "kernel_ms_local": statistics.mean(per), "local_flops": local_flops,
+            "config": {"workload": f"fa2_b{B}_s8192", "batch": B, "heads_q": HQ, "heads_kv": HKV, "seq_len": S,
+                       "head_dim": DD, "causal": True, "layout": "bhsd", "shard": f"kv heads {per_rank}/rank"}}
+
+
+def e2e_gdn_b1(device, rank, world, steps, warmup, inp):
+    """Headline step through the public plugin call from pinned host memory."""
+    host = {k: (v.cpu().pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
+    dev_bufs = {k: torch.empty_like(v, device=device) for k, v in host.items() if isinstance(v, torch.Tensor)}
+    out_host = torch.empty((1, 2048, HV, D), dtype=torch.bfloat16).pin_memory()
+    st_host = torch.empty((1, HV, D, D), dtype=torch.float32).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in host.values() if isinstance(v, torch.Tensor))
+    d2h = out_host.numel() * 2 + st_host.numel() * 4
+
+    def step():
+        for k, v in dev_bufs.items():
+            v.copy_(host[k], non_blocking=True)
+        args = dict(dev_bufs)
+        args["scale"] = host["scale"]
+        out, fs = gdn.kernel_fn(**args)
+        out_host.copy_(out, non_blocking=True)
+        st_host.copy_(fs, non_blocking=True)
+
+    total_s, _ = time_steps(step, steps, warmup, device, flush=True)
+    return {"value": 2048 * world * steps / total_s / 1e6, "unit": "Mtok/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": total_s / steps * 1e3}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_gdn_b1(repeats: int = 3):
+    """The oracle (C restatement of the reference's fp32 recurrence) on the host cores, over the
+    full B=1 T=2048 Hk=16 Hv=32 workload, `repeats` times; returns (Mtok/s median, cores, seconds)."""
+    sys.path.insert(0, ROOT)
+    import oracle  # the CPU restatement; only this leg of the benchmark uses it
+
+    cores = os.cpu_count() or 1
+    inp = gdn_inputs(torch.device("cpu"), 2048, seed=1000)
+    args = [inp[k].float().numpy() for k in ("q", "k", "v", "g", "beta")]
+    st = inp["state"].numpy()
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        oracle.gdn_recurrent(*args, st, inp["scale"], nthreads=cores)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return 2048 / med / 1e6, cores, med
+
+
+def run_reference(args):
+    """`--impl reference`: the reference has no CPU implementation of this path (its oracle is a
+    CUDA kernel), so the reference arm is the oracle port timed on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    times = []
+    cores = os.cpu_count() or 1
+    for i in range(args.warmup + args.steps):
+        v, cores, sec = cpu_gdn_b1(repeats=1)
+        if i >= args.warmup:
+            times.append(sec)
+    total = sum(times)
+    value = 2048 * args.steps / total / 1e6
+    line = {"impl": "reference", "metric": HEADLINE_METRIC,
+            "value": value, "unit": "Mtok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": headline_config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": "Mtok/s", "cores": cores, "kind": "port",
+                             "sample": "full B=1 T=2048 Hk=16 Hv=32 workload per step, fp32 recurrence "
+                                       "(oracle/gdn_recurrent.c) on all host cores"},
+            "e2e": {"value": value, "unit": "Mtok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="gdn_b1_t2048",
+                    choices=["gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_b4_t2048", "fa2_b1_s8192"],
+                    help="gdn_b4_t2048 / fa2_b1_s8192 are profiling-size cases (inputs just above L2)")
+    ap.add_argument("--no-also", action="store_true", help="skip the secondary workloads")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    if world not in (1, 2, 4, 8):
+        raise SystemExit("bench.py supports 1, 2, 4 or 8 GPUs")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    peaks = measured_peaks()
+    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    results = {}
+    head = args.workload
+    order = [head] + ([w for w in ("gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen") if w != head]
+                      if not args.no_also else [])
+    e2e = None
+    for w in order:
+        steps_w = args.steps if w == head else max(5, args.steps // 5)
+        if w in ("gdn_b1_t2048", "gdn_b4_t2048"):
+            r = run_gdn_batch(device, rank, world, steps_w, args.warmup, batch=1 if w == "gdn_b1_t2048" else 4)
+            if w == head == "gdn_b1_t2048":
+                e2e = e2e_gdn_b1(device, rank, world, args.steps, args.warmup, r["inp"])
+            inp = r.pop("inp")
+            r["config"] = headline_config(world) if w == "gdn_b1_t2048" else {
+                "workload": w, "batch_per_rank": 4, "seq_len": 2048, "hk": HK, "hv": HV, "head_dim": D}
+            del inp
+        elif w in ("fa2_b4_s8192", "fa2_b1_s8192"):
+            r = run_fa2(device, rank, world, steps_w, args.warmup, batch=4 if w == "fa2_b4_s8192" else 1)
+        else:
+            r = run_gdn_varlen(device, rank, world, steps_w, args.warmup)
+        results[w] = r
+        torch.cuda.empty_cache()
+    clocks = sampler.stop() if sampler else None
+
+    cpu = None
+    if rank == 0 and world == 1:
+        v, cores, sec = cpu_gdn_b1()
+        cpu = {"value": v, "unit": "Mtok/s", "cores": cores, "kind": "port",
+               "sample": f"full B=1 T=2048 Hk=16 Hv=32 workload, median of 3 runs ({sec:.3f} s each), fp32 "
+                         "recurrence (oracle/gdn_recurrent.c, OpenMP)"}
+
+    def roofline(w, r):
+        kms = r["kernel_ms_local"]
+        if w.startswith("fa2"):
+            ach = r["local_flops"] / (kms / 1e3) / 1e12
+            return {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                    "frac": ach / peaks["bf16_tflops"], "peak_source": peaks["source"] + " burst bf16",
+                    "traffic": NCU_TRAFFIC_BYTES.get(w), "kernel": "tokmix::fa2::fa2_fwd_kernel<128>",
+                    "kernel_ms": kms}
+        ach = r["algo_bytes"] / (kms / 1e3) / 1e9
+        return {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": ach / peaks["hbm_gbs"], "peak_source": peaks["source"] + " copy bandwidth",
+                "traffic": NCU_TRAFFIC_BYTES.get(w), "algorithmic_bytes": r["algo_bytes"],
+                "kernel": "tokmix::gdn::gdn_prefill_kernel", "kernel_ms": kms}
+
+    if rank == 0:
+        hr = results[head]
+        metric = HEADLINE_METRIC if head.startswith("gdn") else "FA2 fwd TFLOPS"
+        cfg = hr["config"]
+        line = {"metric": metric, "value": hr["value"], "unit": hr["unit"], "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": hr["ms"], "higher_is_better": True,
+                "scaling": "weak" if head in ("gdn_b1_t2048", "gdn_b4_t2048") else "strong", "vs_baseline": None,
+                "dtype": "bf16" if head.startswith("fa2") else "bf16 in / fp32 state",
+                "data": "synthetic (seeded, B200 config shapes)", "config": cfg,
+                "roofline": roofline(head, hr), "cpu_baseline": cpu,
+                "e2e": e2e if e2e is not None else None,
+                "gpu_launches": args.steps, "clocks": clocks,
+                "also": {w: {"value": r["value"], "unit": r["unit"], "ms_per_step": r["ms"],
+                             "roofline": roofline(w, r), **({"config": r["config"]} if "config" in r else {})}
+                         for w, r in results.items() if w != head}}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -267,7 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait(&bar_s[i], j & 1, p.status, kDevTimeoutMma)) { ok = false; break; }
+      // tcgen05.ld/st are warp-collective: the whole warp continues or stops together
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_s[i], j & 1, p.status, kDevTimeoutMma))) { ok = false; break; }
       tc_fence_after();
       uint32_t raw[128];
       tmem_ld64(lane_base + col_s, *reinterpret_cast<uint32_t(*)[64]>(&raw[0]));
@@ -287,22 +288,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int cc = 1; cc < 128; ++cc) mx = fmaxf(mx, s[cc]);
       const float mx_scaled = mx * c;
-      if (mx_scaled > m + kRescaleThreshold) {
-        const float alpha = ex2_approx(m - mx_scaled);
-        if (j > 0) {
-          // O holds sum_{<j} P V; PV(j-1) is complete because S(j) was committed after it.
-#pragma unroll 1
-          for (int dc = 0; dc < D; dc += 32) {
-            uint32_t o_raw[32];
-            tmem_ld32(lane_base + col_o + dc, o_raw);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * alpha);
-            tmem_st32(lane_base + col_o + dc, o_raw);
-          }
-        }
-        l *= alpha;
+      // Lazy rescale: a row moves its running max only when it grew by more than 2^8.  The
+      // decision is per row, the O read-modify-write is done by the whole warp (alpha = 1 for
+      // rows that keep their max) because tcgen05.ld/st are warp-collective.
+      const bool grow = mx_scaled > m + kRescaleThreshold;
+      float alpha = 1.0f;
+      if (grow) {
+        alpha = ex2_approx(m - mx_scaled);
         m = mx_scaled;
       }
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O holds sum_{<j} P V; PV(j-1) is complete because S(j) was committed after it.
+#pragma unroll 1
+        for (int dc = 0; dc < D; dc += 32) {
+          uint32_t o_raw[32];
+          tmem_ld32(lane_base + col_o + dc, o_raw);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * alpha);
+          tmem_st32(lane_base + col_o + dc, o_raw);
+        }
+      }
+      l *= alpha;
       float rowsum = 0.0f;
 #pragma unroll
       for (int chunk = 0; chunk < 4; ++chunk) {
@@ -321,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&bar_p[i]);
     }
-    if (ok && n_kv > 0 && mbar_wait(&bar_o[i], 0, p.status, kDevTimeoutMma)) {
+    if (ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&bar_o[i], 0, p.status, kDevTimeoutMma))) {
       tc_fence_after();
       const float inv_l = 1.0f / l;
       __nv_bfloat16* orow = p.o + static_cast<long long>(b) * p.o_sb + static_cast<long long>(tile[i].head) * p.o_sh +

@@ -8,14 +8,17 @@
 // Chunked form used here (C = 64 tokens, in-chunk cumulative log decay G_t, incoming state S0):
 //   L_ts  = beta_t exp(G_t - G_s) (k_t . k_s)          s < t
 //   T     = (I + L)^-1 diag(beta)                      (unit-lower inverse, fp32, blocked 16x16)
-//   W     = T diag(e^G) K                              (tensor core)
-//   Delta = T V - W S0^T                               (tensor core; T split into bf16 hi + lo)
+//   W     = T diag(e^G) K                              (tensor core; T diag(e^G) as bf16 hi + lo)
+//   Delta = T V - W S0^T                               (tensor core; T as hi + lo; W S0^T as the
+//                                                       3-term product W_hi S_hi + W_lo S_hi + W_hi S_lo)
 //   O     = scale (diag(e^G) Q S0^T + P Delta),  P_ts = exp(G_t - G_s)(q_t . k_s), s <= t
 //   S     = e^{G_C} S0 + (diag(e^{G_C - G}) Delta)^T K (tensor core; Delta' split hi + lo)
 // Every contraction is an M=128 tcgen05 MMA because the CTA keeps the VALUE dimension on the
 // 128 TMEM lanes ("transposed" products: Delta^T, O^T, S with lane = value row; W^T with
-// lane = key row).  The fp32 master state never leaves TMEM between chunks; a bf16 copy in
-// shared memory is the MMA operand for the next chunk.
+// lane = key row).  The fp32 master state never leaves TMEM between chunks; a hi + lo bf16 copy
+// in shared memory is the MMA operand for the next chunk.  The hi/lo splits keep every product
+// that feeds the state at ~16 significant bits, so the fp32 final state stays within 1e-3
+// relative of the fp32 recurrence even when the decay is weak.
 //
 // One CTA processes one (sequence, value head) unit, all its chunks in order.  Warp roles:
 //   warps 0-3   state chain: Delta pass (Delta -> bf16 operands in TMEM), state pass (S ->
@@ -52,29 +55,35 @@ constexpr uint32_t kColO = 320;    // O^T fp32, 64 cols
 constexpr uint32_t kColW = 384;    // W^T fp32 (lane = key row), 64 cols
 constexpr uint32_t kColQK = 448;   // lanes 0-63: Q K^T, lanes 64-127: K K^T, 64 cols
 
-// shared memory layout (bytes, 1024-aligned tiles)
+// shared memory layout (bytes; every MMA tile starts on a 1024-byte boundary)
 constexpr int kSlotBytes = 32768;                  // stacked [Q;K] chunk tile: 2 boxes of 128 rows x 128 B
-constexpr int kOffSlot0 = 0;
-constexpr int kOffSlot1 = kSlotBytes;
+constexpr int kOffSlot0 = 0;                       //   rows 0-63 of a box: Q (scaled in place to e^G Q)
+constexpr int kOffSlot1 = kSlotBytes;              //   rows 64-127: K
 constexpr int kOffV = 2 * kSlotBytes;              // V chunk tile: 2 boxes of 64 rows x 128 B
-constexpr int kOffP0 = kOffV + 16384;              // P tiles [t][s] bf16, 2 slots
-constexpr int kOffP1 = kOffP0 + 8192;
-constexpr int kOffThi = kOffP1 + 8192;             // T hi [t][s]
+constexpr int kOffP = kOffV + 16384;               // P [t][s] bf16
+constexpr int kOffThi = kOffP + 8192;              // T hi [t][s]
 constexpr int kOffTlo = kOffThi + 8192;            // T lo
-constexpr int kOffTG = kOffTlo + 8192;             // T diag(e^G)
-constexpr int kOffWneg = kOffTG + 8192;            // -W as [k][t], 128 rows x 128 B
-constexpr int kOffS0 = kOffWneg + 16384;           // bf16 state copies [v][k]: 2 boxes of 128 rows x 128 B
-constexpr int kOffS1 = kOffS0 + 32768;
-constexpr int kOffScratch = kOffS1 + 32768;        // solve scratch fp32 [64][kScStride]
-constexpr int kScStride = 68;
-constexpr int kOffParams = kOffScratch + 64 * kScStride * 4;
+constexpr int kOffTGhi = kOffTlo + 8192;           // T diag(e^G) hi
+constexpr int kOffTGlo = kOffTGhi + 8192;          // T diag(e^G) lo
+constexpr int kOffWhi = kOffTGlo + 8192;           // -W hi as [k][t], 128 rows x 128 B
+constexpr int kOffWlo = kOffWhi + 16384;           // -W lo
+constexpr int kOffShi = kOffWlo + 16384;           // state copy hi [v][k]: 2 boxes of 128 rows x 128 B
+constexpr int kOffSlo = kOffShi + 32768;           // state copy lo
+constexpr int kOffParams = kOffSlo + 32768;
 constexpr int kParamsBytes = 1280;
-constexpr int kSmemBytes = kOffParams + 2 * kParamsBytes;  // + 2 parameter slots
+constexpr int kSmemBytes = kOffParams + 2 * kParamsBytes;
+// The triangular solve works in fp32 scratch that aliases the four T tiles (it writes them only
+// after it has read everything it needs), and keeps its block temporaries in the T^G lo tile.
+constexpr int kOffScratch = kOffThi;
+constexpr int kScStride = 68;
+constexpr int kOffSolveTmp = kOffTGlo;
+static_assert(64 * kScStride * 4 <= kOffSolveTmp - kOffScratch, "solve scratch overlaps its temporaries");
+static_assert(kSmemBytes + 1024 <= 227 * 1024, "shared memory budget");
 
 struct ChunkParams {
   float beta[kC];         // write strength (0 for tokens past the sequence end)
   float g2[kC];           // in-chunk inclusive prefix sum of g, in log2 units
-  float eg[kC];           // exp(G_t)
+  float eg[kC];           // exp(G_t) (0 past the end)
   float egr[kC];          // exp(G_C - G_t) (0 past the end)
   float gamma_c;          // exp(G_C)
   int n_valid;
@@ -95,35 +104,78 @@ struct Params {
   uint32_t* status;
 };
 
+// Hand-off barriers, each a 2-slot array indexed by chunk parity (event of chunk c lives in slot
+// c & 1 and completes its (c >> 1)-th phase).  Every producer of chunk c+2's event causally
+// follows every waiter of chunk c's event, so no waiter can fall two phases behind.
 struct Barriers {
   uint64_t in_full[2], v_full[2], slot_free[2], v_free[2];
   uint64_t qk_done[2], qk_read[2], g_ready[2], prep1[2];
   uint64_t w_done[2], wneg[2], delta[2], da_done[2];
   uint64_t snew[2], s_ready[2], o_done[2], o_free[2];
+  uint64_t p_ready[2];
 };
 
 __device__ __forceinline__ bool wait_c(uint64_t* bars, int c, uint32_t* status, uint32_t code) {
   return mbar_wait(&bars[c & 1], (c >> 1) & 1, status, code);
 }
 __device__ __forceinline__ bool test_c(uint64_t* bars, int c) { return mbar_test(&bars[c & 1], (c >> 1) & 1); }
+// Warp-uniform wait: tcgen05.ld/st are warp-collective, so a warp continues or stops as a whole.
+__device__ __forceinline__ bool wait_c_warp(uint64_t* bars, int c, uint32_t* status, uint32_t code) {
+  return __all_sync(0xffffffffu, wait_c(bars, c, status, code));
+}
 
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// write 64 bf16 values (packed as 32 uint32) as row `row` of a 128-byte-swizzled tile
-__device__ __forceinline__ void store_row_sw128(uint8_t* tile, int row, const uint32_t (&v)[32]) {
+// write 32 bf16 values (16 packed uint32) as half `h` (bytes [64h, 64h+64)) of row `row` of a
+// 128-byte-swizzled tile
+__device__ __forceinline__ void store_half_row_sw128(uint8_t* tile, int row, int h, const uint32_t (&v)[16]) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    uint4 val = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    *reinterpret_cast<uint4*>(tile + row * 128 + ((j ^ (row & 7)) << 4)) = val;
+  for (int j = 0; j < 4; ++j) {
+    const int chunk = 4 * h + j;
+    *reinterpret_cast<uint4*>(tile + row * 128 + ((chunk ^ (row & 7)) << 4)) =
+        make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   }
 }
 
-__device__ __forceinline__ float bf16_lo_part(float x, uint32_t& hi_bits) {
-  const __nv_bfloat16 h = __float2bfloat16_rn(x);
-  hi_bits = __bfloat16_as_ushort(h);
-  return x - __bfloat162float(h);
+__device__ __forceinline__ void store_row_sw128(uint8_t* tile, int row, const uint32_t (&v)[32]) {
+  store_half_row_sw128(tile, row, 0, *reinterpret_cast<const uint32_t(*)[16]>(&v[0]));
+  store_half_row_sw128(tile, row, 1, *reinterpret_cast<const uint32_t(*)[16]>(&v[16]));
+}
+
+// x = hi + lo with hi = bf16(x), lo = bf16(x - hi): ~16 significant bits in two bf16 operands
+__device__ __forceinline__ void split_pack(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat16 h0 = __float2bfloat16_rn(x0);
+  const __nv_bfloat16 h1 = __float2bfloat16_rn(x1);
+  hi = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+  lo = pack_bf16x2(x0 - __bfloat162float(h0), x1 - __bfloat162float(h1));
+}
+
+// Writes 64 fp32 state values (columns [64*half, 64*half+64) of row v) as the hi and lo bf16
+// state copies (box `half` of each).
+__device__ __forceinline__ void store_state_half(uint8_t* smem, int v, int half, const uint32_t (&sv)[64]) {
+#pragma unroll
+  for (int q4 = 0; q4 < 2; ++q4) {
+    uint32_t hi[16], lo[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      split_pack(__uint_as_float(sv[32 * q4 + 2 * j]), __uint_as_float(sv[32 * q4 + 2 * j + 1]), hi[j], lo[j]);
+    store_half_row_sw128(smem + kOffShi + half * 16384, v, q4, hi);
+    store_half_row_sw128(smem + kOffSlo + half * 16384, v, q4, lo);
+  }
+}
+
+__device__ __forceinline__ void output_pass(const Params& p, uint32_t lane_base, int tok0, int len, int cp, int h,
+                                            int r) {
+  const int nv = min(kC, len - cp * kC);
+  uint32_t row[64];
+  tmem_ld64(lane_base + kColO, row);
+  __nv_bfloat16* dst = p.out + (static_cast<size_t>(tok0 + cp * kC) * p.hv + h) * kD + r;
+  const size_t tstride = static_cast<size_t>(p.hv) * kD;
+#pragma unroll
+  for (int t = 0; t < kC; ++t)
+    if (t < nv) dst[t * tstride] = __float2bfloat16_rn(__uint_as_float(row[t]) * p.scale);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -161,6 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars.da_done[i], 128);
       mbar_init(&bars.s_ready[i], 128);
       mbar_init(&bars.o_free[i], 128);
+      mbar_init(&bars.p_ready[i], 128);
     }
     fence_barrier_init();
   }
@@ -187,9 +240,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // =========================================================== state chain (lane = value row)
     const int v = threadIdx.x;
     const uint32_t lane_base = tmem_addr(tbase, warp * 32, 0);
-    bool ok = true;
-    // --- initial state: bf16 copy -> S slot 0, TMEM S <- gamma_C(0) * S0
-    ok = wait_c(bars.g_ready, 0, p.status, kDevTimeoutPipe);
+    // --- initial state: hi/lo bf16 copies, TMEM S <- gamma_C(0) * S0
+    bool ok = wait_c_warp(bars.g_ready, 0, p.status, kDevTimeoutPipe);
     if (ok) {
       const float gam = params[0].gamma_c;
 #pragma unroll 1
@@ -204,10 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           sv[j + 2] = __float_as_uint(val.z);
           sv[j + 3] = __float_as_uint(val.w);
         }
-        uint32_t packed[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) packed[j] = pack_bf16x2(__uint_as_float(sv[2 * j]), __uint_as_float(sv[2 * j + 1]));
-        store_row_sw128(smem + kOffS0 + half * 16384, v, packed);
+        store_state_half(smem, v, half, sv);
 #pragma unroll
         for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
         tmem_st32(lane_base + kColS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
@@ -221,8 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int c = 0; ok && c < nchunks; ++c) {
       const ChunkParams& pc = params[c & 1];
       const uint32_t colx = (c & 1) ? kColX1 : kColX0;
-      // --- Delta pass
-      if (!wait_c(bars.delta, c, p.status, kDevTimeoutMma)) { ok = false; break; }
+      // --- Delta pass: Delta^T (fp32) -> bf16 Delta, Delta' = e^{G_C - G} Delta as hi + lo
+      if (!wait_c_warp(bars.delta, c, p.status, kDevTimeoutMma)) { ok = false; break; }
       tc_fence_after();
       {
         uint32_t d[64];
@@ -233,13 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float d0 = __uint_as_float(d[2 * j]);
           const float d1 = __uint_as_float(d[2 * j + 1]);
           pk[j] = pack_bf16x2(d0, d1);
-          const float e0 = d0 * pc.egr[2 * j];
-          const float e1 = d1 * pc.egr[2 * j + 1];
-          uint32_t h0, h1;
-          const float l0 = bf16_lo_part(e0, h0);
-          const float l1 = bf16_lo_part(e1, h1);
-          hi[j] = h0 | (h1 << 16);
-          lo[j] = pack_bf16x2(l0, l1);
+          split_pack(d0 * pc.egr[2 * j], d1 * pc.egr[2 * j + 1], hi[j], lo[j]);
         }
         tmem_st32(lane_base + colx, pk);
         tmem_st32(lane_base + colx + 32, hi);
@@ -248,16 +291,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&bars.da_done[c & 1]);
-      // --- state pass
-      if (!wait_c(bars.snew, c, p.status, kDevTimeoutMma)) { ok = false; break; }
+      // --- state pass: S (fp32) -> hi/lo bf16 copies for the next chunk, pre-scale by its decay
+      if (!wait_c_warp(bars.snew, c, p.status, kDevTimeoutMma)) { ok = false; break; }
       tc_fence_after();
       const bool last = (c == nchunks - 1);
       float gam = 1.0f;
       if (!last) {
-        if (!wait_c(bars.g_ready, c + 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
+        if (!wait_c_warp(bars.g_ready, c + 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
         gam = params[(c + 1) & 1].gamma_c;
       }
-      uint8_t* sdst = smem + (((c + 1) & 1) ? kOffS1 : kOffS0);
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {
         uint32_t sv[64];
@@ -269,11 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
                                                               __uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3]));
         } else {
-          uint32_t packed[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            packed[j] = pack_bf16x2(__uint_as_float(sv[2 * j]), __uint_as_float(sv[2 * j + 1]));
-          store_row_sw128(sdst + half * 16384, v, packed);
+          store_state_half(smem, v, half, sv);
 #pragma unroll
           for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
           tmem_st32(lane_base + kColS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
@@ -296,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ChunkParams& pc = params[c & 1];
       // --- (1) decay prefix sums for chunk c (warp 4)
       if (warp == 4) {
-        if (c >= 2 && !wait_c(bars.da_done, c - 2, p.status, kDevTimeoutPipe)) { ok = false; break; }
+        if (c >= 2 && !wait_c_warp(bars.da_done, c - 2, p.status, kDevTimeoutPipe)) { ok = false; break; }
         const int n_valid = min(kC, len - c * kC);
         const int t0 = 2 * lane, t1 = 2 * lane + 1;
         const size_t base = static_cast<size_t>(tok0 + c * kC);
@@ -329,27 +367,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         mbar_arrive(&bars.g_ready[c & 1]);
       }
-      // --- (2) QK / KK read-out: P tile, e^G-scaled Q (in place), L rows -> scratch
-      if (!wait_c(bars.qk_done, c, p.status, kDevTimeoutMma)) { ok = false; break; }
-      if (!wait_c(bars.g_ready, c, p.status, kDevTimeoutPipe)) { ok = false; break; }
-      if (c >= 1 && !wait_c(bars.prep1, c - 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
-      if (c >= 2 && !wait_c(bars.o_done, c - 2, p.status, kDevTimeoutMma)) { ok = false; break; }
+      // --- (2a) QK / KK read-out: e^G-scaled Q (in place), L rows -> solve scratch; P row kept
+      //          in registers until the P tile is free
+      bool ready = wait_c_warp(bars.qk_done, c, p.status, kDevTimeoutMma);
+      if (ready) ready = wait_c_warp(bars.g_ready, c, p.status, kDevTimeoutPipe);
+      if (ready && c >= 1) ready = wait_c_warp(bars.w_done, c - 1, p.status, kDevTimeoutMma);  // T tiles free
+      if (!ready) { ok = false; break; }
       tc_fence_after();
+      uint32_t prow[32];
       {
         uint32_t row[64];
         tmem_ld64(lane_base + kColQK, row);
         if (r < 64) {
           const int t = r;
           const float gt = pc.g2[t];
-          uint32_t packed[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int s0 = 2 * j, s1 = 2 * j + 1;
             const float p0 = s0 <= t ? __uint_as_float(row[s0]) * ex2_approx(gt - pc.g2[s0]) : 0.0f;
             const float p1 = s1 <= t ? __uint_as_float(row[s1]) * ex2_approx(gt - pc.g2[s1]) : 0.0f;
-            packed[j] = pack_bf16x2(p0, p1);
+            prow[j] = pack_bf16x2(p0, p1);
           }
-          store_row_sw128(smem + ((c & 1) ? kOffP1 : kOffP0), t, packed);
           // Q row t lives in rows 0..63 of the stacked slot, 2 boxes of 64 columns
           uint8_t* slot = smem + ((c & 1) ? kOffSlot1 : kOffSlot0);
           const float eg = pc.eg[t];
@@ -388,52 +426,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars.qk_read[c & 1]);
-      // --- (3) W pass: W^T (lane = key row k) -> -W as [k][t] bf16
-      if (!wait_c(bars.w_done, c, p.status, kDevTimeoutMma)) { ok = false; break; }
-      if (c >= 1 && !wait_c(bars.delta, c - 1, p.status, kDevTimeoutMma)) { ok = false; break; }
+      // --- (3) W pass: W^T (lane = key row k) -> -W as [k][t], hi and lo bf16 tiles
+      ready = wait_c_warp(bars.w_done, c, p.status, kDevTimeoutMma);
+      if (ready && c >= 1) ready = wait_c_warp(bars.delta, c - 1, p.status, kDevTimeoutMma);  // W tiles free
+      if (!ready) { ok = false; break; }
       tc_fence_after();
-      {
-        uint32_t row[64];
-        tmem_ld64(lane_base + kColW, row);
-        uint32_t packed[32];
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t row[32];
+        tmem_ld32(lane_base + kColW + 32 * half, row);
+        uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          packed[j] = pack_bf16x2(-__uint_as_float(row[2 * j]), -__uint_as_float(row[2 * j + 1]));
-        store_row_sw128(smem + kOffWneg, r, packed);
+        for (int j = 0; j < 16; ++j)
+          split_pack(-__uint_as_float(row[2 * j]), -__uint_as_float(row[2 * j + 1]), hi[j], lo[j]);
+        store_half_row_sw128(smem + kOffWhi, r, half, hi);
+        store_half_row_sw128(smem + kOffWlo, r, half, lo);
       }
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars.wneg[c & 1]);
-      // --- (4) output pass of the previous chunk
+      // --- (4) output pass of the previous chunk, then the P tile of this chunk (single buffer:
+      //         the previous chunk's P V MMA has completed once its output is ready)
       if (c >= 1) {
-        if (!wait_c(bars.o_done, c - 1, p.status, kDevTimeoutMma)) { ok = false; break; }
+        if (!wait_c_warp(bars.o_done, c - 1, p.status, kDevTimeoutMma)) { ok = false; break; }
         tc_fence_after();
-        const int cp = c - 1;
-        const int nv = min(kC, len - cp * kC);
-        uint32_t row[64];
-        tmem_ld64(lane_base + kColO, row);
-        __nv_bfloat16* dst = p.out + (static_cast<size_t>(tok0 + cp * kC) * p.hv + h) * kD + r;
-        const size_t tstride = static_cast<size_t>(p.hv) * kD;
-#pragma unroll
-        for (int t = 0; t < kC; ++t)
-          if (t < nv) dst[t * tstride] = __float2bfloat16_rn(__uint_as_float(row[t]) * p.scale);
+        output_pass(p, lane_base, tok0, len, c - 1, h, r);
         tc_fence_before();
-        mbar_arrive(&bars.o_free[cp & 1]);
+        mbar_arrive(&bars.o_free[(c - 1) & 1]);
       }
+      if (r < 64) store_row_sw128(smem + kOffP, r, prow);
+      fence_async_smem();
+      mbar_arrive(&bars.p_ready[c & 1]);
     }
-    if (ok) {
-      const int cp = nchunks - 1;
-      if (wait_c(bars.o_done, cp, p.status, kDevTimeoutMma)) {
-        tc_fence_after();
-        const int nv = min(kC, len - cp * kC);
-        uint32_t row[64];
-        tmem_ld64(lane_base + kColO, row);
-        __nv_bfloat16* dst = p.out + (static_cast<size_t>(tok0 + cp * kC) * p.hv + h) * kD + r;
-        const size_t tstride = static_cast<size_t>(p.hv) * kD;
-#pragma unroll
-        for (int t = 0; t < kC; ++t)
-          if (t < nv) dst[t * tstride] = __float2bfloat16_rn(__uint_as_float(row[t]) * p.scale);
-      }
+    if (ok && wait_c_warp(bars.o_done, nchunks - 1, p.status, kDevTimeoutMma)) {
+      tc_fence_after();
+      output_pass(p, lane_base, tok0, len, nchunks - 1, h, r);
     }
   } else if (warp < 12) {
     // =========================================================== blocked triangular solve
@@ -441,15 +468,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // transposed into scratch[s][t].  Diagonal blocks D_i = (I + L_ii)^-1 first, then the
     // off-diagonal blocks by distance: That_ij = -D_i * sum_{k=j}^{i-1} L_ik That_kj.
     const int tid = threadIdx.x - 256;
-    float* tmp = reinterpret_cast<float*>(smem + kOffTG);  // X temporaries, reuses the T^G tile
+    float* tmp = reinterpret_cast<float*>(smem + kOffSolveTmp);
     auto Lv = [&](int t, int s) -> float { return scratch[t * kScStride + s]; };
     auto Tv = [&](int t, int s) -> float {  // That[t][s], any t, s
       return t == s ? 1.0f : (t > s ? scratch[s * kScStride + t] : 0.0f);
     };
     bool ok = true;
     for (int c = 0; ok && c < nchunks; ++c) {
-      bool ready = wait_c(bars.qk_read, c, p.status, kDevTimeoutPipe);
-      if (ready && c >= 1) ready = wait_c(bars.w_done, c - 1, p.status, kDevTimeoutMma);
+      const bool ready = wait_c(bars.qk_read, c, p.status, kDevTimeoutPipe);
       // the four warps leave together or not at all (they meet at named barriers below)
       if (!named_sync_and(1, 128, ready)) { ok = false; break; }
       const ChunkParams& pc = params[c & 1];
@@ -478,8 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // steps 2-4: block distance 1, 2, 3
 #pragma unroll 1
       for (int dist = 1; dist <= 3; ++dist) {
-        const int nblk = 4 - dist;  // blocks (i, j = i - dist), i = dist..3
-        const int nelem = nblk * 256;
+        const int nelem = (4 - dist) * 256;  // blocks (i, j = i - dist), i = dist..3
         // X = sum_{k=j}^{i-1} L_ik That_kj   (16x16 each)
         for (int e = tid; e < nelem; e += 128) {
           const int bi = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
@@ -504,34 +529,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         named_sync(1, 128);
       }
-      // step 5: T = That diag(beta) (hi/lo) and T diag(e^G) as bf16 [t][s] tiles
+      // step 5: T = That diag(beta) and T diag(beta e^G), each as hi + lo bf16 [t][s] tiles.
+      // Rows are computed into registers first: the tiles overwrite the scratch.
       {
         const int t = tid & 63;
+        const bool with_decay = tid >= 64;
         uint32_t a[32], b[32];
-        if (tid < 64) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float v0 = Tv(t, 2 * j) * pc.beta[2 * j];
-            const float v1 = Tv(t, 2 * j + 1) * pc.beta[2 * j + 1];
-            uint32_t h0, h1;
-            const float l0 = bf16_lo_part(v0, h0);
-            const float l1 = bf16_lo_part(v1, h1);
-            a[j] = h0 | (h1 << 16);
-            b[j] = pack_bf16x2(l0, l1);
+        for (int j = 0; j < 32; ++j) {
+          const int s0 = 2 * j, s1 = 2 * j + 1;
+          float w0 = pc.beta[s0], w1 = pc.beta[s1];
+          if (with_decay) {
+            w0 *= pc.eg[s0];
+            w1 *= pc.eg[s1];
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            a[j] = pack_bf16x2(Tv(t, 2 * j) * pc.beta[2 * j] * pc.eg[2 * j],
-                               Tv(t, 2 * j + 1) * pc.beta[2 * j + 1] * pc.eg[2 * j + 1]);
+          split_pack(Tv(t, s0) * w0, Tv(t, s1) * w1, a[j], b[j]);
         }
-        named_sync(1, 128);  // tmp (aliasing the T^G tile) is dead from here on
-        if (tid < 64) {
-          store_row_sw128(smem + kOffThi, t, a);
-          store_row_sw128(smem + kOffTlo, t, b);
-        } else {
-          store_row_sw128(smem + kOffTG, t, a);
-        }
+        named_sync(1, 128);
+        store_row_sw128(smem + (with_decay ? kOffTGhi : kOffThi), t, a);
+        store_row_sw128(smem + (with_decay ? kOffTGlo : kOffTlo), t, b);
       }
       fence_async_smem();
       mbar_arrive(&bars.prep1[c & 1]);
@@ -566,23 +582,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // =========================================================== MMA issuer (polling)
+    // Groups per chunk c, issued in dependency order, critical path first:
+    //   T1  [Q;K] K^T                                   -> QK region          (state-independent)
+    //   T2  W^T = K^T (TG_hi + TG_lo)^T ; Delta^T = V^T (T_hi + T_lo)^T        (state-independent)
+    //   T3a Delta^T += S_hi (-W_hi)^T + S_lo (-W_hi)^T + S_hi (-W_lo)^T        (critical)
+    //   T3b O^T = S_hi (e^G Q)^T
+    //   T4  S += Delta'_hi^T K + Delta'_lo^T K                                  (critical)
+    //   T5  O^T += Delta^T P^T
     if (lane == 0 && nchunks > 0) {
       const uint32_t id_qk = make_idesc(128, 64, 1, 0, 0);    // [Q;K] K^T
-      const uint32_t id_w = make_idesc(128, 64, 1, 1, 0);     // W^T = K^T (T^G)^T, A MN-major
-      const uint32_t id_vt = make_idesc(128, 64, 1, 1, 0);    // Delta^T = V^T T^T, A MN-major
-      const uint32_t id_sw = make_idesc(128, 64, 1, 0, 1);    // Delta^T += S (-W)^T, B MN-major
-      const uint32_t id_upd = make_idesc(128, 128, 1, 0, 1);  // S += Delta'^T K, A TMEM, B MN-major
-      const uint32_t id_sq = make_idesc(128, 64, 1, 0, 0);    // O^T = S Qt^T
-      const uint32_t id_dp = make_idesc(128, 64, 1, 0, 0);    // O^T += Delta^T P^T, A TMEM
+      const uint32_t id_mnk = make_idesc(128, 64, 1, 1, 0);   // A MN-major (K^T, V^T), B K-major
+      const uint32_t id_sw = make_idesc(128, 64, 1, 0, 1);    // A K-major (S), B MN-major (-W as [k][t])
+      const uint32_t id_upd = make_idesc(128, 128, 1, 0, 1);  // A TMEM, B MN-major (K as [t][k])
+      const uint32_t id_kk = make_idesc(128, 64, 1, 0, 0);    // both K-major / A TMEM
       const uint32_t a_thi = smem_u32(smem + kOffThi), a_tlo = smem_u32(smem + kOffTlo);
-      const uint32_t a_tg = smem_u32(smem + kOffTG), a_v = smem_u32(smem + kOffV);
-      const uint32_t a_wneg = smem_u32(smem + kOffWneg);
-      int n1 = 0, n2 = 0, n3 = 0, n4 = 0, n5 = 0;
+      const uint32_t a_tghi = smem_u32(smem + kOffTGhi), a_tglo = smem_u32(smem + kOffTGlo);
+      const uint32_t a_v = smem_u32(smem + kOffV), a_p = smem_u32(smem + kOffP);
+      const uint32_t a_whi = smem_u32(smem + kOffWhi), a_wlo = smem_u32(smem + kOffWlo);
+      const uint32_t a_shi = smem_u32(smem + kOffShi), a_slo = smem_u32(smem + kOffSlo);
+      auto kmaj = [](uint32_t base, int kk) {  // K-major tile of 2 boxes (16 KB apart), 16-element k step
+        return make_sdesc_sw128(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+      };
+      int n1 = 0, n2 = 0, n3a = 0, n3b = 0, n4 = 0, n5 = 0;
       const int N = nchunks;
       unsigned long long idle_since = 0;
+      uint32_t idle_polls = 0;
       while (n5 < N) {
         bool issued = false;
-        if (n4 < n3 && n4 <= n5 && test_c(bars.da_done, n4)) {
+        if (n4 < n3b && test_c(bars.da_done, n4)) {
           // T4: S += Delta'_hi^T K + Delta'_lo^T K
           const int c = n4;
           tc_fence_after();
@@ -597,58 +624,65 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&bars.snew[c & 1]);
           ++n4;
           issued = true;
-        } else if (n3 < n2 && n3 == n4 && test_c(bars.wneg, n3) && test_c(bars.s_ready, n3)) {
-          // T3: Delta^T += S (-W)^T
-          const int c = n3;
+        } else if (n3a < n2 && n3a == n4 && test_c(bars.wneg, n3a) && test_c(bars.s_ready, n3a)) {
+          // T3a: Delta^T += S_hi (-W_hi)^T + S_lo (-W_hi)^T + S_hi (-W_lo)^T
+          const int c = n3a;
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + ((c & 1) ? kOffS1 : kOffS0));
           const uint32_t colx = (c & 1) ? kColX1 : kColX0;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_bf16_ss(tbase + colx, make_sdesc_sw128(sa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                         make_sdesc_sw128(a_wneg + kk * 2048, 16384, 1024), id_sw, 1u);
+          for (int term = 0; term < 3; ++term) {
+            const uint32_t sa = term == 1 ? a_slo : a_shi;
+            const uint32_t wa = term == 2 ? a_wlo : a_whi;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16_ss(tbase + colx, kmaj(sa, kk), make_sdesc_sw128(wa + kk * 2048, 16384, 1024), id_sw, 1u);
+          }
           umma_commit(&bars.delta[c & 1]);
-          ++n3;
+          ++n3a;
           issued = true;
-        } else if (n5 < n4 && test_c(bars.qk_read, n5) && (n5 == 0 || test_c(bars.o_free, n5 - 1))) {
-          // T5: O^T = S Qt^T + Delta^T P^T
+        } else if (n3b < n3a && (n3b == 0 || test_c(bars.o_free, n3b - 1))) {
+          // T3b: O^T = S_hi (e^G Q)^T
+          const int c = n3b;
+          tc_fence_after();
+          const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16_ss(tbase + kColO, kmaj(a_shi, kk), kmaj(slot, kk), id_kk, kk > 0 ? 1u : 0u);
+          ++n3b;
+          issued = true;
+        } else if (n5 < n4 && test_c(bars.p_ready, n5)) {
+          // T5: O^T += Delta^T P^T
           const int c = n5;
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + ((c & 1) ? kOffS1 : kOffS0));
-          const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
-          const uint32_t pa = smem_u32(smem + ((c & 1) ? kOffP1 : kOffP0));
           const uint32_t colx = (c & 1) ? kColX1 : kColX0;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_bf16_ss(tbase + kColO, make_sdesc_sw128(sa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                         make_sdesc_sw128(slot + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), id_sq,
-                         kk > 0 ? 1u : 0u);
-#pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16_ts(tbase + kColO, tbase + colx + 8 * kk, make_sdesc_sw128(pa + kk * 32, 16, 1024), id_dp, 1u);
+            umma_bf16_ts(tbase + kColO, tbase + colx + 8 * kk, make_sdesc_sw128(a_p + kk * 32, 16, 1024), id_kk, 1u);
           umma_commit(&bars.o_done[c & 1]);
           umma_commit(&bars.slot_free[c & 1]);
           ++n5;
           issued = true;
-        } else if (n2 < n1 && n2 < n4 + 2 && n2 < n5 + 2 && test_c(bars.prep1, n2) && test_c(bars.v_full, n2) &&
+        } else if (n2 < n1 && n2 < n5 + 2 && test_c(bars.prep1, n2) && test_c(bars.v_full, n2) &&
                    (n2 == 0 || test_c(bars.wneg, n2 - 1))) {
-          // T2: W^T = K^T (T^G)^T ; Delta^T = V^T T_hi^T + V^T T_lo^T
+          // T2: W^T = K^T (TG_hi + TG_lo)^T ; Delta^T = V^T T_hi^T + V^T T_lo^T
           const int c = n2;
           tc_fence_after();
           const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
           const uint32_t colx = (c & 1) ? kColX1 : kColX0;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16_ss(tbase + kColW, make_sdesc_sw128(slot + 8192 + kk * 2048, 16384, 1024),
-                         make_sdesc_sw128(a_tg + kk * 32, 16, 1024), id_w, kk > 0 ? 1u : 0u);
+          for (int part = 0; part < 2; ++part)
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16_ss(tbase + colx, make_sdesc_sw128(a_v + kk * 2048, 8192, 1024),
-                         make_sdesc_sw128(a_thi + kk * 32, 16, 1024), id_vt, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16_ss(tbase + kColW, make_sdesc_sw128(slot + 8192 + kk * 2048, 16384, 1024),
+                           make_sdesc_sw128((part ? a_tglo : a_tghi) + kk * 32, 16, 1024), id_mnk,
+                           (part > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16_ss(tbase + colx, make_sdesc_sw128(a_v + kk * 2048, 8192, 1024),
-                         make_sdesc_sw128(a_tlo + kk * 32, 16, 1024), id_vt, 1u);
+          for (int part = 0; part < 2; ++part)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16_ss(tbase + colx, make_sdesc_sw128(a_v + kk * 2048, 8192, 1024),
+                           make_sdesc_sw128((part ? a_tlo : a_thi) + kk * 32, 16, 1024), id_mnk,
+                           (part > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&bars.w_done[c & 1]);
           umma_commit(&bars.v_free[c & 1]);
           ++n2;
@@ -660,23 +694,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_bf16_ss(tbase + kColQK, make_sdesc_sw128(slot + off, 16, 1024),
-                         make_sdesc_sw128(slot + 8192 + off, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
-          }
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16_ss(tbase + kColQK, kmaj(slot, kk), kmaj(slot + 8192, kk), id_qk, kk > 0 ? 1u : 0u);
           umma_commit(&bars.qk_done[c & 1]);
           ++n1;
           issued = true;
         }
         if (issued) {
-          idle_since = 0;
-        } else {
+          idle_polls = 0;
+        } else if ((++idle_polls & 255u) == 0u) {
+          // every 256 empty polls: give up after kWaitTimeoutNs without progress, or as soon as
+          // another warp of the CTA has reported a timeout
           const unsigned long long now = global_timer_ns();
-          if (idle_since == 0) {
-            idle_since = now;
-          } else if (now - idle_since > kWaitTimeoutNs ||
-                     *reinterpret_cast<volatile uint32_t*>(p.status) != 0u) {
+          if (idle_polls == 256u) idle_since = now;
+          if (now - idle_since > kWaitTimeoutNs || *reinterpret_cast<volatile uint32_t*>(p.status) != 0u) {
             record_status(p.status, kDevTimeoutPipe);
             break;
           }

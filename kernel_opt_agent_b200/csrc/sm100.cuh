@@ -69,7 +69,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+// Potentially blocking test: the hardware may suspend the thread for a short while if the phase
+// has not completed yet.  Used inside wait loops.
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -81,15 +83,28 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// Non-blocking test, for a thread that polls several barriers and must not park on one of them.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Wait until the phase with the given parity has completed.  Gives up after kWaitTimeoutNs,
 // records `code` in *status and returns false.  Once *status is non-zero (another warp gave up)
 // the wait returns false as soon as it notices, so a failing CTA drains quickly.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t code) {
-  if (mbar_test(bar, parity)) return true;
+  if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   uint32_t spins = 0;
   while (true) {
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_try(bar, parity)) return true;
     if ((++spins & 63u) == 0u) {
       if (status != nullptr && *reinterpret_cast<volatile uint32_t*>(status) != 0u) return false;
       if (global_timer_ns() - t0 > kWaitTimeoutNs) {
