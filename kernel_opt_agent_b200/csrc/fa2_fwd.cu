@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nmax = max(tile[0].n_kv, tile[1].n_kv);
 
   if (threadIdx.x == 0) {
+    cta_abort_flag() = 0u;
     mbar_init(&bar_q, 1);
     mbar_init(&bar_drain, 1);
     for (int i = 0; i < 2; ++i) {
@@ -177,10 +178,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = j + 1;
       }
       // before the CTA retires, let the last loads land (bounded; a no-op on the normal path)
-      mbar_wait(&bar_q, 0, nullptr, 0);
+      mbar_drain(&bar_q, 0);
       for (int j = max(0, issued - 2); j < issued; ++j) {
-        mbar_wait(&bar_kfull[j & 1], (j >> 1) & 1, nullptr, 0);
-        mbar_wait(&bar_vfull[j & 1], (j >> 1) & 1, nullptr, 0);
+        mbar_drain(&bar_kfull[j & 1], (j >> 1) & 1);
+        mbar_drain(&bar_vfull[j & 1], (j >> 1) & 1);
       }
     }
   } else if (warp == kWarpMma) {
@@ -250,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // every MMA issued by this thread completes before TMEM is released (bounded)
       umma_commit(&bar_drain);
-      mbar_wait(&bar_drain, 0, nullptr, 0);
+      mbar_drain(&bar_drain, 0);
     }
     __syncwarp();
   } else {

@@ -25,11 +25,12 @@
 //               bf16 shared copy, pre-scale by the next chunk's decay), initial/final state
 //   warps 4-7   operands: decay prefix sums, QK/KK read-out (P tile, e^G-scaled Q, L rows),
 //               W pass (W^T -> -W bf16 tile), output pass (O^T -> global)
-//   warps 8-11  blocked triangular solve -> T (hi/lo) and T diag(e^G) tiles
-//   warp 12     TMA producer (stacked Q/K chunk tile, V chunk tile)
-//   warp 13     TMEM owner and MMA issuer; it polls the hand-off barriers and issues the next
-//               ready MMA group, critical-path groups first, so the state chain never waits
-//               behind the next chunk's preparation.
+//   warps 8-9   triangular solve -> T (hi/lo) and T diag(e^G) tiles
+//   warp 10     TMA producer (stacked Q/K chunk tile, V chunk tile)
+//   warp 11     TMEM owner and MMA issuer for the state-independent groups; it polls the
+//               hand-off barriers and issues whichever group is ready.  The state-dependent
+//               groups are issued by the warps that produce their inputs, so the state chain
+//               never waits behind the next chunk's preparation.
 // Hand-off barriers are two-slot arrays indexed by chunk parity.  All waits are bounded.
 #include <cuda_runtime.h>
 
@@ -43,9 +44,9 @@ namespace gdn {
 
 constexpr int kC = 64;     // tokens per chunk
 constexpr int kD = 128;    // head dim (keys and values)
-constexpr int kThreads = 448;
-constexpr int kWarpTma = 12;
-constexpr int kWarpMma = 13;
+constexpr int kThreads = 384;
+constexpr int kWarpTma = 10;
+constexpr int kWarpMma = 11;
 
 // TMEM columns
 constexpr uint32_t kColS = 0;      // state S[v][k] fp32, 128 cols
@@ -72,12 +73,11 @@ constexpr int kOffSlo = kOffShi + 32768;           // state copy lo
 constexpr int kOffParams = kOffSlo + 32768;
 constexpr int kParamsBytes = 1280;
 constexpr int kSmemBytes = kOffParams + 2 * kParamsBytes;
-// The triangular solve works in fp32 scratch that aliases the four T tiles (it writes them only
-// after it has read everything it needs), and keeps its block temporaries in the T^G lo tile.
+// The triangular solve reads L from fp32 scratch that aliases the T hi/lo tiles and keeps its
+// solved columns in a buffer that aliases the T diag(e^G) tiles; it writes the tiles only after
+// both have been read into registers.  L is stored column-major: scratch[s * 64 + t] = L[t][s].
 constexpr int kOffScratch = kOffThi;
-constexpr int kScStride = 68;
-constexpr int kOffSolveTmp = kOffTGlo;
-static_assert(64 * kScStride * 4 <= kOffSolveTmp - kOffScratch, "solve scratch overlaps its temporaries");
+static_assert(kOffTGhi - kOffThi >= 64 * 64 * 4 && kOffWhi - kOffTGhi >= 64 * 64 * 4, "solve buffers");
 static_assert(kSmemBytes + 1024 <= 227 * 1024, "shared memory budget");
 
 struct ChunkParams {
@@ -108,11 +108,11 @@ struct Params {
 // c & 1 and completes its (c >> 1)-th phase).  Every producer of chunk c+2's event causally
 // follows every waiter of chunk c's event, so no waiter can fall two phases behind.
 struct Barriers {
-  uint64_t in_full[2], v_full[2], slot_free[2], v_free[2];
+  uint64_t in_full[2], v_full[2], v_free[2];
   uint64_t qk_done[2], qk_read[2], g_ready[2], prep1[2];
   uint64_t w_done[2], wneg[2], delta[2], da_done[2];
-  uint64_t snew[2], s_ready[2], o_done[2], o_free[2];
-  uint64_t p_ready[2];
+  uint64_t snew[2], s_ready[2], o_done[2];
+  uint64_t p_ready[2], t3b[2];
 };
 
 __device__ __forceinline__ bool wait_c(uint64_t* bars, int c, uint32_t* status, uint32_t code) {
@@ -123,6 +123,22 @@ __device__ __forceinline__ bool test_c(uint64_t* bars, int c) { return mbar_test
 __device__ __forceinline__ bool wait_c_warp(uint64_t* bars, int c, uint32_t* status, uint32_t code) {
   return __all_sync(0xffffffffu, wait_c(bars, c, status, code));
 }
+
+// Optional phase trace (build with -DTOKMIX_GDN_TRACE): %globaltimer stamps of CTA 0, indexed
+// by event and chunk, read back with tokmix_gdn_trace_read().  Compiled out otherwise.
+#ifdef TOKMIX_GDN_TRACE
+constexpr int kTraceChunks = 64;
+constexpr int kTraceEvents = 24;
+__device__ unsigned long long g_trace[kTraceEvents * kTraceChunks];
+#define GDN_TRACE(ev, c)                                                          \
+  do {                                                                            \
+    if (blockIdx.x == 0 && (c) < kTraceChunks) g_trace[(ev) * kTraceChunks + (c)] = global_timer_ns(); \
+  } while (0)
+#else
+#define GDN_TRACE(ev, c) \
+  do {                   \
+  } while (0)
+#endif
 
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -144,12 +160,12 @@ __device__ __forceinline__ void store_row_sw128(uint8_t* tile, int row, const ui
   store_half_row_sw128(tile, row, 1, *reinterpret_cast<const uint32_t(*)[16]>(&v[16]));
 }
 
-// x = hi + lo with hi = bf16(x), lo = bf16(x - hi): ~16 significant bits in two bf16 operands
+// x = hi + lo as two bf16 operands: hi = x truncated to bf16 (its top 16 bits, exact), lo =
+// the exact fp32 remainder rounded to bf16.  |x - hi - lo| <= 2^-16 |x|.
 __device__ __forceinline__ void split_pack(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-  const __nv_bfloat16 h0 = __float2bfloat16_rn(x0);
-  const __nv_bfloat16 h1 = __float2bfloat16_rn(x1);
-  hi = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
-  lo = pack_bf16x2(x0 - __bfloat162float(h0), x1 - __bfloat162float(h1));
+  const uint32_t b0 = __float_as_uint(x0), b1 = __float_as_uint(x1);
+  hi = __byte_perm(b0, b1, 0x7632);
+  lo = pack_bf16x2(x0 - __uint_as_float(b0 & 0xFFFF0000u), x1 - __uint_as_float(b1 & 0xFFFF0000u));
 }
 
 // Writes 64 fp32 state values (columns [64*half, 64*half+64) of row v) as the hi and lo bf16
@@ -171,11 +187,54 @@ __device__ __forceinline__ void output_pass(const Params& p, uint32_t lane_base,
   const int nv = min(kC, len - cp * kC);
   uint32_t row[64];
   tmem_ld64(lane_base + kColO, row);
+  if (r == 0) GDN_TRACE(20, cp);
   __nv_bfloat16* dst = p.out + (static_cast<size_t>(tok0 + cp * kC) * p.hv + h) * kD + r;
   const size_t tstride = static_cast<size_t>(p.hv) * kD;
 #pragma unroll
   for (int t = 0; t < kC; ++t)
     if (t < nv) dst[t * tstride] = __float2bfloat16_rn(__uint_as_float(row[t]) * p.scale);
+}
+
+// K-major tile of 2 boxes (16 KB apart): descriptor of the 16-element k step kk
+__device__ __forceinline__ uint64_t kmaj_desc(uint32_t base, int kk) {
+  return make_sdesc_sw128(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+}
+
+// T3a  Delta^T += S_hi (-W_hi)^T + S_lo (-W_hi)^T + S_hi (-W_lo)^T   (M=128 v, N=64 t, K=128 k)
+__device__ __forceinline__ void issue_t3a(uint32_t tbase, const uint8_t* smem, int c) {
+  const uint32_t id_sw = make_idesc(128, 64, 1, 0, 1);  // A K-major (S), B MN-major (-W as [k][t])
+  const uint32_t colx = (c & 1) ? kColX1 : kColX0;
+#pragma unroll
+  for (int term = 0; term < 3; ++term) {
+    const uint32_t sa = smem_u32(smem + (term == 1 ? kOffSlo : kOffShi));
+    const uint32_t wa = smem_u32(smem + (term == 2 ? kOffWlo : kOffWhi));
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+      umma_bf16_ss(tbase + colx, kmaj_desc(sa, kk), make_sdesc_sw128(wa + kk * 2048, 16384, 1024), id_sw, 1u);
+  }
+}
+
+// T3b  O^T = S_hi (e^G Q)^T   (M=128 v, N=64 t, K=128 k)
+__device__ __forceinline__ void issue_t3b(uint32_t tbase, const uint8_t* smem, int c) {
+  const uint32_t id = make_idesc(128, 64, 1, 0, 0);
+  const uint32_t sa = smem_u32(smem + kOffShi);
+  const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    umma_bf16_ss(tbase + kColO, kmaj_desc(sa, kk), kmaj_desc(slot, kk), id, kk > 0 ? 1u : 0u);
+}
+
+// T4  S += Delta'_hi^T K + Delta'_lo^T K   (M=128 v, N=128 k, K=64 t; A from TMEM)
+__device__ __forceinline__ void issue_t4(uint32_t tbase, const uint8_t* smem, int c) {
+  const uint32_t id_upd = make_idesc(128, 128, 1, 0, 1);
+  const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
+  const uint32_t colx = (c & 1) ? kColX1 : kColX0;
+#pragma unroll
+  for (int part = 0; part < 2; ++part)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+      umma_bf16_ts(tbase + kColS, tbase + colx + 32 + 32 * part + 8 * kk,
+                   make_sdesc_sw128(slot + 8192 + kk * 2048, 16384, 1024), id_upd, 1u);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -202,17 +261,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const size_t state_off = (static_cast<size_t>(seq) * p.hv + h) * kD * kD;
 
   if (threadIdx.x == 0) {
+    cta_abort_flag() = 0u;
     uint64_t* all = reinterpret_cast<uint64_t*>(&bars);
     for (int i = 0; i < static_cast<int>(sizeof(Barriers) / 8); ++i) mbar_init(&all[i], 1);
     mbar_init(&drain_bar, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars.qk_read[i], 128);
       mbar_init(&bars.g_ready[i], 32);
-      mbar_init(&bars.prep1[i], 128);
+      mbar_init(&bars.prep1[i], 64);
       mbar_init(&bars.wneg[i], 128);
       mbar_init(&bars.da_done[i], 128);
       mbar_init(&bars.s_ready[i], 128);
-      mbar_init(&bars.o_free[i], 128);
       mbar_init(&bars.p_ready[i], 128);
     }
     fence_barrier_init();
@@ -225,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = tmem_base_shared;
+  if (threadIdx.x == 0) GDN_TRACE(19, 0);
 
   if (nchunks == 0) {
     // empty sequence: final state = initial state
@@ -270,9 +330,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int c = 0; ok && c < nchunks; ++c) {
       const ChunkParams& pc = params[c & 1];
       const uint32_t colx = (c & 1) ? kColX1 : kColX0;
+      // --- (one thread) T3a: the state-dependent part of Delta, as soon as S(c) and W(c) exist
+      if (v == 0 && wait_c(bars.s_ready, c, p.status, kDevTimeoutPipe) &&
+          wait_c(bars.wneg, c, p.status, kDevTimeoutPipe)) {
+        tc_fence_after();
+        issue_t3a(tbase, smem, c);
+        umma_commit(&bars.delta[c & 1]);
+        GDN_TRACE(13, c);
+      }
       // --- Delta pass: Delta^T (fp32) -> bf16 Delta, Delta' = e^{G_C - G} Delta as hi + lo
       if (!wait_c_warp(bars.delta, c, p.status, kDevTimeoutMma)) { ok = false; break; }
       tc_fence_after();
+      if (v == 0) GDN_TRACE(0, c);
       {
         uint32_t d[64];
         tmem_ld64(lane_base + colx, d);
@@ -291,9 +360,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&bars.da_done[c & 1]);
+      if (v == 0) GDN_TRACE(1, c);
+      // --- (one thread) T4: the state update
+      if (v == 0 && wait_c(bars.da_done, c, p.status, kDevTimeoutPipe)) {
+        tc_fence_after();
+        issue_t4(tbase, smem, c);
+        umma_commit(&bars.snew[c & 1]);
+        GDN_TRACE(14, c);
+      }
       // --- state pass: S (fp32) -> hi/lo bf16 copies for the next chunk, pre-scale by its decay
+      //     (the copies are overwritten in place: T3b, the other reader, must have completed)
       if (!wait_c_warp(bars.snew, c, p.status, kDevTimeoutMma)) { ok = false; break; }
+      if (!wait_c_warp(bars.t3b, c, p.status, kDevTimeoutMma)) { ok = false; break; }
       tc_fence_after();
+      if (v == 0) GDN_TRACE(2, c);
       const bool last = (c == nchunks - 1);
       float gam = 1.0f;
       if (!last) {
@@ -304,6 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int half = 0; half < 2; ++half) {
         uint32_t sv[64];
         tmem_ld64(lane_base + kColS + half * 64, sv);
+        if (v == 0 && half == 0) GDN_TRACE(21, c);
         if (last) {
           float* dst = p.state_out + state_off + v * kD + half * 64;
 #pragma unroll
@@ -323,6 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bars.s_ready[(c + 1) & 1]);
+        if (v == 0) GDN_TRACE(3, c);
       }
     }
   } else if (warp < 8) {
@@ -366,6 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         mbar_arrive(&bars.g_ready[c & 1]);
+        if (lane == 0) GDN_TRACE(18, c);
       }
       // --- (2a) QK / KK read-out: e^G-scaled Q (in place), L rows -> solve scratch; P row kept
       //          in registers until the P tile is free
@@ -375,9 +458,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ready) { ok = false; break; }
       tc_fence_after();
       uint32_t prow[32];
+      if (r == 0) GDN_TRACE(4, c);
       {
         uint32_t row[64];
         tmem_ld64(lane_base + kColQK, row);
+        if (r == 0) GDN_TRACE(22, c);
         if (r < 64) {
           const int t = r;
           const float gt = pc.g2[t];
@@ -411,21 +496,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int t = r - 64;
           const float gt = pc.g2[t];
           const float bt = pc.beta[t];
-          float* dst = scratch + t * kScStride;
 #pragma unroll
-          for (int s = 0; s < 64; s += 4) {
-            float4 val;
-            val.x = s + 0 < t ? bt * ex2_approx(gt - pc.g2[s + 0]) * __uint_as_float(row[s + 0]) : 0.0f;
-            val.y = s + 1 < t ? bt * ex2_approx(gt - pc.g2[s + 1]) * __uint_as_float(row[s + 1]) : 0.0f;
-            val.z = s + 2 < t ? bt * ex2_approx(gt - pc.g2[s + 2]) * __uint_as_float(row[s + 2]) : 0.0f;
-            val.w = s + 3 < t ? bt * ex2_approx(gt - pc.g2[s + 3]) * __uint_as_float(row[s + 3]) : 0.0f;
-            *reinterpret_cast<float4*>(dst + s) = val;
-          }
+          for (int s = 0; s < 64; ++s)
+            scratch[s * 64 + t] = s < t ? bt * ex2_approx(gt - pc.g2[s]) * __uint_as_float(row[s]) : 0.0f;
         }
       }
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars.qk_read[c & 1]);
+      if (r == 0) GDN_TRACE(5, c);
       // --- (3) W pass: W^T (lane = key row k) -> -W as [k][t], hi and lo bf16 tiles
       ready = wait_c_warp(bars.w_done, c, p.status, kDevTimeoutMma);
       if (ready && c >= 1) ready = wait_c_warp(bars.delta, c - 1, p.status, kDevTimeoutMma);  // W tiles free
@@ -445,111 +524,112 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars.wneg[c & 1]);
+      if (r == 0) GDN_TRACE(6, c);
       // --- (4) output pass of the previous chunk, then the P tile of this chunk (single buffer:
       //         the previous chunk's P V MMA has completed once its output is ready)
       if (c >= 1) {
         if (!wait_c_warp(bars.o_done, c - 1, p.status, kDevTimeoutMma)) { ok = false; break; }
         tc_fence_after();
         output_pass(p, lane_base, tok0, len, c - 1, h, r);
+        if (r == 0) GDN_TRACE(7, c - 1);
         tc_fence_before();
-        mbar_arrive(&bars.o_free[(c - 1) & 1]);
+      }
+      // --- (5) T3b: O^T = S_hi (e^G Q)^T once all 128 threads have read the O region out and
+      //         the state copy of chunk c exists
+      if (!named_sync_and(2, 128, true)) { ok = false; break; }
+      if (r == 0 && wait_c(bars.s_ready, c, p.status, kDevTimeoutPipe)) {
+        tc_fence_after();
+        issue_t3b(tbase, smem, c);
+        umma_commit(&bars.t3b[c & 1]);
+        GDN_TRACE(15, c);
       }
       if (r < 64) store_row_sw128(smem + kOffP, r, prow);
       fence_async_smem();
       mbar_arrive(&bars.p_ready[c & 1]);
+      if (r == 0) GDN_TRACE(8, c);
     }
     if (ok && wait_c_warp(bars.o_done, nchunks - 1, p.status, kDevTimeoutMma)) {
       tc_fence_after();
       output_pass(p, lane_base, tok0, len, nchunks - 1, h, r);
     }
-  } else if (warp < 12) {
-    // =========================================================== blocked triangular solve
-    // scratch[t][s] (t > s) holds L; the unit-lower inverse That[t][s] (t > s) is written
-    // transposed into scratch[s][t].  Diagonal blocks D_i = (I + L_ii)^-1 first, then the
-    // off-diagonal blocks by distance: That_ij = -D_i * sum_{k=j}^{i-1} L_ik That_kj.
+  } else if (warp < 10) {
+    // =========================================================== triangular solve
+    // That = (I + L)^-1, one column per thread (warps 8, 9), by 16-row blocks: for block B the
+    // thread starts from e_j, subtracts the contributions of the already-solved rows
+    // (left-looking, sum_{s < 16B} L[r][s] x_s) and finishes the block by right-looking forward
+    // substitution.  Only 16 accumulators are live; solved rows go to an fp32 column buffer in
+    // shared memory (each thread reads back only its own column).  A warp skips the blocks above
+    // its first column (x = 0 there).  Column j then becomes row j of the MN-major ([s][t]) tiles
+    // T = That diag(beta) and T diag(e^G), each as hi + lo.
     const int tid = threadIdx.x - 256;
-    float* tmp = reinterpret_cast<float*>(smem + kOffSolveTmp);
-    auto Lv = [&](int t, int s) -> float { return scratch[t * kScStride + s]; };
-    auto Tv = [&](int t, int s) -> float {  // That[t][s], any t, s
-      return t == s ? 1.0f : (t > s ? scratch[s * kScStride + t] : 0.0f);
-    };
+    const int j = tid;                 // column
+    const int wfirst = tid & ~31;      // first column of this warp
+    float* xbuf = reinterpret_cast<float*>(smem + kOffTGhi);  // That[r][j] at xbuf[r * 64 + j]
     bool ok = true;
     for (int c = 0; ok && c < nchunks; ++c) {
       const bool ready = wait_c(bars.qk_read, c, p.status, kDevTimeoutPipe);
-      // the four warps leave together or not at all (they meet at named barriers below)
-      if (!named_sync_and(1, 128, ready)) { ok = false; break; }
+      // the two warps leave together or not at all (they meet at named barriers below)
+      if (!named_sync_and(1, 64, ready)) { ok = false; break; }
+      if (tid == 0) GDN_TRACE(9, c);
       const ChunkParams& pc = params[c & 1];
-      // step 1: diagonal 16x16 blocks, one column per thread (threads 0..63)
-      if (tid < 64) {
-        const int blk = tid >> 4, col = tid & 15, o = blk * 16;
-        float x[16];
 #pragma unroll
-        for (int rr = 0; rr < 16; ++rr) {
-          if (rr < col) {
-            x[rr] = 0.0f;
-          } else if (rr == col) {
-            x[rr] = 1.0f;
-          } else {
-            float acc = 0.0f;
+      for (int B = 0; B < 4; ++B) {
+        float acc[16];
 #pragma unroll
-            for (int s = 0; s < rr; ++s) acc = fmaf(Lv(o + rr, o + s), x[s], acc);
-            x[rr] = -acc;
+        for (int i = 0; i < 16; ++i) acc[i] = (16 * B + i == j) ? 1.0f : 0.0f;
+        if (16 * B + 15 >= wfirst) {  // warp-uniform
+          // left-looking: rows of the previous blocks (x_s = 0 for s < j)
+#pragma unroll 2
+          for (int s0 = wfirst; s0 < 16 * B; ++s0) {
+            const float xs = xbuf[s0 * 64 + j];
+            const float4* lc = reinterpret_cast<const float4*>(scratch + s0 * 64 + 16 * B);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float4 l = lc[q];
+              acc[4 * q + 0] = fmaf(-l.x, xs, acc[4 * q + 0]);
+              acc[4 * q + 1] = fmaf(-l.y, xs, acc[4 * q + 1]);
+              acc[4 * q + 2] = fmaf(-l.z, xs, acc[4 * q + 2]);
+              acc[4 * q + 3] = fmaf(-l.w, xs, acc[4 * q + 3]);
+            }
+          }
+          // right-looking inside the block (L[r][t] = 0 for r <= t)
+#pragma unroll
+          for (int tt = 0; tt < 15; ++tt) {
+            const float xt = acc[tt];
+            const float* lc = scratch + (16 * B + tt) * 64 + 16 * B;
+#pragma unroll
+            for (int i4 = (tt + 1) & ~3; i4 < 16; i4 += 4) {
+              const float4 l = *reinterpret_cast<const float4*>(lc + i4);
+              acc[i4 + 0] = fmaf(-l.x, xt, acc[i4 + 0]);
+              acc[i4 + 1] = fmaf(-l.y, xt, acc[i4 + 1]);
+              acc[i4 + 2] = fmaf(-l.z, xt, acc[i4 + 2]);
+              acc[i4 + 3] = fmaf(-l.w, xt, acc[i4 + 3]);
+            }
           }
         }
 #pragma unroll
-        for (int rr = 0; rr < 16; ++rr)
-          if (rr > col) scratch[(o + col) * kScStride + o + rr] = x[rr];
+        for (int i = 0; i < 16; ++i) xbuf[(16 * B + i) * 64 + j] = acc[i];
       }
-      named_sync(1, 128);
-      // steps 2-4: block distance 1, 2, 3
-#pragma unroll 1
-      for (int dist = 1; dist <= 3; ++dist) {
-        const int nelem = (4 - dist) * 256;  // blocks (i, j = i - dist), i = dist..3
-        // X = sum_{k=j}^{i-1} L_ik That_kj   (16x16 each)
-        for (int e = tid; e < nelem; e += 128) {
-          const int bi = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
-          const int i = dist + bi, j = i - dist;
-          float acc = 0.0f;
-          for (int kb = j; kb < i; ++kb) {
+      float x[64];
 #pragma unroll
-            for (int s = 0; s < 16; ++s) acc = fmaf(Lv(16 * i + rr, 16 * kb + s), Tv(16 * kb + s, 16 * j + cc), acc);
-          }
-          tmp[e] = acc;
-        }
-        named_sync(1, 128);
-        // That_ij = -D_i X
-        for (int e = tid; e < nelem; e += 128) {
-          const int bi = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
-          const int i = dist + bi, j = i - dist;
-          float acc = tmp[e];  // D_i has a unit diagonal
+      for (int r = 0; r < 64; ++r) x[r] = xbuf[r * 64 + j];
+      named_sync(1, 64);  // L and every column are in registers: the tiles may overwrite both
+      const float w0 = pc.beta[j];
+      const float w1 = w0 * pc.eg[j];
 #pragma unroll
-          for (int s = 0; s < 16; ++s)
-            if (s < rr) acc = fmaf(scratch[(16 * i + s) * kScStride + 16 * i + rr], tmp[(bi << 8) + (s << 4) + cc], acc);
-          scratch[(16 * j + cc) * kScStride + 16 * i + rr] = -acc;
-        }
-        named_sync(1, 128);
-      }
-      // step 5: T = That diag(beta) and T diag(beta e^G), each as hi + lo bf16 [t][s] tiles.
-      // Rows are computed into registers first: the tiles overwrite the scratch.
-      {
-        const int t = tid & 63;
-        const bool with_decay = tid >= 64;
-        uint32_t a[32], b[32];
+      for (int q = 0; q < 2; ++q) {  // q = 0: T, q = 1: T diag(e^G)
+        const float w = q ? w1 : w0;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int s0 = 2 * j, s1 = 2 * j + 1;
-          float w0 = pc.beta[s0], w1 = pc.beta[s1];
-          if (with_decay) {
-            w0 *= pc.eg[s0];
-            w1 *= pc.eg[s1];
-          }
-          split_pack(Tv(t, s0) * w0, Tv(t, s1) * w1, a[j], b[j]);
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) split_pack(x[32 * hf + 2 * i] * w, x[32 * hf + 2 * i + 1] * w, hi[i], lo[i]);
+          store_half_row_sw128(smem + (q ? kOffTGhi : kOffThi), j, hf, hi);
+          store_half_row_sw128(smem + (q ? kOffTGlo : kOffTlo), j, hf, lo);
         }
-        named_sync(1, 128);
-        store_row_sw128(smem + (with_decay ? kOffTGhi : kOffThi), t, a);
-        store_row_sw128(smem + (with_decay ? kOffTGlo : kOffTlo), t, b);
       }
       fence_async_smem();
+      if (tid == 0) GDN_TRACE(10, c);
       mbar_arrive(&bars.prep1[c & 1]);
     }
   } else if (warp == kWarpTma) {
@@ -561,9 +641,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       for (int c = 0; c < nchunks; ++c) {
         const int row = tok0 + c * kC;
-        if (c >= 2 && !wait_c(bars.slot_free, c - 2, p.status, kDevTimeoutPipe)) break;
+        // the slot of chunk c-2 is free once its state pass ran: T1-T4 and T3b have completed
+        if (c >= 2 && !wait_c(bars.s_ready, c - 1, p.status, kDevTimeoutPipe)) break;
         uint8_t* slot = smem + ((c & 1) ? kOffSlot1 : kOffSlot0);
         mbar_arrive_expect_tx(&bars.in_full[c & 1], kSlotBytes);
+        GDN_TRACE(17, c);
         for (int bx = 0; bx < 2; ++bx) {
           tma_load_3d(slot + bx * 16384, &map_q, &bars.in_full[c & 1], bx * 64, kh, row);
           tma_load_3d(slot + bx * 16384 + 8192, &map_k, &bars.in_full[c & 1], bx * 64, kh, row);
@@ -576,95 +658,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // before the CTA retires, let the last loads land (bounded; a no-op on the normal path)
       for (int c = max(0, issued - 2); c < issued; ++c) {
-        wait_c(bars.in_full, c, nullptr, 0);
-        wait_c(bars.v_full, c, nullptr, 0);
+        mbar_drain(&bars.in_full[c & 1], (c >> 1) & 1);
+        mbar_drain(&bars.v_full[c & 1], (c >> 1) & 1);
       }
     }
   } else {
     // =========================================================== MMA issuer (polling)
-    // Groups per chunk c, issued in dependency order, critical path first:
-    //   T1  [Q;K] K^T                                   -> QK region          (state-independent)
-    //   T2  W^T = K^T (TG_hi + TG_lo)^T ; Delta^T = V^T (T_hi + T_lo)^T        (state-independent)
-    //   T3a Delta^T += S_hi (-W_hi)^T + S_lo (-W_hi)^T + S_hi (-W_lo)^T        (critical)
-    //   T3b O^T = S_hi (e^G Q)^T
-    //   T4  S += Delta'_hi^T K + Delta'_lo^T K                                  (critical)
+    // Groups per chunk c (the state-dependent groups T3a/T4 are issued by the state-chain warps,
+    // T3b by the operand warps):
+    //   T1  [Q;K] K^T                                                   -> QK region
+    //   T2  W^T = K^T (TG_hi + TG_lo)^T ; Delta^T = V^T (T_hi + T_lo)^T  -> W region, X slot
     //   T5  O^T += Delta^T P^T
+    // This thread polls the hand-off barriers (non-blocking) and issues whichever group is ready.
     if (lane == 0 && nchunks > 0) {
       const uint32_t id_qk = make_idesc(128, 64, 1, 0, 0);    // [Q;K] K^T
-      const uint32_t id_mnk = make_idesc(128, 64, 1, 1, 0);   // A MN-major (K^T, V^T), B K-major
-      const uint32_t id_sw = make_idesc(128, 64, 1, 0, 1);    // A K-major (S), B MN-major (-W as [k][t])
-      const uint32_t id_upd = make_idesc(128, 128, 1, 0, 1);  // A TMEM, B MN-major (K as [t][k])
-      const uint32_t id_kk = make_idesc(128, 64, 1, 0, 0);    // both K-major / A TMEM
+      const uint32_t id_mnmn = make_idesc(128, 64, 1, 1, 1);  // A MN-major (K^T, V^T), B MN-major (T tiles [s][t])
+      const uint32_t id_dp = make_idesc(128, 64, 1, 0, 0);    // A TMEM, B K-major (P [t][s])
       const uint32_t a_thi = smem_u32(smem + kOffThi), a_tlo = smem_u32(smem + kOffTlo);
       const uint32_t a_tghi = smem_u32(smem + kOffTGhi), a_tglo = smem_u32(smem + kOffTGlo);
       const uint32_t a_v = smem_u32(smem + kOffV), a_p = smem_u32(smem + kOffP);
-      const uint32_t a_whi = smem_u32(smem + kOffWhi), a_wlo = smem_u32(smem + kOffWlo);
-      const uint32_t a_shi = smem_u32(smem + kOffShi), a_slo = smem_u32(smem + kOffSlo);
-      auto kmaj = [](uint32_t base, int kk) {  // K-major tile of 2 boxes (16 KB apart), 16-element k step
-        return make_sdesc_sw128(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-      };
-      int n1 = 0, n2 = 0, n3a = 0, n3b = 0, n4 = 0, n5 = 0;
+      int n1 = 0, n2 = 0, n5 = 0;
       const int N = nchunks;
       unsigned long long idle_since = 0;
       uint32_t idle_polls = 0;
       while (n5 < N) {
         bool issued = false;
-        if (n4 < n3b && test_c(bars.da_done, n4)) {
-          // T4: S += Delta'_hi^T K + Delta'_lo^T K
-          const int c = n4;
-          tc_fence_after();
-          const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
-          const uint32_t colx = (c & 1) ? kColX1 : kColX0;
-#pragma unroll
-          for (int part = 0; part < 2; ++part)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16_ts(tbase + kColS, tbase + colx + 32 + 32 * part + 8 * kk,
-                           make_sdesc_sw128(slot + 8192 + kk * 2048, 16384, 1024), id_upd, 1u);
-          umma_commit(&bars.snew[c & 1]);
-          ++n4;
-          issued = true;
-        } else if (n3a < n2 && n3a == n4 && test_c(bars.wneg, n3a) && test_c(bars.s_ready, n3a)) {
-          // T3a: Delta^T += S_hi (-W_hi)^T + S_lo (-W_hi)^T + S_hi (-W_lo)^T
-          const int c = n3a;
-          tc_fence_after();
-          const uint32_t colx = (c & 1) ? kColX1 : kColX0;
-#pragma unroll
-          for (int term = 0; term < 3; ++term) {
-            const uint32_t sa = term == 1 ? a_slo : a_shi;
-            const uint32_t wa = term == 2 ? a_wlo : a_whi;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_bf16_ss(tbase + colx, kmaj(sa, kk), make_sdesc_sw128(wa + kk * 2048, 16384, 1024), id_sw, 1u);
-          }
-          umma_commit(&bars.delta[c & 1]);
-          ++n3a;
-          issued = true;
-        } else if (n3b < n3a && (n3b == 0 || test_c(bars.o_free, n3b - 1))) {
-          // T3b: O^T = S_hi (e^G Q)^T
-          const int c = n3b;
-          tc_fence_after();
-          const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_bf16_ss(tbase + kColO, kmaj(a_shi, kk), kmaj(slot, kk), id_kk, kk > 0 ? 1u : 0u);
-          ++n3b;
-          issued = true;
-        } else if (n5 < n4 && test_c(bars.p_ready, n5)) {
+        if (n5 < n2 && test_c(bars.t3b, n5) && test_c(bars.da_done, n5) && test_c(bars.p_ready, n5)) {
           // T5: O^T += Delta^T P^T
           const int c = n5;
           tc_fence_after();
           const uint32_t colx = (c & 1) ? kColX1 : kColX0;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16_ts(tbase + kColO, tbase + colx + 8 * kk, make_sdesc_sw128(a_p + kk * 32, 16, 1024), id_kk, 1u);
+            umma_bf16_ts(tbase + kColO, tbase + colx + 8 * kk, make_sdesc_sw128(a_p + kk * 32, 16, 1024), id_dp, 1u);
           umma_commit(&bars.o_done[c & 1]);
-          umma_commit(&bars.slot_free[c & 1]);
+          GDN_TRACE(16, c);
           ++n5;
           issued = true;
         } else if (n2 < n1 && n2 < n5 + 2 && test_c(bars.prep1, n2) && test_c(bars.v_full, n2) &&
-                   (n2 == 0 || test_c(bars.wneg, n2 - 1))) {
+                   (n2 == 0 || test_c(bars.wneg, n2 - 1)) && (n2 < 2 || test_c(bars.snew, n2 - 2))) {
           // T2: W^T = K^T (TG_hi + TG_lo)^T ; Delta^T = V^T T_hi^T + V^T T_lo^T
+          // (the X slot of chunk c was last read by T4(c-2) and T5(c-2))
           const int c = n2;
           tc_fence_after();
           const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
@@ -674,48 +708,53 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               umma_bf16_ss(tbase + kColW, make_sdesc_sw128(slot + 8192 + kk * 2048, 16384, 1024),
-                           make_sdesc_sw128((part ? a_tglo : a_tghi) + kk * 32, 16, 1024), id_mnk,
+                           make_sdesc_sw128((part ? a_tglo : a_tghi) + kk * 2048, 16384, 1024), id_mnmn,
                            (part > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int part = 0; part < 2; ++part)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               umma_bf16_ss(tbase + colx, make_sdesc_sw128(a_v + kk * 2048, 8192, 1024),
-                           make_sdesc_sw128((part ? a_tlo : a_thi) + kk * 32, 16, 1024), id_mnk,
+                           make_sdesc_sw128((part ? a_tlo : a_thi) + kk * 2048, 16384, 1024), id_mnmn,
                            (part > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&bars.w_done[c & 1]);
           umma_commit(&bars.v_free[c & 1]);
+          GDN_TRACE(12, c);
           ++n2;
           issued = true;
-        } else if (n1 < N && n1 <= n2 + 1 && n1 < n5 + 2 && test_c(bars.in_full, n1) &&
-                   (n1 == 0 || test_c(bars.qk_read, n1 - 1))) {
+        } else if (n1 < N && n1 <= n2 + 1 && test_c(bars.in_full, n1) && (n1 == 0 || test_c(bars.qk_read, n1 - 1))) {
           // T1: [Q;K] K^T
           const int c = n1;
           tc_fence_after();
           const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_bf16_ss(tbase + kColQK, kmaj(slot, kk), kmaj(slot + 8192, kk), id_qk, kk > 0 ? 1u : 0u);
+            umma_bf16_ss(tbase + kColQK, kmaj_desc(slot, kk), kmaj_desc(slot + 8192, kk), id_qk, kk > 0 ? 1u : 0u);
           umma_commit(&bars.qk_done[c & 1]);
+          GDN_TRACE(11, c);
           ++n1;
           issued = true;
         }
         if (issued) {
           idle_polls = 0;
-        } else if ((++idle_polls & 255u) == 0u) {
+        } else if ((++idle_polls & 255u) != 0u) {
+          __nanosleep(32);  // leave issue slots and shared-memory bandwidth to the other warps
+        } else {
           // every 256 empty polls: give up after kWaitTimeoutNs without progress, or as soon as
           // another warp of the CTA has reported a timeout
           const unsigned long long now = global_timer_ns();
           if (idle_polls == 256u) idle_since = now;
-          if (now - idle_since > kWaitTimeoutNs || *reinterpret_cast<volatile uint32_t*>(p.status) != 0u) {
+          if (cta_abort_flag() != 0u) break;
+          if (now - idle_since > kWaitTimeoutNs) {
             record_status(p.status, kDevTimeoutPipe);
+            cta_abort_flag() = 1u;
             break;
           }
         }
       }
       // every MMA issued by this thread completes before TMEM is released (bounded)
       umma_commit(&drain_bar);
-      mbar_wait(&drain_bar, 0, nullptr, 0);
+      mbar_drain(&drain_bar, 0);
     }
     __syncwarp();
   }
@@ -797,3 +836,11 @@ extern "C" int tokmix_gdn_prefill(const void* q, const void* k, const void* v, c
       mq, mk, mv, p);
   return check_launch("tokmix_gdn_prefill");
 }
+
+#ifdef TOKMIX_GDN_TRACE
+extern "C" int tokmix_gdn_trace_read(unsigned long long* host, int n) {
+  using namespace tokmix::gdn;
+  const int count = n < kTraceEvents * kTraceChunks ? n : kTraceEvents * kTraceChunks;
+  return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * count) == cudaSuccess ? count : -1;
+}
+#endif

@@ -96,23 +96,52 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// Blocking test with a suspend-time hint: the thread sleeps in hardware until the phase
+// completes or `hint_ns` passes, so waiting warps take no issue slots or shared-memory bandwidth.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
+// CTA-wide abort flag in shared memory: set by the first wait that runs out, checked by every
+// other wait so the whole CTA drains quickly.  Kernels zero it before their first barrier.
+__device__ __forceinline__ volatile uint32_t& cta_abort_flag() {
+  __shared__ uint32_t flag;
+  return *reinterpret_cast<volatile uint32_t*>(&flag);
+}
+
 // Wait until the phase with the given parity has completed.  Gives up after kWaitTimeoutNs,
-// records `code` in *status and returns false.  Once *status is non-zero (another warp gave up)
-// the wait returns false as soon as it notices, so a failing CTA drains quickly.
+// records `code` in *status (device memory, may be null), raises the CTA abort flag and returns
+// false; returns false at once if another warp of the CTA has already given up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t code) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
-  uint32_t spins = 0;
   while (true) {
-    if (mbar_try(bar, parity)) return true;
-    if ((++spins & 63u) == 0u) {
-      if (status != nullptr && *reinterpret_cast<volatile uint32_t*>(status) != 0u) return false;
-      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
-        record_status(status, code);
-        return false;
-      }
+    if (mbar_try_sleep(bar, parity, 100000u)) return true;
+    if (cta_abort_flag() != 0u) return false;
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      record_status(status, code);
+      cta_abort_flag() = 1u;
+      return false;
     }
   }
+}
+
+// Bounded wait that ignores the abort flag: used before a CTA retires, to let its own TMA loads
+// and MMAs land before shared memory and TMEM are released.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = global_timer_ns();
+  while (!mbar_try_sleep(bar, parity, 100000u)) {
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+  }
+  return true;
 }
 
 // ------------------------------------------------------------------------------------------
