@@ -89,6 +89,23 @@ int tokmix_gdn_prefill(const void* q, const void* k, const void* v, const float*
                        const int32_t* seq_order_dev, int num_seqs, int total_tokens, int heads_k, int heads_v,
                        int head_dim_k, int head_dim_v, float scale, int io_dtype, uint32_t* status, void* stream);
 
+/* Gated-delta-rule prefill for a batch of equal-length sequences that allocates nothing.
+ *
+ * For callers that cannot allocate device memory while they run an op (graph executors that
+ * plan every buffer in advance, C / FFI callers without a device allocator).  Same maths and
+ * arguments as tokmix_gdn_prefill with batched layout q, k [batch, seqlen, heads_k, 128],
+ * v, out [batch, seqlen, heads_v, 128], g, beta [batch, seqlen, heads_v], states
+ * [batch, heads_v, 128, 128]; the per-sequence token offsets (and the device status word when
+ * `status` is NULL) live in a library-owned device array of about 16 KB per device instead of
+ * caller memory.  batch must be <= 4095.  The first call on a device looks up that array's
+ * address on the current device; make it before capturing the stream into a CUDA graph.  All
+ * calls on a device share the array: calls that may overlap on the GPU (different streams
+ * without ordering) race on it.  No counterpart in the reference. */
+int tokmix_gdn_prefill_noalloc(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                               const float* initial_state, void* out, float* final_state, int batch, int seqlen,
+                               int heads_k, int heads_v, int head_dim_k, int head_dim_v, float scale, int io_dtype,
+                               uint32_t* status, void* stream);
+
 /* Text of the last error reported on the calling thread ("" if none). */
 const char* tokmix_last_error(void);
 

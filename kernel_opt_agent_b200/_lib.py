@@ -44,6 +44,8 @@ SIGNATURES = {
     "tokmix_fa2_fwd": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _F, _VP, _VP]),
     "tokmix_gdn_prefill": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _F, _I, _VP,
                                 _VP]),
+    "tokmix_gdn_prefill_noalloc": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _F, _I, _VP,
+                                        _VP]),
     "tokmix_last_error": (ctypes.c_char_p, []),
     "tokmix_version": (ctypes.c_char_p, []),
 }

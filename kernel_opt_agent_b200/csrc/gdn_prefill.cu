@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <mutex>
 
 #include "host_common.h"
 #include "sm100.cuh"
@@ -844,3 +845,73 @@ extern "C" int tokmix_gdn_trace_read(unsigned long long* host, int n) {
   return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * count) == cudaSuccess ? count : -1;
 }
 #endif
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free entry point for equal-length batches.
+//
+// Some callers cannot allocate device memory when they run an op: a graph executor that plans
+// every buffer ahead of time (the llama.cpp-style backends the reference's fp32 GDN interface is
+// written for), or C / FFI callers without a device allocator.  They can hand us their inputs
+// and outputs, but not the small scratch the kernel needs (the per-sequence token offsets and
+// the device status word).  This entry point keeps that scratch in a file-scope device array.
+namespace tokmix {
+namespace gdn {
+namespace noalloc {
+
+constexpr int kMaxSeqs = 4095;  // largest batch this entry point accepts
+// [0, 64): status word (word 0) + padding; [64, 64 + kMaxSeqs + 1): token offsets of the batch
+static __device__ __align__(256) int32_t g_scratch[64 + kMaxSeqs + 1];
+
+__global__ void fill_offsets(int32_t* offsets, int batch, int seqlen, uint32_t* status_to_clear) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i <= batch) offsets[i] = i * seqlen;
+  if (i == 0 && status_to_clear != nullptr) *status_to_clear = 0u;
+}
+
+std::mutex g_mu;
+int32_t* g_base[64] = {};  // device address of g_scratch, per device (set up once)
+
+}  // namespace noalloc
+}  // namespace gdn
+}  // namespace tokmix
+
+extern "C" int tokmix_gdn_prefill_noalloc(const void* q, const void* k, const void* v, const float* g,
+                                          const float* beta, const float* initial_state, void* out,
+                                          float* final_state, int batch, int seqlen, int heads_k, int heads_v,
+                                          int head_dim_k, int head_dim_v, float scale, int io_dtype,
+                                          uint32_t* status, void* stream) {
+  using namespace tokmix;
+  namespace na = tokmix::gdn::noalloc;
+  if (batch < 0 || seqlen < 0) return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_noalloc: negative size");
+  if (batch > na::kMaxSeqs)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_noalloc: batch %d exceeds the maximum of %d",
+                batch, na::kMaxSeqs);
+  if (static_cast<long long>(batch) * seqlen > 0x7FFFFFFFll)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_noalloc: batch * seqlen exceeds 2^31 - 1");
+  if (batch == 0) return TOKMIX_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(TOKMIX_ERR_DEVICE, "tokmix_gdn_prefill_noalloc: no usable current device");
+  int32_t* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(na::g_mu);
+    if (na::g_base[dev] == nullptr) {
+      // set-up, once per device, with that device current: the host-side symbol is only a
+      // stand-in, the kernels need the device address of this device's copy of the array
+      void* ptr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&ptr, na::g_scratch);
+      if (e != cudaSuccess)
+        return fail(TOKMIX_ERR_DEVICE, "tokmix_gdn_prefill_noalloc: cudaGetSymbolAddress failed: %s",
+                    cudaGetErrorString(e));
+      na::g_base[dev] = static_cast<int32_t*>(ptr);
+    }
+    base = na::g_base[dev];
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t* st = status != nullptr ? status : reinterpret_cast<uint32_t*>(base);
+  int32_t* offsets = base + 64;
+  na::fill_offsets<<<(batch + 1 + 255) / 256, 256, 0, s>>>(offsets, batch, seqlen, status != nullptr ? nullptr : st);
+  if (const int rc = check_launch("tokmix_gdn_prefill_noalloc")) return rc;
+  return tokmix_gdn_prefill(q, k, v, g, beta, initial_state, out, final_state, offsets, nullptr, batch, batch * seqlen,
+                            heads_k, heads_v, head_dim_k, head_dim_v, scale, io_dtype, st, stream);
+}
