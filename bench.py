@@ -39,6 +39,7 @@ sys.path.insert(0, ROOT)
 
 from kernel_opt_agent_b200 import flash_attention_2 as fa2  # noqa: E402
 from kernel_opt_agent_b200 import qwen35moe_gdn_prefill as gdn  # noqa: E402
+from kernel_opt_agent_b200 import sharding  # noqa: E402
 
 L2_BYTES = 126 * 1024 * 1024
 D = 128
@@ -59,7 +60,7 @@ def measured_peaks() -> dict:
 
 
 # ----------------------------------------------------------------------------- input generation
-def gdn_inputs(device, tokens_per_seq, seed, lengths=None, state_std=0.0, hk=HK, hv=HV, head_slice=None):
+def gdn_inputs(device, tokens_per_seq, seed, lengths=None, state_std=0.0, hk=HK, hv=HV):
     """GDN workload drawn on the device from a seeded generator (q, k L2-normalised, v ~ N(0,1),
     g = -softplus(N(0,1)), beta = sigmoid(N(0,1)))."""
     gen = torch.Generator(device=device).manual_seed(seed)
@@ -74,15 +75,6 @@ def gdn_inputs(device, tokens_per_seq, seed, lengths=None, state_std=0.0, hk=HK,
     beta = torch.sigmoid(torch.randn(1, T, hv, device=device, generator=gen))
     state = torch.randn(nseq, hv, D, D, device=device, generator=gen) * state_std
     inp = {"q": q, "k": k, "v": v, "g": g, "beta": beta, "state": state, "scale": D ** -0.5}
-    if head_slice is not None:
-        # key heads [a, b) and the value heads that read them (h % hk in [a, b)), kept in an order
-        # where local value head i reads local key head i % (b - a)
-        a, b = head_slice
-        vh = [h for r in range(hv // hk) for h in range(r * hk + a, r * hk + b)]
-        inp["q"], inp["k"] = inp["q"][:, :, a:b].contiguous(), inp["k"][:, :, a:b].contiguous()
-        for key in ("v", "g", "beta"):
-            inp[key] = inp[key][:, :, vh].contiguous()
-        inp["state"] = inp["state"][:, vh].contiguous()
     if lengths is not None:
         cu = [0]
         for n in lengths:
@@ -96,16 +88,13 @@ def varlen_lengths(n=8, lo=1024, hi=32768, seed=0):
     return [int(x) for x in torch.randint(lo, hi + 1, (n,), generator=gen)]
 
 
-def fa2_inputs(device, batch, hq, hkv, s, d, seed, kv_slice=None):
+def fa2_inputs(device, batch, hq, hkv, s, d, seed):
+    """q, k, v ~ N(0,1) drawn on the device from a seeded generator (same values on every rank)."""
     gen = torch.Generator(device=device).manual_seed(seed)
-    a, b = kv_slice if kv_slice is not None else (0, hkv)
-    group = hq // hkv
-    # draw the full tensors (same values on every rank), keep this rank's head slice
-    q = torch.randn(batch, hq, s, d, device=device, generator=gen, dtype=torch.bfloat16)[:, a * group:b * group]
-    k = torch.randn(batch, hkv, s, d, device=device, generator=gen, dtype=torch.bfloat16)[:, a:b]
-    v = torch.randn(batch, hkv, s, d, device=device, generator=gen, dtype=torch.bfloat16)[:, a:b]
-    return {"q": q.contiguous(), "k": k.contiguous(), "v": v.contiguous(), "causal": True,
-            "sm_scale": 1.0 / math.sqrt(d)}
+    q = torch.randn(batch, hq, s, d, device=device, generator=gen, dtype=torch.bfloat16)
+    k = torch.randn(batch, hkv, s, d, device=device, generator=gen, dtype=torch.bfloat16)
+    v = torch.randn(batch, hkv, s, d, device=device, generator=gen, dtype=torch.bfloat16)
+    return {"q": q, "k": k, "v": v, "causal": True, "sm_scale": 1.0 / math.sqrt(d)}
 
 
 def input_bytes(inp) -> int:
@@ -219,37 +208,61 @@ def headline_config(world: int) -> dict:
 HEADLINE_METRIC = "GDN prefill Mtok/s"
 
 
-def run_gdn_varlen(device, rank, world, steps, warmup):
+def run_gdn_varlen(device, rank, world, steps, warmup, verify=False):
     lengths = varlen_lengths()
-    per_rank = HK // world
-    a, b = rank * per_rank, (rank + 1) * per_rank
-    inp = gdn_inputs(device, 0, seed=7, lengths=lengths, state_std=0.02, head_slice=(a, b))
+    full = gdn_inputs(device, 0, seed=7, lengths=lengths, state_std=0.02)
+    ranges = sharding.even_ranges(HK, world)
+    a, b = ranges[rank]
+    inp = sharding.slice_gdn_inputs(full, a, b)
+    if not verify:
+        del full
     tokens = sum(lengths)
     total_s, per = time_steps(lambda: gdn.kernel_fn(**inp), steps, warmup, device,
                               flush=input_bytes(inp) < L2_BYTES)
     gdn.check_device_status(device)
     algo = gdn.algorithmic_bytes(tokens, len(lengths), hk=b - a, hv=2 * (b - a))
-    return {"tokens_per_step": tokens, "ms": total_s / steps * 1e3, "value": tokens * steps / total_s / 1e6,
-            "unit": "Mtok/s", "kernel_ms_local": statistics.mean(per), "algo_bytes": algo,
-            "config": {"workload": "gdn_varlen", "n_seqs": 8, "lengths": lengths, "total_tokens": tokens,
-                       "hk": HK, "hv": HV, "head_dim": D, "chunk": 64, "initial_state": "N(0,0.02)",
-                       "shard": f"key heads {HK // world}/rank"}}
+    res = {"tokens_per_step": tokens, "ms": total_s / steps * 1e3, "value": tokens * steps / total_s / 1e6,
+           "unit": "Mtok/s", "kernel_ms_local": statistics.mean(per), "algo_bytes": algo,
+           "config": {"workload": "gdn_varlen", "n_seqs": 8, "lengths": lengths, "total_tokens": tokens,
+                      "hk": HK, "hv": HV, "head_dim": D, "chunk": 64, "initial_state": "N(0,0.02)",
+                      "shard": f"key heads {HK // world}/rank (+ the value heads reading them)"}}
+    if verify and world > 1:
+        out, fs = gdn.kernel_fn(**inp)
+        go = sharding.gather_to_rank0(out, dim=2)
+        gs = sharding.gather_to_rank0(fs, dim=1)
+        if rank == 0:
+            ref_o, ref_s = gdn.kernel_fn(**full)
+            sizes = [2 * (y - x) for x, y in ranges]
+            offs = [sum(sizes[:i]) for i in range(world)]
+            o = sharding.unscatter_gdn_heads([go.narrow(2, o0, n) for o0, n in zip(offs, sizes)], ranges, HK, HV, 2)
+            st = sharding.unscatter_gdn_heads([gs.narrow(1, o0, n) for o0, n in zip(offs, sizes)], ranges, HK, HV, 1)
+            res["verified_vs_one_gpu"] = bool(torch.equal(o, ref_o) and torch.equal(st, ref_s))
+    return res
 
 
-def run_fa2(device, rank, world, steps, warmup, batch=4):
+def run_fa2(device, rank, world, steps, warmup, batch=4, verify=False):
     B, HQ, HKV, S, DD = batch, 32, 8, 8192, 128
-    per_rank = HKV // world
-    a, b = rank * per_rank, (rank + 1) * per_rank
-    inp = fa2_inputs(device, B, HQ, HKV, S, DD, seed=3, kv_slice=(a, b))
+    ranges = sharding.even_ranges(HKV, world)
+    a, b = ranges[rank]
+    full = fa2_inputs(device, B, HQ, HKV, S, DD, seed=3)
+    inp = sharding.slice_fa2_inputs(full, a, b)
+    if not verify:
+        del full
     flops_total = fa2.get_flops(B, HQ, S, DD, causal=True)
     total_s, per = time_steps(lambda: fa2.kernel_fn(**inp), steps, warmup, device,
                               flush=input_bytes(inp) < L2_BYTES)
     fa2.check_device_status(device)
     local_flops = fa2.get_flops(B, (b - a) * (HQ // HKV), S, DD, causal=True)
-    return {"ms": total_s / steps * 1e3, "value": flops_total * steps / total_s / 1e12, "unit": "TFLOP/s",
-            "kernel_ms_local": statistics.mean(per), "local_flops": local_flops,
-            "config": {"workload": f"fa2_b{B}_s8192", "batch": B, "heads_q": HQ, "heads_kv": HKV, "seq_len": S,
-                       "head_dim": DD, "causal": True, "layout": "bhsd", "shard": f"kv heads {per_rank}/rank"}}
+    res = {"ms": total_s / steps * 1e3, "value": flops_total * steps / total_s / 1e12, "unit": "TFLOP/s",
+           "kernel_ms_local": statistics.mean(per), "local_flops": local_flops,
+           "config": {"workload": f"fa2_b{B}_s8192", "batch": B, "heads_q": HQ, "heads_kv": HKV, "seq_len": S,
+                      "head_dim": DD, "causal": True, "layout": "bhsd",
+                      "shard": f"kv heads {HKV // world}/rank (+ their query heads)"}}
+    if verify and world > 1:
+        got = sharding.gather_to_rank0(fa2.kernel_fn(**inp), dim=1)
+        if rank == 0:
+            res["verified_vs_one_gpu"] = bool(torch.equal(got, fa2.kernel_fn(**full)))
+    return res
 
 
 def e2e_gdn_b1(device, rank, world, steps, warmup, inp):
@@ -332,6 +345,8 @@ def main():
                     choices=["gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_b4_t2048", "fa2_b1_s8192"],
                     help="gdn_b4_t2048 / fa2_b1_s8192 are profiling-size cases (inputs just above L2)")
     ap.add_argument("--no-also", action="store_true", help="skip the secondary workloads")
+    ap.add_argument("--no-verify", action="store_true",
+                    help="with N > 1, skip gathering the sharded outputs to rank 0 for comparison with a one-GPU run")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -369,9 +384,10 @@ def main():
                 "workload": w, "batch_per_rank": 4, "seq_len": 2048, "hk": HK, "hv": HV, "head_dim": D}
             del inp
         elif w in ("fa2_b4_s8192", "fa2_b1_s8192"):
-            r = run_fa2(device, rank, world, steps_w, args.warmup, batch=4 if w == "fa2_b4_s8192" else 1)
+            r = run_fa2(device, rank, world, steps_w, args.warmup, batch=4 if w == "fa2_b4_s8192" else 1,
+                        verify=not args.no_verify)
         else:
-            r = run_gdn_varlen(device, rank, world, steps_w, args.warmup)
+            r = run_gdn_varlen(device, rank, world, steps_w, args.warmup, verify=not args.no_verify)
         results[w] = r
         torch.cuda.empty_cache()
     clocks = sampler.stop() if sampler else None
@@ -410,7 +426,9 @@ def main():
                 "e2e": e2e if e2e is not None else None,
                 "gpu_launches": args.steps, "clocks": clocks,
                 "also": {w: {"value": r["value"], "unit": r["unit"], "ms_per_step": r["ms"],
-                             "roofline": roofline(w, r), **({"config": r["config"]} if "config" in r else {})}
+                             "roofline": roofline(w, r), **({"config": r["config"]} if "config" in r else {}),
+                             **({"verified_vs_one_gpu": r["verified_vs_one_gpu"]}
+                                if "verified_vs_one_gpu" in r else {})}
                          for w, r in results.items() if w != head}}
         print(json.dumps(line), flush=True)
     if world > 1:
