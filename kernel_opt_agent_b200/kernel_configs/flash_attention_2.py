@@ -10,7 +10,7 @@ import math
 
 import torch
 
-from .. import references
+from kernel_opt_agent_b200 import references
 from ._utils import dtype_bytes
 
 KERNEL_OPT_CHARACTERISTICS = {
@@ -54,7 +54,7 @@ def input_generator(size: dict, dtype: torch.dtype, device: str, seed: int = 42)
     return _make_attention_inputs(size, dtype, device, seed=seed)
 
 
-def baseline_inputs(size: dict, dtype: torch.dtype = torch.bfloat16, device: str = "cuda", seed: int = 0) -> dict:
+def random_inputs(size: dict, dtype: torch.dtype = torch.bfloat16, device: str = "cuda", seed: int = 0) -> dict:
     """The B200 workload generator: q, k, v ~ N(0,1) from `seed` (no RMS normalisation)."""
     return _make_attention_inputs(size, dtype, device, seed=seed, rms=False)
 

@@ -1,7 +1,7 @@
 """qwen35moe_gdn_prefill config callables.
 
 ``dist = "fixture"`` (default) reproduces the reference's deterministic inputs
-(``kernel_configs/qwen35moe_gdn_prefill.py:23-44``); ``dist = "baseline"`` draws the B200
+(``kernel_configs/qwen35moe_gdn_prefill.py:23-44``); ``dist = "random"`` draws the B200
 workload distribution from a seeded CPU generator: q, k ~ N(0,1) L2-normalised per (token,
 head), v ~ N(0,1), g = -softplus(N(0,1)), beta = sigmoid(N(0,1)), zero state (or N(0, 0.02) per
 sequence with ``state_std``).  ``varlen = [len, ...]`` packs sequences along T with cu_seqlens.
@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import torch
 
-from .. import references
+from kernel_opt_agent_b200 import references
 from ._utils import dtype_bytes
 
 D = 128
@@ -47,7 +47,7 @@ def fixture_inputs(batch: int, seq_len: int, dtype: torch.dtype, device: str) ->
     }
 
 
-def baseline_inputs(batch: int, seq_len: int, dtype: torch.dtype = torch.bfloat16, device: str = "cuda",
+def random_inputs(batch: int, seq_len: int, dtype: torch.dtype = torch.bfloat16, device: str = "cuda",
                     seed: int = 0, lengths: list[int] | None = None, state_std: float = 0.0,
                     hk: int = H_K, hv: int = H_V) -> dict:
     gen = torch.Generator().manual_seed(seed)
@@ -86,7 +86,7 @@ def varlen_lengths(n_seqs: int = 8, lo: int = 1024, hi: int = 32768, seed: int =
 def input_generator(size: dict, dtype: torch.dtype, device: str, seed: int = 42) -> dict:
     if size.get("dist", "fixture") == "fixture":
         return fixture_inputs(int(size["batch"]), int(size["seq_len"]), dtype, device)
-    return baseline_inputs(int(size["batch"]), int(size["seq_len"]), dtype, device, seed=seed,
+    return random_inputs(int(size["batch"]), int(size["seq_len"]), dtype, device, seed=seed,
                            lengths=size.get("varlen"), state_std=float(size.get("state_std", 0.0)))
 
 
@@ -103,7 +103,7 @@ def numerical_stability_cases(size: dict, dtype: torch.dtype, device: str, seed:
     zero_state["state"] = torch.zeros_like(zero_state["state"])
     softer_gate = {k: (v.clone() if isinstance(v, torch.Tensor) else v) for k, v in base.items()}
     softer_gate["g"] = torch.full_like(softer_gate["g"], -0.02)
-    strong = baseline_inputs(1, 64, dtype, device, seed=seed)
+    strong = random_inputs(1, 64, dtype, device, seed=seed)
     gen = torch.Generator().manual_seed(seed + 1)
     strong["g"] = (torch.rand(strong["g"].shape, generator=gen) * 17.0 - 25.0).to(device)
     return [("baseline", base), ("zero_state", zero_state), ("softer_gate", softer_gate),

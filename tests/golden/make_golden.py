@@ -38,7 +38,7 @@ FA2_CASES = {
 
 GDN_CASES = {
     "gdn_fixture_t67": dict(kind="fixture", t=67),
-    "gdn_baseline_t96_state": dict(kind="baseline", t=96, seed=7, state_std=0.02),
+    "gdn_random_t96_state": dict(kind="random", t=96, seed=7, state_std=0.02),
     "gdn_strong_gate_t64": dict(kind="strong_gate", t=64, seed=3),
 }
 

@@ -52,12 +52,12 @@ def _check(inp, threads, out_tol=OUT_TOL, state_tol=STATE_TOL):
     (3, 129, 4, 8, 0.02),
 ])
 def test_gdn_matches_oracle(cuda_device, oracle_threads, b, t, hk, hv, state_std):
-    inp = gcfg.baseline_inputs(b, t, seed=t + hk, state_std=state_std, hk=hk, hv=hv)
+    inp = gcfg.random_inputs(b, t, seed=t + hk, state_std=state_std, hk=hk, hv=hv)
     _check(inp, oracle_threads)
 
 
 def test_gdn_varlen_with_empty_and_tail_sequences(cuda_device, oracle_threads):
-    inp = gcfg.baseline_inputs(1, 0, lengths=[1, 63, 64, 65, 200, 0, 129], seed=5, state_std=0.02)
+    inp = gcfg.random_inputs(1, 0, lengths=[1, 63, 64, 65, 200, 0, 129], seed=5, state_std=0.02)
     _check(inp, oracle_threads)
 
 
@@ -76,7 +76,7 @@ def test_gdn_reference_fixture_fp32_io(cuda_device, oracle_threads):
 
 def test_gdn_stability_cases(cuda_device, oracle_threads):
     cfg = KERNEL_CONFIGS["qwen35moe_gdn_prefill"]
-    for name, inp in cfg["numerical_stability_cases"]({"batch": 1, "seq_len": 300, "dist": "baseline"},
+    for name, inp in cfg["numerical_stability_cases"]({"batch": 1, "seq_len": 300, "dist": "random"},
                                                        torch.bfloat16, "cuda"):
         out, fs = gdn.kernel_fn(**inp)
         o_ref, s_ref = _oracle(inp, oracle_threads)
@@ -86,7 +86,7 @@ def test_gdn_stability_cases(cuda_device, oracle_threads):
 
 
 def test_gdn_strong_negative_gate_strict(cuda_device, oracle_threads):
-    inp = gcfg.baseline_inputs(1, 64, seed=3)
+    inp = gcfg.random_inputs(1, 64, seed=3)
     gen = torch.Generator().manual_seed(4)
     inp["g"] = (torch.rand(inp["g"].shape, generator=gen) * 17.0 - 25.0).cuda()
     _check(inp, oracle_threads)
@@ -109,13 +109,13 @@ def test_gdn_matches_reference_kernel_golden(cuda_device, name):
 
 def test_gdn_config1_full(cuda_device, oracle_threads):
     """B=1, T=2048, Hk=16, Hv=32, zero state: every output and the fp32 final state."""
-    inp = gcfg.baseline_inputs(1, 2048, seed=0)
+    inp = gcfg.random_inputs(1, 2048, seed=0)
     _check(inp, oracle_threads)
 
 
 def test_gdn_state_continuation_is_exact(cuda_device):
     """Chunk-aligned split with the state handed over equals the one-shot run bit for bit."""
-    inp = gcfg.baseline_inputs(1, 640, seed=8, state_std=0.02)
+    inp = gcfg.random_inputs(1, 640, seed=8, state_std=0.02)
     out, fs = gdn.kernel_fn(**inp)
     a = {k: (v[:, :256] if k in ("q", "k", "v", "g", "beta") else v) for k, v in inp.items()}
     oa, sa = gdn.kernel_fn(**a)
@@ -127,7 +127,7 @@ def test_gdn_state_continuation_is_exact(cuda_device):
 
 
 def test_gdn_deterministic(cuda_device):
-    inp = gcfg.baseline_inputs(2, 700, seed=11, state_std=0.02)
+    inp = gcfg.random_inputs(2, 700, seed=11, state_std=0.02)
     r = [gdn.kernel_fn(**inp) for _ in range(3)]
     for o, s in r[1:]:
         assert torch.equal(o, r[0][0]) and torch.equal(s, r[0][1])
@@ -137,7 +137,7 @@ def test_gdn_varlen_full_size(cuda_device, oracle_threads):
     """8 sequences, lengths ~U[1024, 32768], per-sequence initial state N(0, 0.02): the two
     shortest sequences against the oracle, every sequence against its own one-sequence run."""
     lengths = gcfg.varlen_lengths(8, seed=0)
-    inp = gcfg.baseline_inputs(1, 0, lengths=lengths, seed=0, state_std=0.02)
+    inp = gcfg.random_inputs(1, 0, lengths=lengths, seed=0, state_std=0.02)
     out, fs = gdn.kernel_fn(**inp)
     gdn.check_device_status(cuda_device)
     cu = np.cumsum([0] + lengths)

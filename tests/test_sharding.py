@@ -35,7 +35,7 @@ def test_gdn_value_heads_keep_the_kernel_mapping():
 
 
 def test_gdn_slice_equals_heads_of_full_run():
-    inp = gcfg.baseline_inputs(1, 70, torch.float32, "cpu", seed=3, state_std=0.02, hk=4, hv=8)
+    inp = gcfg.random_inputs(1, 70, torch.float32, "cpu", seed=3, state_std=0.02, hk=4, hv=8)
     args = lambda d: [d[x].numpy() for x in ("q", "k", "v", "g", "beta", "state")]  # noqa: E731
     o_full, s_full = oracle.gdn_recurrent(*args(inp))
     parts_o, parts_s = [], []
@@ -78,7 +78,7 @@ def _worker(rank, world, port, q):
         o = torch.from_numpy(oracle.fa2_attention(loc["q"].numpy(), loc["k"].numpy(), loc["v"].numpy()))
         full = sharding.gather_to_rank0(o, dim=1)
         # GDN: key-head groups, outputs and states gathered and put back in head order
-        inp = gcfg.baseline_inputs(1, 50, torch.float32, "cpu", seed=5, state_std=0.02, hk=4, hv=8)
+        inp = gcfg.random_inputs(1, 50, torch.float32, "cpu", seed=5, state_std=0.02, hk=4, hv=8)
         ranges = sharding.even_ranges(4, world)
         sl = sharding.slice_gdn_inputs(inp, *ranges[rank])
         go, gs = oracle.gdn_recurrent(*(sl[x].numpy() for x in ("q", "k", "v", "g", "beta", "state")))

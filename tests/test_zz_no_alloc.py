@@ -37,8 +37,8 @@ def _noalloc(inp, status=None):
 
 
 def test_noalloc_matches_regular_entry_point_twice(cuda_device):
-    cases = [gcfg.baseline_inputs(3, 200, seed=21, state_std=0.02, hk=4, hv=8),
-             gcfg.baseline_inputs(2, 129, seed=22, state_std=0.02)]
+    cases = [gcfg.random_inputs(3, 200, seed=21, state_std=0.02, hk=4, hv=8),
+             gcfg.random_inputs(2, 129, seed=22, state_std=0.02)]
     word = torch.zeros(1, dtype=torch.int32, device=cuda_device)
     for i, inp in enumerate(cases):
         ref_out, ref_state = gdn.kernel_fn(**inp)
