@@ -7,7 +7,7 @@
 //
 // Chunked form used here (C = 64 tokens, in-chunk cumulative log decay G_t, incoming state S0):
 //   L_ts  = beta_t exp(G_t - G_s) (k_t . k_s)          s < t
-//   T     = (I + L)^-1 diag(beta)                      (unit-lower inverse, fp32, blocked 16x16)
+//   T     = (I + L)^-1 diag(beta)                      (unit-lower inverse in fp32, 16x16 blocks)
 //   W     = T diag(e^G) K                              (tensor core; T diag(e^G) as bf16 hi + lo)
 //   Delta = T V - W S0^T                               (tensor core; T as hi + lo; W S0^T as the
 //                                                       3-term product W_hi S_hi + W_lo S_hi + W_hi S_lo)
@@ -15,23 +15,25 @@
 //   S     = e^{G_C} S0 + (diag(e^{G_C - G}) Delta)^T K (tensor core; Delta' split hi + lo)
 // Every contraction is an M=128 tcgen05 MMA because the CTA keeps the VALUE dimension on the
 // 128 TMEM lanes ("transposed" products: Delta^T, O^T, S with lane = value row; W^T with
-// lane = key row).  The fp32 master state never leaves TMEM between chunks; a hi + lo bf16 copy
-// in shared memory is the MMA operand for the next chunk.  The hi/lo splits keep every product
-// that feeds the state at ~16 significant bits, so the fp32 final state stays within 1e-3
-// relative of the fp32 recurrence even when the decay is weak.
+// lane = key row).  The fp32 state and its hi + lo bf16 copies (the A operand of the next
+// chunk's products) never leave TMEM between chunks.  The hi/lo splits keep every product that
+// feeds the state at ~16 significant bits, so the fp32 final state stays within 1e-3 relative of
+// the fp32 recurrence even when the decay is weak.
 //
-// One CTA processes one (sequence, value head) unit, all its chunks in order.  Warp roles:
-//   warps 0-3   state chain: Delta pass (Delta -> bf16 operands in TMEM), state pass (S ->
-//               bf16 shared copy, pre-scale by the next chunk's decay), initial/final state
-//   warps 4-7   operands: decay prefix sums, QK/KK read-out (P tile, e^G-scaled Q, L rows),
-//               W pass (W^T -> -W bf16 tile), output pass (O^T -> global)
-//   warps 8-9   triangular solve -> T (hi/lo) and T diag(e^G) tiles
-//   warp 10     TMA producer (stacked Q/K chunk tile, V chunk tile)
-//   warp 11     TMEM owner and MMA issuer for the state-independent groups; it polls the
-//               hand-off barriers and issues whichever group is ready.  The state-dependent
-//               groups are issued by the warps that produce their inputs, so the state chain
-//               never waits behind the next chunk's preparation.
-// Hand-off barriers are two-slot arrays indexed by chunk parity.  All waits are bounded.
+// One CTA processes one (sequence, value head) unit, all its chunks in order.  Only the state
+// chain is sequential: Delta(c) -> S(c+1) -> Delta(c+1).  Everything that does not depend on the
+// state (decay sums, Q K^T / K K^T, the triangular solve, W) is prepared for chunk c+1 while the
+// chain works on chunk c.  Warp roles (384 threads):
+//   warps 0-3   state chain, thread = value row: issues the state-dependent MMAs, Delta pass
+//               (Delta -> bf16 operands in TMEM), state pass (S -> hi/lo copies, decay for the
+//               next chunk), initial / final state; thread 0 also issues every TMA load
+//   warps 4-7   operands, each warp polling on its own: decay prefix sums (warp 4), Q K^T / K K^T
+//               read-out (P tile, e^G-scaled Q in place, rows of L), output pass (O^T -> global)
+//   warps 8-11  triangular solve (16x16 blocks), T / T diag(e^G) tiles, W pass (W^T -> -W
+//               tiles); thread 0 issues the preparation MMAs (Q K^T, W)
+// Hand-off barriers are two-slot arrays indexed by chunk parity (the Q/K ring has three).  Every
+// producer of chunk c+2's event causally follows every waiter of chunk c's event, so no waiter
+// can fall two phases behind (argued next to each barrier below).  All waits are bounded.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -46,40 +48,34 @@ namespace gdn {
 constexpr int kC = 64;     // tokens per chunk
 constexpr int kD = 128;    // head dim (keys and values)
 constexpr int kThreads = 384;
-constexpr int kWarpTma = 10;
-constexpr int kWarpMma = 11;
+constexpr int kSlots = 3;  // Q/K chunk tiles in flight
 
-// TMEM columns
+// TMEM columns (512 allocated)
 constexpr uint32_t kColS = 0;      // state S[v][k] fp32, 128 cols
-constexpr uint32_t kColX0 = 128;   // Delta^T fp32 (64 cols) then bf16 A operands (96 cols), 2 slots
-constexpr uint32_t kColX1 = 224;
-constexpr uint32_t kColO = 320;    // O^T fp32, 64 cols
-constexpr uint32_t kColW = 384;    // W^T fp32 (lane = key row), 64 cols
-constexpr uint32_t kColQK = 448;   // lanes 0-63: Q K^T, lanes 64-127: K K^T, 64 cols
+constexpr uint32_t kColShi = 128;  // state hi copy, bf16 pairs along k, 64 cols
+constexpr uint32_t kColSlo = 192;  // state lo copy
+constexpr uint32_t kColX = 256;    // Delta^T fp32 (64 cols), then Delta'hi | Delta'lo | Delta bf16 (32 each)
+constexpr uint32_t kColO = 352;    // O^T fp32, 64 cols
+constexpr uint32_t kColQW = 416;   // Q K^T (lanes 0-63) / K K^T (lanes 64-127), later W^T (lane = key row)
 
 // shared memory layout (bytes; every MMA tile starts on a 1024-byte boundary)
 constexpr int kSlotBytes = 32768;                  // stacked [Q;K] chunk tile: 2 boxes of 128 rows x 128 B
-constexpr int kOffSlot0 = 0;                       //   rows 0-63 of a box: Q (scaled in place to e^G Q)
-constexpr int kOffSlot1 = kSlotBytes;              //   rows 64-127: K
-constexpr int kOffV = 2 * kSlotBytes;              // V chunk tile: 2 boxes of 64 rows x 128 B
-constexpr int kOffP = kOffV + 16384;               // P [t][s] bf16
-constexpr int kOffThi = kOffP + 8192;              // T hi [t][s]
-constexpr int kOffTlo = kOffThi + 8192;            // T lo
-constexpr int kOffTGhi = kOffTlo + 8192;           // T diag(e^G) hi
-constexpr int kOffTGlo = kOffTGhi + 8192;          // T diag(e^G) lo
-constexpr int kOffWhi = kOffTGlo + 8192;           // -W hi as [k][t], 128 rows x 128 B
-constexpr int kOffWlo = kOffWhi + 16384;           // -W lo
-constexpr int kOffShi = kOffWlo + 16384;           // state copy hi [v][k]: 2 boxes of 128 rows x 128 B
-constexpr int kOffSlo = kOffShi + 32768;           // state copy lo
-constexpr int kOffParams = kOffSlo + 32768;
+constexpr int kOffSlots = 0;                       //   rows 0-63 of a box: Q (scaled in place to scale e^G Q)
+                                                   //   rows 64-127: K
+constexpr int kOffV = kSlots * kSlotBytes;         // V chunk tile: 2 boxes of 64 rows x 128 B
+constexpr int kOffP = kOffV + 16384;               // P [t][s] bf16, 2 x 8 KB (chunk parity)
+constexpr int kOffT = kOffP + 16384;               // T hi [s][t] (8 KB), T lo (8 KB)
+constexpr int kLds = 68;                           // fp32 row stride of the solve matrices
+constexpr int kOffL = kOffT + 16384;               // L fp32 [t][s] (row stride kLds); after the
+                                                   //   solve: T diag(e^G) hi [s][t], lo (8 KB each)
+constexpr int kOffX = kOffL + 64 * kLds * 4;       // (I + L)^-1 fp32 [t][s] (row stride kLds)
+constexpr int kOffW = kOffX + 64 * kLds * 4;       // -W hi as [k][t] (16 KB), -W lo (16 KB)
+constexpr int kOffStage = kOffW + 32768;           // output staging, 4 warps x 32 tokens x 64 B
+constexpr int kOffParams = kOffStage + 8192;
 constexpr int kParamsBytes = 1280;
 constexpr int kSmemBytes = kOffParams + 2 * kParamsBytes;
-// The triangular solve reads L from fp32 scratch that aliases the T hi/lo tiles and keeps its
-// solved columns in a buffer that aliases the T diag(e^G) tiles; it writes the tiles only after
-// both have been read into registers.  L is stored column-major: scratch[s * 64 + t] = L[t][s].
-constexpr int kOffScratch = kOffThi;
-static_assert(kOffTGhi - kOffThi >= 64 * 64 * 4 && kOffWhi - kOffTGhi >= 64 * 64 * 4, "solve buffers");
-static_assert(kSmemBytes + 1024 <= 227 * 1024, "shared memory budget");
+static_assert(kOffL % 1024 == 0 && kOffX % 1024 == 0 && kOffW % 1024 == 0, "tile alignment");
+static_assert(kSmemBytes + 1024 + 512 <= 227 * 1024, "shared memory budget");
 
 struct ChunkParams {
   float beta[kC];         // write strength (0 for tokens past the sequence end)
@@ -105,15 +101,21 @@ struct Params {
   uint32_t* status;
 };
 
-// Hand-off barriers, each a 2-slot array indexed by chunk parity (event of chunk c lives in slot
-// c & 1 and completes its (c >> 1)-th phase).  Every producer of chunk c+2's event causally
-// follows every waiter of chunk c's event, so no waiter can fall two phases behind.
+// Hand-off barriers.  Event of chunk c lives in slot c & 1 (in_full: c % 3) and completes the
+// slot's (c >> 1)-th (c / 3-th) phase.
 struct Barriers {
-  uint64_t in_full[2], v_full[2], v_free[2];
-  uint64_t qk_done[2], qk_read[2], g_ready[2], prep1[2];
-  uint64_t w_done[2], wneg[2], delta[2], da_done[2];
-  uint64_t snew[2], s_ready[2], o_done[2];
-  uint64_t p_ready[2], t3b[2];
+  uint64_t in_full[kSlots];  // TMA Q/K(c) landed.   waiter: solve t0 (T1).  next phase needs T4(c)
+  uint64_t v_full[2];        // TMA V(c) landed.     waiter: chain t0 (T3).  V(c+2) issued after T3(c+1)
+  uint64_t qk_done[2];       // T1(c) complete.      waiters: operand warps; T1(c+2) follows readout(c+1)
+  uint64_t qk_read[2];       // read-out(c) done (128). waiters: solve; readout(c+2) follows T1(c+2) <- solve(c+1)
+  uint64_t g_ready[2];       // decay sums(c) (32).  waiters: operand warps, chain; scan(c+2) follows output(c)
+  uint64_t w_done[2];        // T2(c) complete.      waiters: solve; T2(c+2) follows their W pass(c+1)
+  uint64_t w_ready[2];       // W/T tiles(c) (128).  waiter: chain t0; W pass(c+2) follows T3(c+1)
+  uint64_t x_ready[2];       // T3(c) complete.      waiters: chain, solve; T3(c+2) follows both
+  uint64_t s_new[2];         // T3b(c), T4(c) complete. waiters: chain
+  uint64_t o_done[2];        // T5(c) complete.      waiters: operand warps, chain t0
+  uint64_t o_read[2];        // O(c) read out (128). waiter: chain t0 (T3b(c+1))
+  uint64_t drain[2];         // retirement of the two MMA-issuing threads
 };
 
 __device__ __forceinline__ bool wait_c(uint64_t* bars, int c, uint32_t* status, uint32_t code) {
@@ -169,31 +171,15 @@ __device__ __forceinline__ void split_pack(float x0, float x1, uint32_t& hi, uin
   lo = pack_bf16x2(x0 - __uint_as_float(b0 & 0xFFFF0000u), x1 - __uint_as_float(b1 & 0xFFFF0000u));
 }
 
-// Writes 64 fp32 state values (columns [64*half, 64*half+64) of row v) as the hi and lo bf16
-// state copies (box `half` of each).
-__device__ __forceinline__ void store_state_half(uint8_t* smem, int v, int half, const uint32_t (&sv)[64]) {
+// 32 fp32 values x[OFF, OFF+32) (raw bits) -> hi and lo bf16 copies, 16 TMEM columns each
+template <int OFF>
+__device__ __forceinline__ void store_split32(uint32_t hi_addr, uint32_t lo_addr, const uint32_t (&x)[64]) {
+  uint32_t hi[16], lo[16];
 #pragma unroll
-  for (int q4 = 0; q4 < 2; ++q4) {
-    uint32_t hi[16], lo[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      split_pack(__uint_as_float(sv[32 * q4 + 2 * j]), __uint_as_float(sv[32 * q4 + 2 * j + 1]), hi[j], lo[j]);
-    store_half_row_sw128(smem + kOffShi + half * 16384, v, q4, hi);
-    store_half_row_sw128(smem + kOffSlo + half * 16384, v, q4, lo);
-  }
-}
-
-__device__ __forceinline__ void output_pass(const Params& p, uint32_t lane_base, int tok0, int len, int cp, int h,
-                                            int r) {
-  const int nv = min(kC, len - cp * kC);
-  uint32_t row[64];
-  tmem_ld64(lane_base + kColO, row);
-  if (r == 0) GDN_TRACE(20, cp);
-  __nv_bfloat16* dst = p.out + (static_cast<size_t>(tok0 + cp * kC) * p.hv + h) * kD + r;
-  const size_t tstride = static_cast<size_t>(p.hv) * kD;
-#pragma unroll
-  for (int t = 0; t < kC; ++t)
-    if (t < nv) dst[t * tstride] = __float2bfloat16_rn(__uint_as_float(row[t]) * p.scale);
+  for (int j = 0; j < 16; ++j)
+    split_pack(__uint_as_float(x[OFF + 2 * j]), __uint_as_float(x[OFF + 2 * j + 1]), hi[j], lo[j]);
+  tmem_st16(hi_addr, hi);
+  tmem_st16(lo_addr, lo);
 }
 
 // K-major tile of 2 boxes (16 KB apart): descriptor of the 16-element k step kk
@@ -201,41 +187,82 @@ __device__ __forceinline__ uint64_t kmaj_desc(uint32_t base, int kk) {
   return make_sdesc_sw128(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
 }
 
-// T3a  Delta^T += S_hi (-W_hi)^T + S_lo (-W_hi)^T + S_hi (-W_lo)^T   (M=128 v, N=64 t, K=128 k)
-__device__ __forceinline__ void issue_t3a(uint32_t tbase, const uint8_t* smem, int c) {
-  const uint32_t id_sw = make_idesc(128, 64, 1, 0, 1);  // A K-major (S), B MN-major (-W as [k][t])
-  const uint32_t colx = (c & 1) ? kColX1 : kColX0;
-#pragma unroll
-  for (int term = 0; term < 3; ++term) {
-    const uint32_t sa = smem_u32(smem + (term == 1 ? kOffSlo : kOffShi));
-    const uint32_t wa = smem_u32(smem + (term == 2 ? kOffWlo : kOffWhi));
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-      umma_bf16_ss(tbase + colx, kmaj_desc(sa, kk), make_sdesc_sw128(wa + kk * 2048, 16384, 1024), id_sw, 1u);
-  }
+__device__ __forceinline__ uint32_t slot_addr(const uint8_t* smem, int c) {
+  return smem_u32(smem + kOffSlots + (c % kSlots) * kSlotBytes);
 }
 
-// T3b  O^T = S_hi (e^G Q)^T   (M=128 v, N=64 t, K=128 k)
-__device__ __forceinline__ void issue_t3b(uint32_t tbase, const uint8_t* smem, int c) {
+// T1  [Q;K] K^T   (M=128 rows of the stacked tile, N=64 keys s, K=128)
+__device__ __forceinline__ void issue_t1(uint32_t tbase, const uint8_t* smem, int c) {
   const uint32_t id = make_idesc(128, 64, 1, 0, 0);
-  const uint32_t sa = smem_u32(smem + kOffShi);
-  const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
+  const uint32_t slot = slot_addr(smem, c);
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
-    umma_bf16_ss(tbase + kColO, kmaj_desc(sa, kk), kmaj_desc(slot, kk), id, kk > 0 ? 1u : 0u);
+    umma_bf16_ss(tbase + kColQW, kmaj_desc(slot, kk), kmaj_desc(slot + 8192, kk), id, kk > 0 ? 1u : 0u);
 }
 
-// T4  S += Delta'_hi^T K + Delta'_lo^T K   (M=128 v, N=128 k, K=64 t; A from TMEM)
-__device__ __forceinline__ void issue_t4(uint32_t tbase, const uint8_t* smem, int c) {
-  const uint32_t id_upd = make_idesc(128, 128, 1, 0, 1);
-  const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
-  const uint32_t colx = (c & 1) ? kColX1 : kColX0;
+// T2  W^T = K^T (TG_hi + TG_lo)^T   (M=128 k, N=64 t, K=64 s; both operands MN-major)
+__device__ __forceinline__ void issue_t2(uint32_t tbase, const uint8_t* smem, int c) {
+  const uint32_t id = make_idesc(128, 64, 1, 1, 1);
+  const uint32_t kt = slot_addr(smem, c) + 8192;
+  const uint32_t tg = smem_u32(smem + kOffL);
 #pragma unroll
   for (int part = 0; part < 2; ++part)
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk)
-      umma_bf16_ts(tbase + kColS, tbase + colx + 32 + 32 * part + 8 * kk,
-                   make_sdesc_sw128(slot + 8192 + kk * 2048, 16384, 1024), id_upd, 1u);
+      umma_bf16_ss(tbase + kColQW, make_sdesc_sw128(kt + kk * 2048, 16384, 1024),
+                   make_sdesc_sw128(tg + part * 8192 + kk * 2048, 16384, 1024), id, (part > 0 || kk > 0) ? 1u : 0u);
+}
+
+// T3  Delta^T = V^T (T_hi + T_lo)^T + S_hi (-W_hi)^T + S_lo (-W_hi)^T + S_hi (-W_lo)^T
+//     (M=128 v, N=64 t; the state terms take S from TMEM)
+__device__ __forceinline__ void issue_t3(uint32_t tbase, const uint8_t* smem) {
+  const uint32_t id_v = make_idesc(128, 64, 1, 1, 1);  // A = V^T MN-major, B = T [s][t] MN-major
+  const uint32_t id_s = make_idesc(128, 64, 1, 0, 1);  // A = S (TMEM), B = -W [k][t] MN-major
+  const uint32_t a_v = smem_u32(smem + kOffV), a_t = smem_u32(smem + kOffT), a_w = smem_u32(smem + kOffW);
+#pragma unroll
+  for (int part = 0; part < 2; ++part)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+      umma_bf16_ss(tbase + kColX, make_sdesc_sw128(a_v + kk * 2048, 8192, 1024),
+                   make_sdesc_sw128(a_t + part * 8192 + kk * 2048, 16384, 1024), id_v, (part > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+  for (int term = 0; term < 3; ++term) {
+    const uint32_t sa = tbase + (term == 1 ? kColSlo : kColShi);
+    const uint32_t wb = a_w + (term == 2 ? 16384 : 0);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+      umma_bf16_ts(tbase + kColX, sa + 8 * kk, make_sdesc_sw128(wb + kk * 2048, 16384, 1024), id_s, 1u);
+  }
+}
+
+// T3b  O^T = S_hi (scale e^G Q)^T   (M=128 v, N=64 t, K=128 k; A from TMEM)
+__device__ __forceinline__ void issue_t3b(uint32_t tbase, const uint8_t* smem, int c) {
+  const uint32_t id = make_idesc(128, 64, 1, 0, 0);
+  const uint32_t slot = slot_addr(smem, c);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    umma_bf16_ts(tbase + kColO, tbase + kColShi + 8 * kk, kmaj_desc(slot, kk), id, kk > 0 ? 1u : 0u);
+}
+
+// T4  S += Delta'_hi^T K + Delta'_lo^T K   (M=128 v, N=128 k, K=64 t; A from TMEM)
+__device__ __forceinline__ void issue_t4(uint32_t tbase, const uint8_t* smem, int c) {
+  const uint32_t id = make_idesc(128, 128, 1, 0, 1);
+  const uint32_t kt = slot_addr(smem, c) + 8192;
+#pragma unroll
+  for (int part = 0; part < 2; ++part)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+      umma_bf16_ts(tbase + kColS, tbase + kColX + 32 * part + 8 * kk, make_sdesc_sw128(kt + kk * 2048, 16384, 1024),
+                   id, 1u);
+}
+
+// T5  O^T += Delta^T (scale P)^T   (M=128 v, N=64 t, K=64 s; A from TMEM, B = P [t][s] K-major)
+__device__ __forceinline__ void issue_t5(uint32_t tbase, const uint8_t* smem, int c) {
+  const uint32_t id = make_idesc(128, 64, 1, 0, 0);
+  const uint32_t a_p = smem_u32(smem + kOffP + (c & 1) * 8192);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+    umma_bf16_ts(tbase + kColO, tbase + kColX + 64 + 8 * kk, make_sdesc_sw128(a_p + kk * 32, 16, 1024), id, 1u);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -244,7 +271,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ Barriers bars;
-  __shared__ uint64_t drain_bar;
   __shared__ uint32_t tmem_base_shared;
 
   const int warp = warp_id();
@@ -256,28 +282,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kh = h % p.hk;
   const int tok0 = p.cu_seqlens[seq];
   const int len = p.cu_seqlens[seq + 1] - tok0;
-  const int nchunks = len > 0 ? (len + kC - 1) / kC : 0;
+  const int N = len > 0 ? (len + kC - 1) / kC : 0;
   ChunkParams* params = reinterpret_cast<ChunkParams*>(smem + kOffParams);
-  float* scratch = reinterpret_cast<float*>(smem + kOffScratch);
   const size_t state_off = (static_cast<size_t>(seq) * p.hv + h) * kD * kD;
 
   if (threadIdx.x == 0) {
     cta_abort_flag() = 0u;
     uint64_t* all = reinterpret_cast<uint64_t*>(&bars);
     for (int i = 0; i < static_cast<int>(sizeof(Barriers) / 8); ++i) mbar_init(&all[i], 1);
-    mbar_init(&drain_bar, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars.qk_read[i], 128);
       mbar_init(&bars.g_ready[i], 32);
-      mbar_init(&bars.prep1[i], 64);
-      mbar_init(&bars.wneg[i], 128);
-      mbar_init(&bars.da_done[i], 128);
-      mbar_init(&bars.s_ready[i], 128);
-      mbar_init(&bars.p_ready[i], 128);
+      mbar_init(&bars.w_ready[i], 128);
+      mbar_init(&bars.o_read[i], 128);
     }
     fence_barrier_init();
   }
-  if (warp == kWarpMma) {
+  if (warp == 0) {
     tmem_alloc(&tmem_base_shared, 512);
     tmem_relinquish();
   }
@@ -287,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = tmem_base_shared;
   if (threadIdx.x == 0) GDN_TRACE(19, 0);
 
-  if (nchunks == 0) {
+  if (N == 0) {
     // empty sequence: final state = initial state
     if (warp < 4) {
       const int v = threadIdx.x;
@@ -300,8 +321,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < 4) {
     // =========================================================== state chain (lane = value row)
     const int v = threadIdx.x;
-    const uint32_t lane_base = tmem_addr(tbase, warp * 32, 0);
-    // --- initial state: hi/lo bf16 copies, TMEM S <- gamma_C(0) * S0
+    const uint32_t lb = tmem_addr(tbase, warp * 32, 0);
+    int qk_issued = 0, v_issued = 0;
+    auto load_qk = [&](int c) {  // thread 0 only
+      const int s = c % kSlots;
+      uint8_t* slot = smem + kOffSlots + s * kSlotBytes;
+      mbar_arrive_expect_tx(&bars.in_full[s], kSlotBytes);
+      for (int bx = 0; bx < 2; ++bx) {
+        tma_load_3d(slot + bx * 16384, &map_q, &bars.in_full[s], bx * 64, kh, tok0 + c * kC);
+        tma_load_3d(slot + bx * 16384 + 8192, &map_k, &bars.in_full[s], bx * 64, kh, tok0 + c * kC);
+      }
+      qk_issued = c + 1;
+    };
+    auto load_v = [&](int c) {  // thread 0 only
+      mbar_arrive_expect_tx(&bars.v_full[c & 1], 16384);
+      for (int bx = 0; bx < 2; ++bx)
+        tma_load_3d(smem + kOffV + bx * 8192, &map_v, &bars.v_full[c & 1], bx * 64, h, tok0 + c * kC);
+      v_issued = c + 1;
+    };
+    if (v == 0) {
+      tma_prefetch_desc(&map_q);
+      tma_prefetch_desc(&map_k);
+      tma_prefetch_desc(&map_v);
+      for (int c = 0; c < kSlots && c < N; ++c) load_qk(c);
+      load_v(0);
+    }
+    // --- initial state: hi/lo copies and S <- gamma(0) S0
     bool ok = wait_c_warp(bars.g_ready, 0, p.status, kDevTimeoutPipe);
     if (ok) {
       const float gam = params[0].gamma_c;
@@ -317,75 +362,87 @@ __global__ void __launch_bounds__(kThreads, 1)
           sv[j + 2] = __float_as_uint(val.z);
           sv[j + 3] = __float_as_uint(val.w);
         }
-        store_state_half(smem, v, half, sv);
+        store_split32<0>(lb + kColShi + 32 * half, lb + kColSlo + 32 * half, sv);
+        store_split32<32>(lb + kColShi + 32 * half + 16, lb + kColSlo + 32 * half + 16, sv);
 #pragma unroll
         for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
-        tmem_st32(lane_base + kColS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_st32(lane_base + kColS + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_st32(lb + kColS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_st32(lb + kColS + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
       }
-      fence_async_smem();
       tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bars.s_ready[0]);
     }
-    for (int c = 0; ok && c < nchunks; ++c) {
-      const ChunkParams& pc = params[c & 1];
-      const uint32_t colx = (c & 1) ? kColX1 : kColX0;
-      // --- (one thread) T3a: the state-dependent part of Delta, as soon as S(c) and W(c) exist
-      if (v == 0 && wait_c(bars.s_ready, c, p.status, kDevTimeoutPipe) &&
-          wait_c(bars.wneg, c, p.status, kDevTimeoutPipe)) {
-        tc_fence_after();
-        issue_t3a(tbase, smem, c);
-        umma_commit(&bars.delta[c & 1]);
-        GDN_TRACE(13, c);
-      }
-      // --- Delta pass: Delta^T (fp32) -> bf16 Delta, Delta' = e^{G_C - G} Delta as hi + lo
-      if (!wait_c_warp(bars.delta, c, p.status, kDevTimeoutMma)) { ok = false; break; }
-      tc_fence_after();
-      if (v == 0) GDN_TRACE(0, c);
-      {
-        uint32_t d[64];
-        tmem_ld64(lane_base + colx, d);
-        uint32_t pk[32], hi[32], lo[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float d0 = __uint_as_float(d[2 * j]);
-          const float d1 = __uint_as_float(d[2 * j + 1]);
-          pk[j] = pack_bf16x2(d0, d1);
-          split_pack(d0 * pc.egr[2 * j], d1 * pc.egr[2 * j + 1], hi[j], lo[j]);
+    tc_fence_before();
+    ok = named_sync_and(1, 128, ok);
+    for (int c = 0; ok && c < N; ++c) {
+      // --- (thread 0) T3 as soon as the W/T tiles and V of chunk c exist and T5(c-1) has read
+      //     the X region; then T3b once the output pass has read O(c-1)
+      if (v == 0) {
+        bool r = wait_c(bars.w_ready, c, p.status, kDevTimeoutPipe) &&
+                 wait_c(bars.v_full, c, p.status, kDevTimeoutTma) &&
+                 (c == 0 || wait_c(bars.o_done, c - 1, p.status, kDevTimeoutMma));
+        if (r) {
+          tc_fence_after();
+          issue_t3(tbase, smem);
+          umma_commit(&bars.x_ready[c & 1]);
+          GDN_TRACE(0, c);
         }
-        tmem_st32(lane_base + colx, pk);
-        tmem_st32(lane_base + colx + 32, hi);
-        tmem_st32(lane_base + colx + 64, lo);
+        if (r && c >= 1) r = wait_c(bars.o_read, c - 1, p.status, kDevTimeoutPipe);
+        if (r) {
+          tc_fence_after();
+          issue_t3b(tbase, smem, c);
+        }
+      }
+      // --- Delta pass: Delta^T (fp32) -> Delta'hi | Delta'lo | Delta bf16
+      // (every exit from this loop goes through a named_sync_and, so the four warps leave together)
+      const bool xr = wait_c_warp(bars.x_ready, c, p.status, kDevTimeoutMma);
+      tc_fence_after();
+      if (xr && v == 0) {
+        GDN_TRACE(1, c);
+        if (c + 1 < N) load_v(c + 1);  // V(c) has been read by T3(c)
+      }
+      if (xr) {
+        const ChunkParams& pc = params[c & 1];
+        uint32_t d[64];
+        tmem_ld64(lb + kColX, d);
+        uint32_t hi[32], lo[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          split_pack(__uint_as_float(d[2 * j]) * pc.egr[2 * j], __uint_as_float(d[2 * j + 1]) * pc.egr[2 * j + 1],
+                     hi[j], lo[j]);
+        tmem_st32(lb + kColX, hi);
+        tmem_st32(lb + kColX + 32, lo);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) hi[j] = pack_bf16x2(__uint_as_float(d[2 * j]), __uint_as_float(d[2 * j + 1]));
+        tmem_st32(lb + kColX + 64, hi);
         tmem_wait_st();
       }
       tc_fence_before();
-      mbar_arrive(&bars.da_done[c & 1]);
-      if (v == 0) GDN_TRACE(1, c);
-      // --- (one thread) T4: the state update
-      if (v == 0 && wait_c(bars.da_done, c, p.status, kDevTimeoutPipe)) {
+      if (!named_sync_and(1, 128, xr)) { ok = false; break; }
+      if (v == 0) {
+        GDN_TRACE(2, c);
         tc_fence_after();
         issue_t4(tbase, smem, c);
-        umma_commit(&bars.snew[c & 1]);
-        GDN_TRACE(14, c);
+        umma_commit(&bars.s_new[c & 1]);
+        issue_t5(tbase, smem, c);
+        umma_commit(&bars.o_done[c & 1]);
       }
-      // --- state pass: S (fp32) -> hi/lo bf16 copies for the next chunk, pre-scale by its decay
-      //     (the copies are overwritten in place: T3b, the other reader, must have completed)
-      if (!wait_c_warp(bars.snew, c, p.status, kDevTimeoutMma)) { ok = false; break; }
-      if (!wait_c_warp(bars.t3b, c, p.status, kDevTimeoutMma)) { ok = false; break; }
+      // --- state pass: S(c+1) -> hi/lo copies, pre-scaled fp32 state for the next update
+      const bool last = (c == N - 1);
+      bool sr = wait_c_warp(bars.s_new, c, p.status, kDevTimeoutMma);
       tc_fence_after();
-      if (v == 0) GDN_TRACE(2, c);
-      const bool last = (c == nchunks - 1);
+      if (sr && v == 0) {
+        GDN_TRACE(3, c);
+        if (c + kSlots < N) load_qk(c + kSlots);  // every reader of Q/K(c) has completed
+      }
       float gam = 1.0f;
-      if (!last) {
-        if (!wait_c_warp(bars.g_ready, c + 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
+      if (sr && !last) {
+        sr = wait_c_warp(bars.g_ready, c + 1, p.status, kDevTimeoutPipe);
         gam = params[(c + 1) & 1].gamma_c;
       }
 #pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
+      for (int half = 0; sr && half < 2; ++half) {
         uint32_t sv[64];
-        tmem_ld64(lane_base + kColS + half * 64, sv);
-        if (v == 0 && half == 0) GDN_TRACE(21, c);
+        tmem_ld64(lb + kColS + half * 64, sv);
         if (last) {
           float* dst = p.state_out + state_off + v * kD + half * 64;
 #pragma unroll
@@ -393,38 +450,94 @@ __global__ void __launch_bounds__(kThreads, 1)
             *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
                                                               __uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3]));
         } else {
-          store_state_half(smem, v, half, sv);
+          store_split32<0>(lb + kColShi + 32 * half, lb + kColSlo + 32 * half, sv);
+          store_split32<32>(lb + kColShi + 32 * half + 16, lb + kColSlo + 32 * half + 16, sv);
 #pragma unroll
           for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
-          tmem_st32(lane_base + kColS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-          tmem_st32(lane_base + kColS + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tmem_st32(lb + kColS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_st32(lb + kColS + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         }
       }
       if (!last) {
-        fence_async_smem();
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&bars.s_ready[(c + 1) & 1]);
-        if (v == 0) GDN_TRACE(3, c);
+        if (!named_sync_and(1, 128, sr)) { ok = false; break; }
+        if (v == 0) GDN_TRACE(4, c);
       }
+    }
+    if (v == 0) {
+      // before the CTA retires: this thread's MMAs and TMA loads have landed (bounded; no-ops on
+      // the normal path)
+      umma_commit(&bars.drain[0]);
+      mbar_drain(&bars.drain[0], 0);
+      for (int c = max(0, qk_issued - kSlots); c < qk_issued; ++c)
+        mbar_drain(&bars.in_full[c % kSlots], (c / kSlots) & 1);
+      if (v_issued > 0) mbar_drain(&bars.v_full[(v_issued - 1) & 1], ((v_issued - 1) >> 1) & 1);
     }
   } else if (warp < 8) {
     // =========================================================== operand warps
+    // Each warp polls on its own (lane 0 tests, the warp follows): output pass of chunk co once
+    // T5(co) is done, decay sums of chunk cg (warp 4), read-out of chunk cr once T1(cr) is done.
     const int r = threadIdx.x - 128;  // TMEM lane / row owned by this thread
-    const uint32_t lane_base = tmem_addr(tbase, (warp & 3) * 32, 0);
-    bool ok = true;
-    for (int c = 0; ok && c < nchunks; ++c) {
-      ChunkParams& pc = params[c & 1];
-      // --- (1) decay prefix sums for chunk c (warp 4)
-      if (warp == 4) {
-        if (c >= 2 && !wait_c_warp(bars.da_done, c - 2, p.status, kDevTimeoutPipe)) { ok = false; break; }
-        const int n_valid = min(kC, len - c * kC);
+    const int wq = warp & 3;
+    const uint32_t lb = tmem_addr(tbase, wq * 32, 0);
+    float* Ls = reinterpret_cast<float*>(smem + kOffL);
+    uint8_t* stage = smem + kOffStage + wq * 2048;
+    int cr = 0, co = 0, cg = (warp == 4) ? 0 : N;
+    // decay inputs of chunk cg, two tokens per lane, loaded one chunk ahead (warp 4)
+    float ga = 0.f, gb = 0.f, ba = 0.f, bb = 0.f;
+    auto load_g = [&](int c) {
+      const int n_valid = min(kC, len - c * kC);
+      const int t0 = 2 * lane, t1 = 2 * lane + 1;
+      const size_t base = static_cast<size_t>(tok0 + c * kC);
+      ga = t0 < n_valid ? p.g[(base + t0) * p.hv + h] : 0.0f;
+      gb = t1 < n_valid ? p.g[(base + t1) * p.hv + h] : 0.0f;
+      ba = t0 < n_valid ? p.beta[(base + t0) * p.hv + h] : 0.0f;
+      bb = t1 < n_valid ? p.beta[(base + t1) * p.hv + h] : 0.0f;
+    };
+    if (warp == 4) load_g(0);
+    unsigned long long idle_since = 0;
+    uint32_t idle_polls = 0;
+    while (co < N) {
+      bool did = false;
+      // (1) output pass of chunk co
+      if (co < cr && __shfl_sync(0xffffffffu, lane == 0 ? test_c(bars.o_done, co) : false, 0)) {
+        tc_fence_after();
+        if (r == 0) GDN_TRACE(7, co);
+        uint32_t o[64];
+        tmem_ld64(lb + kColO, o);
+        tc_fence_before();
+        mbar_arrive(&bars.o_read[co & 1]);
+        const int nv = min(kC, len - co * kC);
+        __nv_bfloat16* dst = p.out + (static_cast<size_t>(tok0 + co * kC) * p.hv + h) * kD + wq * 32;
+        const size_t tstride = static_cast<size_t>(p.hv) * kD;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          // stage[i][v] for 32 tokens i, 16-byte chunks XOR-swizzled by (i >> 1) & 3
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            *reinterpret_cast<__nv_bfloat16*>(stage + i * 64 + ((((lane >> 3) ^ (i >> 1)) & 3) << 4) +
+                                              ((lane & 7) << 1)) = __float2bfloat16_rn(__uint_as_float(o[32 * hf + i]));
+          __syncwarp();
+          const int t = 32 * hf + lane;
+          if (t < nv) {
+            const uint8_t* src = stage + lane * 64;
+            uint4* g = reinterpret_cast<uint4*>(dst + t * tstride);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) g[j] = *reinterpret_cast<const uint4*>(src + (((j ^ (lane >> 1)) & 3) << 4));
+          }
+          __syncwarp();
+        }
+        if (r == 0) GDN_TRACE(8, co);
+        ++co;
+        did = true;
+      } else if (cg < N && cg <= co + 1) {
+        // (2) decay prefix sums of chunk cg (warp 4).  Its params slot held chunk cg-2, whose
+        //     last readers (Delta pass, state pass) finished before T5(cg-2) and so before the
+        //     output pass of cg-2 that this warp has done.
+        ChunkParams& pc = params[cg & 1];
+        const int n_valid = min(kC, len - cg * kC);
         const int t0 = 2 * lane, t1 = 2 * lane + 1;
-        const size_t base = static_cast<size_t>(tok0 + c * kC);
-        const float ga = t0 < n_valid ? p.g[(base + t0) * p.hv + h] : 0.0f;
-        const float gb = t1 < n_valid ? p.g[(base + t1) * p.hv + h] : 0.0f;
-        const float ba = t0 < n_valid ? p.beta[(base + t0) * p.hv + h] : 0.0f;
-        const float bb = t1 < n_valid ? p.beta[(base + t1) * p.hv + h] : 0.0f;
         float incl = ga + gb;  // inclusive scan of pair sums
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
@@ -448,35 +561,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           pc.n_valid = n_valid;
         }
         __syncwarp();
-        mbar_arrive(&bars.g_ready[c & 1]);
-        if (lane == 0) GDN_TRACE(18, c);
-      }
-      // --- (2a) QK / KK read-out: e^G-scaled Q (in place), L rows -> solve scratch; P row kept
-      //          in registers until the P tile is free
-      bool ready = wait_c_warp(bars.qk_done, c, p.status, kDevTimeoutMma);
-      if (ready) ready = wait_c_warp(bars.g_ready, c, p.status, kDevTimeoutPipe);
-      if (ready && c >= 1) ready = wait_c_warp(bars.w_done, c - 1, p.status, kDevTimeoutMma);  // T tiles free
-      if (!ready) { ok = false; break; }
-      tc_fence_after();
-      uint32_t prow[32];
-      if (r == 0) GDN_TRACE(4, c);
-      {
+        mbar_arrive(&bars.g_ready[cg & 1]);
+        if (lane == 0) GDN_TRACE(15, cg);
+        ++cg;
+        if (cg < N) load_g(cg);
+        did = true;
+      } else if (cr < N && cr <= co + 1 &&
+                 __shfl_sync(0xffffffffu, lane == 0 ? (test_c(bars.qk_done, cr) && test_c(bars.g_ready, cr)) : false,
+                             0)) {
+        // (3) read-out of chunk cr: P row (scale folded in), scale e^G Q in place, L row.  The P
+        //     slot was last read by T5(cr-2) (output pass cr-2 done); the L region by T2(cr-1),
+        //     which completed before T1(cr) was issued.
+        tc_fence_after();
+        if (r == 0) GDN_TRACE(5, cr);
+        const ChunkParams& pc = params[cr & 1];
         uint32_t row[64];
-        tmem_ld64(lane_base + kColQK, row);
-        if (r == 0) GDN_TRACE(22, c);
+        tmem_ld64(lb + kColQW, row);
         if (r < 64) {
           const int t = r;
           const float gt = pc.g2[t];
+          uint32_t prow[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int s0 = 2 * j, s1 = 2 * j + 1;
-            const float p0 = s0 <= t ? __uint_as_float(row[s0]) * ex2_approx(gt - pc.g2[s0]) : 0.0f;
-            const float p1 = s1 <= t ? __uint_as_float(row[s1]) * ex2_approx(gt - pc.g2[s1]) : 0.0f;
+            const float p0 = s0 <= t ? __uint_as_float(row[s0]) * ex2_approx(gt - pc.g2[s0]) * p.scale : 0.0f;
+            const float p1 = s1 <= t ? __uint_as_float(row[s1]) * ex2_approx(gt - pc.g2[s1]) * p.scale : 0.0f;
             prow[j] = pack_bf16x2(p0, p1);
           }
+          store_row_sw128(smem + kOffP + (cr & 1) * 8192, t, prow);
           // Q row t lives in rows 0..63 of the stacked slot, 2 boxes of 64 columns
-          uint8_t* slot = smem + ((c & 1) ? kOffSlot1 : kOffSlot0);
-          const float eg = pc.eg[t];
+          uint8_t* slot = smem + kOffSlots + (cr % kSlots) * kSlotBytes;
+          const float f = pc.eg[t] * p.scale;
 #pragma unroll
           for (int bx = 0; bx < 2; ++bx) {
 #pragma unroll
@@ -487,8 +602,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 __nv_bfloat162 b2 = *reinterpret_cast<__nv_bfloat162*>(&w[e]);
-                const float2 f = __bfloat1622float2(b2);
-                w[e] = pack_bf16x2(f.x * eg, f.y * eg);
+                const float2 fl = __bfloat1622float2(b2);
+                w[e] = pack_bf16x2(fl.x * f, fl.y * f);
               }
               *ptr = val;
             }
@@ -497,272 +612,224 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int t = r - 64;
           const float gt = pc.g2[t];
           const float bt = pc.beta[t];
+          float* lrow = Ls + t * kLds;
 #pragma unroll
-          for (int s = 0; s < 64; ++s)
-            scratch[s * 64 + t] = s < t ? bt * ex2_approx(gt - pc.g2[s]) * __uint_as_float(row[s]) : 0.0f;
+          for (int s4 = 0; s4 < 64; s4 += 4) {
+            float4 val;
+            val.x = s4 + 0 < t ? bt * ex2_approx(gt - pc.g2[s4 + 0]) * __uint_as_float(row[s4 + 0]) : 0.0f;
+            val.y = s4 + 1 < t ? bt * ex2_approx(gt - pc.g2[s4 + 1]) * __uint_as_float(row[s4 + 1]) : 0.0f;
+            val.z = s4 + 2 < t ? bt * ex2_approx(gt - pc.g2[s4 + 2]) * __uint_as_float(row[s4 + 2]) : 0.0f;
+            val.w = s4 + 3 < t ? bt * ex2_approx(gt - pc.g2[s4 + 3]) * __uint_as_float(row[s4 + 3]) : 0.0f;
+            *reinterpret_cast<float4*>(lrow + s4) = val;
+          }
         }
-      }
-      fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(&bars.qk_read[c & 1]);
-      if (r == 0) GDN_TRACE(5, c);
-      // --- (3) W pass: W^T (lane = key row k) -> -W as [k][t], hi and lo bf16 tiles
-      ready = wait_c_warp(bars.w_done, c, p.status, kDevTimeoutMma);
-      if (ready && c >= 1) ready = wait_c_warp(bars.delta, c - 1, p.status, kDevTimeoutMma);  // W tiles free
-      if (!ready) { ok = false; break; }
-      tc_fence_after();
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t row[32];
-        tmem_ld32(lane_base + kColW + 32 * half, row);
-        uint32_t hi[16], lo[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          split_pack(-__uint_as_float(row[2 * j]), -__uint_as_float(row[2 * j + 1]), hi[j], lo[j]);
-        store_half_row_sw128(smem + kOffWhi, r, half, hi);
-        store_half_row_sw128(smem + kOffWlo, r, half, lo);
-      }
-      fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(&bars.wneg[c & 1]);
-      if (r == 0) GDN_TRACE(6, c);
-      // --- (4) output pass of the previous chunk, then the P tile of this chunk (single buffer:
-      //         the previous chunk's P V MMA has completed once its output is ready)
-      if (c >= 1) {
-        if (!wait_c_warp(bars.o_done, c - 1, p.status, kDevTimeoutMma)) { ok = false; break; }
-        tc_fence_after();
-        output_pass(p, lane_base, tok0, len, c - 1, h, r);
-        if (r == 0) GDN_TRACE(7, c - 1);
+        fence_async_smem();
         tc_fence_before();
+        mbar_arrive(&bars.qk_read[cr & 1]);
+        if (r == 0) GDN_TRACE(6, cr);
+        ++cr;
+        did = true;
       }
-      // --- (5) T3b: O^T = S_hi (e^G Q)^T once all 128 threads have read the O region out and
-      //         the state copy of chunk c exists
-      if (!named_sync_and(2, 128, true)) { ok = false; break; }
-      if (r == 0 && wait_c(bars.s_ready, c, p.status, kDevTimeoutPipe)) {
-        tc_fence_after();
-        issue_t3b(tbase, smem, c);
-        umma_commit(&bars.t3b[c & 1]);
-        GDN_TRACE(15, c);
-      }
-      if (r < 64) store_row_sw128(smem + kOffP, r, prow);
-      fence_async_smem();
-      mbar_arrive(&bars.p_ready[c & 1]);
-      if (r == 0) GDN_TRACE(8, c);
-    }
-    if (ok && wait_c_warp(bars.o_done, nchunks - 1, p.status, kDevTimeoutMma)) {
-      tc_fence_after();
-      output_pass(p, lane_base, tok0, len, nchunks - 1, h, r);
-    }
-  } else if (warp < 10) {
-    // =========================================================== triangular solve
-    // That = (I + L)^-1, one column per thread (warps 8, 9), by 16-row blocks: for block B the
-    // thread starts from e_j, subtracts the contributions of the already-solved rows
-    // (left-looking, sum_{s < 16B} L[r][s] x_s) and finishes the block by right-looking forward
-    // substitution.  Only 16 accumulators are live; solved rows go to an fp32 column buffer in
-    // shared memory (each thread reads back only its own column).  A warp skips the blocks above
-    // its first column (x = 0 there).  Column j then becomes row j of the MN-major ([s][t]) tiles
-    // T = That diag(beta) and T diag(e^G), each as hi + lo.
-    const int tid = threadIdx.x - 256;
-    const int j = tid;                 // column
-    const int wfirst = tid & ~31;      // first column of this warp
-    float* xbuf = reinterpret_cast<float*>(smem + kOffTGhi);  // That[r][j] at xbuf[r * 64 + j]
-    bool ok = true;
-    for (int c = 0; ok && c < nchunks; ++c) {
-      const bool ready = wait_c(bars.qk_read, c, p.status, kDevTimeoutPipe);
-      // the two warps leave together or not at all (they meet at named barriers below)
-      if (!named_sync_and(1, 64, ready)) { ok = false; break; }
-      if (tid == 0) GDN_TRACE(9, c);
-      const ChunkParams& pc = params[c & 1];
-#pragma unroll
-      for (int B = 0; B < 4; ++B) {
-        float acc[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = (16 * B + i == j) ? 1.0f : 0.0f;
-        if (16 * B + 15 >= wfirst) {  // warp-uniform
-          // left-looking: rows of the previous blocks (x_s = 0 for s < j)
-#pragma unroll 2
-          for (int s0 = wfirst; s0 < 16 * B; ++s0) {
-            const float xs = xbuf[s0 * 64 + j];
-            const float4* lc = reinterpret_cast<const float4*>(scratch + s0 * 64 + 16 * B);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float4 l = lc[q];
-              acc[4 * q + 0] = fmaf(-l.x, xs, acc[4 * q + 0]);
-              acc[4 * q + 1] = fmaf(-l.y, xs, acc[4 * q + 1]);
-              acc[4 * q + 2] = fmaf(-l.z, xs, acc[4 * q + 2]);
-              acc[4 * q + 3] = fmaf(-l.w, xs, acc[4 * q + 3]);
-            }
+      if (did) {
+        idle_polls = 0;
+      } else if ((++idle_polls & 255u) != 0u) {
+        __nanosleep(64);
+      } else {
+        // every 256 empty polls: give up after kWaitTimeoutNs without progress, or as soon as
+        // another warp of the CTA has reported a timeout
+        const unsigned long long now = global_timer_ns();
+        if (idle_polls == 256u) idle_since = now;
+        const bool stop = cta_abort_flag() != 0u || now - idle_since > kWaitTimeoutNs;
+        if (__shfl_sync(0xffffffffu, stop, 0)) {
+          if (cta_abort_flag() == 0u && lane == 0) {
+            record_status(p.status, kDevTimeoutPipe);
+            cta_abort_flag() = 1u;
           }
-          // right-looking inside the block (L[r][t] = 0 for r <= t)
-#pragma unroll
-          for (int tt = 0; tt < 15; ++tt) {
-            const float xt = acc[tt];
-            const float* lc = scratch + (16 * B + tt) * 64 + 16 * B;
-#pragma unroll
-            for (int i4 = (tt + 1) & ~3; i4 < 16; i4 += 4) {
-              const float4 l = *reinterpret_cast<const float4*>(lc + i4);
-              acc[i4 + 0] = fmaf(-l.x, xt, acc[i4 + 0]);
-              acc[i4 + 1] = fmaf(-l.y, xt, acc[i4 + 1]);
-              acc[i4 + 2] = fmaf(-l.z, xt, acc[i4 + 2]);
-              acc[i4 + 3] = fmaf(-l.w, xt, acc[i4 + 3]);
-            }
-          }
+          break;
         }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) xbuf[(16 * B + i) * 64 + j] = acc[i];
-      }
-      float x[64];
-#pragma unroll
-      for (int r = 0; r < 64; ++r) x[r] = xbuf[r * 64 + j];
-      named_sync(1, 64);  // L and every column are in registers: the tiles may overwrite both
-      const float w0 = pc.beta[j];
-      const float w1 = w0 * pc.eg[j];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {  // q = 0: T, q = 1: T diag(e^G)
-        const float w = q ? w1 : w0;
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) split_pack(x[32 * hf + 2 * i] * w, x[32 * hf + 2 * i + 1] * w, hi[i], lo[i]);
-          store_half_row_sw128(smem + (q ? kOffTGhi : kOffThi), j, hf, hi);
-          store_half_row_sw128(smem + (q ? kOffTGlo : kOffTlo), j, hf, lo);
-        }
-      }
-      fence_async_smem();
-      if (tid == 0) GDN_TRACE(10, c);
-      mbar_arrive(&bars.prep1[c & 1]);
-    }
-  } else if (warp == kWarpTma) {
-    // =========================================================== TMA producer
-    if (lane == 0) {
-      tma_prefetch_desc(&map_q);
-      tma_prefetch_desc(&map_k);
-      tma_prefetch_desc(&map_v);
-      int issued = 0;
-      for (int c = 0; c < nchunks; ++c) {
-        const int row = tok0 + c * kC;
-        // the slot of chunk c-2 is free once its state pass ran: T1-T4 and T3b have completed
-        if (c >= 2 && !wait_c(bars.s_ready, c - 1, p.status, kDevTimeoutPipe)) break;
-        uint8_t* slot = smem + ((c & 1) ? kOffSlot1 : kOffSlot0);
-        mbar_arrive_expect_tx(&bars.in_full[c & 1], kSlotBytes);
-        GDN_TRACE(17, c);
-        for (int bx = 0; bx < 2; ++bx) {
-          tma_load_3d(slot + bx * 16384, &map_q, &bars.in_full[c & 1], bx * 64, kh, row);
-          tma_load_3d(slot + bx * 16384 + 8192, &map_k, &bars.in_full[c & 1], bx * 64, kh, row);
-        }
-        if (c >= 1 && !wait_c(bars.v_free, c - 1, p.status, kDevTimeoutPipe)) break;
-        mbar_arrive_expect_tx(&bars.v_full[c & 1], 16384);
-        for (int bx = 0; bx < 2; ++bx)
-          tma_load_3d(smem + kOffV + bx * 8192, &map_v, &bars.v_full[c & 1], bx * 64, h, row);
-        issued = c + 1;
-      }
-      // before the CTA retires, let the last loads land (bounded; a no-op on the normal path)
-      for (int c = max(0, issued - 2); c < issued; ++c) {
-        mbar_drain(&bars.in_full[c & 1], (c >> 1) & 1);
-        mbar_drain(&bars.v_full[c & 1], (c >> 1) & 1);
       }
     }
   } else {
-    // =========================================================== MMA issuer (polling)
-    // Groups per chunk c (the state-dependent groups T3a/T4 are issued by the state-chain warps,
-    // T3b by the operand warps):
-    //   T1  [Q;K] K^T                                                   -> QK region
-    //   T2  W^T = K^T (TG_hi + TG_lo)^T ; Delta^T = V^T (T_hi + T_lo)^T  -> W region, X slot
-    //   T5  O^T += Delta^T P^T
-    // This thread polls the hand-off barriers (non-blocking) and issues whichever group is ready.
-    if (lane == 0 && nchunks > 0) {
-      const uint32_t id_qk = make_idesc(128, 64, 1, 0, 0);    // [Q;K] K^T
-      const uint32_t id_mnmn = make_idesc(128, 64, 1, 1, 1);  // A MN-major (K^T, V^T), B MN-major (T tiles [s][t])
-      const uint32_t id_dp = make_idesc(128, 64, 1, 0, 0);    // A TMEM, B K-major (P [t][s])
-      const uint32_t a_thi = smem_u32(smem + kOffThi), a_tlo = smem_u32(smem + kOffTlo);
-      const uint32_t a_tghi = smem_u32(smem + kOffTGhi), a_tglo = smem_u32(smem + kOffTGlo);
-      const uint32_t a_v = smem_u32(smem + kOffV), a_p = smem_u32(smem + kOffP);
-      int n1 = 0, n2 = 0, n5 = 0;
-      const int N = nchunks;
-      unsigned long long idle_since = 0;
-      uint32_t idle_polls = 0;
-      while (n5 < N) {
-        bool issued = false;
-        if (n5 < n2 && test_c(bars.t3b, n5) && test_c(bars.da_done, n5) && test_c(bars.p_ready, n5)) {
-          // T5: O^T += Delta^T P^T
-          const int c = n5;
-          tc_fence_after();
-          const uint32_t colx = (c & 1) ? kColX1 : kColX0;
+    // =========================================================== triangular solve and W
+    // X = (I + L)^-1 by 16x16 blocks: the four diagonal blocks by forward substitution (one
+    // column per thread), then block rows i = 1..3 as X[i, <i] = -D_i (L[i, <i] X[<i, <i]).
+    // X's diagonal blocks hold explicit zeros above the diagonal; the blocks above the block
+    // diagonal are never read.
+    const int tid = threadIdx.x - 256;
+    const uint32_t lb = tmem_addr(tbase, (warp & 3) * 32, 0);
+    float* Ls = reinterpret_cast<float*>(smem + kOffL);
+    float* Xs = reinterpret_cast<float*>(smem + kOffX);
+    bool ok = true;
+    if (tid == 0) {
+      ok = mbar_wait(&bars.in_full[0], 0, p.status, kDevTimeoutTma);
+      if (ok) {
+        tc_fence_after();
+        issue_t1(tbase, smem, 0);
+        umma_commit(&bars.qk_done[0]);
+        GDN_TRACE(14, 0);
+      }
+    }
+    for (int c = 0; c < N; ++c) {
+      const bool ready = wait_c(bars.qk_read, c, p.status, kDevTimeoutPipe);
+      if (!named_sync_and(3, 128, ready && ok)) { ok = false; break; }
+      if (tid == 0) GDN_TRACE(9, c);
+      // --- diagonal blocks D_b = (I + L_bb)^-1, column j per thread
+      if (tid < 64) {
+        const int b = tid >> 4, j = tid & 15;
+        const float* lb16 = Ls + 16 * b * kLds + 16 * b;
+        float acc[16];
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16_ts(tbase + kColO, tbase + colx + 8 * kk, make_sdesc_sw128(a_p + kk * 32, 16, 1024), id_dp, 1u);
-          umma_commit(&bars.o_done[c & 1]);
-          GDN_TRACE(16, c);
-          ++n5;
-          issued = true;
-        } else if (n2 < n1 && n2 < n5 + 2 && test_c(bars.prep1, n2) && test_c(bars.v_full, n2) &&
-                   (n2 == 0 || test_c(bars.wneg, n2 - 1)) && (n2 < 2 || test_c(bars.snew, n2 - 2))) {
-          // T2: W^T = K^T (TG_hi + TG_lo)^T ; Delta^T = V^T T_hi^T + V^T T_lo^T
-          // (the X slot of chunk c was last read by T4(c-2) and T5(c-2))
-          const int c = n2;
-          tc_fence_after();
-          const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
-          const uint32_t colx = (c & 1) ? kColX1 : kColX0;
+        for (int i = 0; i < 16; ++i) acc[i] = (i == j) ? 1.0f : 0.0f;
 #pragma unroll
-          for (int part = 0; part < 2; ++part)
+        for (int s = 0; s < 15; ++s) {
+          const float xs = acc[s];
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16_ss(tbase + kColW, make_sdesc_sw128(slot + 8192 + kk * 2048, 16384, 1024),
-                           make_sdesc_sw128((part ? a_tglo : a_tghi) + kk * 2048, 16384, 1024), id_mnmn,
-                           (part > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-          for (int part = 0; part < 2; ++part)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16_ss(tbase + colx, make_sdesc_sw128(a_v + kk * 2048, 8192, 1024),
-                           make_sdesc_sw128((part ? a_tlo : a_thi) + kk * 2048, 16384, 1024), id_mnmn,
-                           (part > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&bars.w_done[c & 1]);
-          umma_commit(&bars.v_free[c & 1]);
-          GDN_TRACE(12, c);
-          ++n2;
-          issued = true;
-        } else if (n1 < N && n1 <= n2 + 1 && test_c(bars.in_full, n1) && (n1 == 0 || test_c(bars.qk_read, n1 - 1))) {
-          // T1: [Q;K] K^T
-          const int c = n1;
-          tc_fence_after();
-          const uint32_t slot = smem_u32(smem + ((c & 1) ? kOffSlot1 : kOffSlot0));
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_bf16_ss(tbase + kColQK, kmaj_desc(slot, kk), kmaj_desc(slot + 8192, kk), id_qk, kk > 0 ? 1u : 0u);
-          umma_commit(&bars.qk_done[c & 1]);
-          GDN_TRACE(11, c);
-          ++n1;
-          issued = true;
+          for (int i = s + 1; i < 16; ++i) acc[i] = fmaf(-lb16[i * kLds + s], xs, acc[i]);
         }
-        if (issued) {
-          idle_polls = 0;
-        } else if ((++idle_polls & 255u) != 0u) {
-          __nanosleep(32);  // leave issue slots and shared-memory bandwidth to the other warps
-        } else {
-          // every 256 empty polls: give up after kWaitTimeoutNs without progress, or as soon as
-          // another warp of the CTA has reported a timeout
-          const unsigned long long now = global_timer_ns();
-          if (idle_polls == 256u) idle_since = now;
-          if (cta_abort_flag() != 0u) break;
-          if (now - idle_since > kWaitTimeoutNs) {
-            record_status(p.status, kDevTimeoutPipe);
-            cta_abort_flag() = 1u;
-            break;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) Xs[(16 * b + i) * kLds + 16 * b + j] = acc[i];
+      }
+      named_sync(3, 128);
+      // --- block rows 1..3; thread = (row rr of the block row, column pair cg of each block)
+      {
+        const int rr = tid >> 3, cg = tid & 7;
+#pragma unroll
+        for (int i = 1; i < 4; ++i) {
+          float2 y[3];
+          const float* lrow = Ls + (16 * i + rr) * kLds;
+#pragma unroll
+          for (int cb = 0; cb < i; ++cb) {
+            const int c0 = 16 * cb + 2 * cg;
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int k4 = 16 * cb; k4 < 16 * i; k4 += 4) {
+              const float4 l = *reinterpret_cast<const float4*>(lrow + k4);
+              const float2 x0 = *reinterpret_cast<const float2*>(Xs + (k4 + 0) * kLds + c0);
+              const float2 x1 = *reinterpret_cast<const float2*>(Xs + (k4 + 1) * kLds + c0);
+              const float2 x2 = *reinterpret_cast<const float2*>(Xs + (k4 + 2) * kLds + c0);
+              const float2 x3 = *reinterpret_cast<const float2*>(Xs + (k4 + 3) * kLds + c0);
+              a0 = fmaf(l.x, x0.x, a0);
+              a1 = fmaf(l.x, x0.y, a1);
+              a0 = fmaf(l.y, x1.x, a0);
+              a1 = fmaf(l.y, x1.y, a1);
+              a0 = fmaf(l.z, x2.x, a0);
+              a1 = fmaf(l.z, x2.y, a1);
+              a0 = fmaf(l.w, x3.x, a0);
+              a1 = fmaf(l.w, x3.y, a1);
+            }
+            y[cb] = make_float2(a0, a1);
+          }
+          // Y = L[i, <i] X[<i, <i] goes to X's block row i (not read by this step)
+#pragma unroll
+          for (int cb = 0; cb < i; ++cb) *reinterpret_cast<float2*>(Xs + (16 * i + rr) * kLds + 16 * cb + 2 * cg) = y[cb];
+          named_sync(3, 128);
+          float dr[16];
+#pragma unroll
+          for (int m4 = 0; m4 < 16; m4 += 4) {
+            const float4 d4 = *reinterpret_cast<const float4*>(Xs + (16 * i + rr) * kLds + 16 * i + m4);
+            dr[m4] = d4.x;
+            dr[m4 + 1] = d4.y;
+            dr[m4 + 2] = d4.z;
+            dr[m4 + 3] = d4.w;
+          }
+          float2 z[3];
+#pragma unroll
+          for (int cb = 0; cb < i; ++cb) {
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+              const float2 ym = *reinterpret_cast<const float2*>(Xs + (16 * i + m) * kLds + 16 * cb + 2 * cg);
+              a0 = fmaf(dr[m], ym.x, a0);
+              a1 = fmaf(dr[m], ym.y, a1);
+            }
+            z[cb] = make_float2(-a0, -a1);
+          }
+          named_sync(3, 128);
+#pragma unroll
+          for (int cb = 0; cb < i; ++cb) *reinterpret_cast<float2*>(Xs + (16 * i + rr) * kLds + 16 * cb + 2 * cg) = z[cb];
+          named_sync(3, 128);
+        }
+      }
+      if (tid == 0) GDN_TRACE(10, c);
+      // --- T = X diag(beta) and T diag(e^G) as MN-major hi/lo tiles (row s, tokens t of one
+      //     half).  The T tiles and the W tiles were last read by T3(c-1).
+      const bool free_tiles = (c == 0) || wait_c(bars.x_ready, c - 1, p.status, kDevTimeoutMma);
+      if (!named_sync_and(3, 128, free_tiles)) { ok = false; break; }
+      {
+        const ChunkParams& pc = params[c & 1];
+        const int s = tid & 63, half = tid >> 6;
+        float xv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int t = 32 * half + i;
+          xv[i] = t >= s ? Xs[t * kLds + s] : 0.0f;
+        }
+        const float w0 = pc.beta[s];
+        const float w1 = w0 * pc.eg[s];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {  // q = 0: T, q = 1: T diag(e^G) (over the dead L)
+          const float w = q ? w1 : w0;
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) split_pack(xv[2 * i] * w, xv[2 * i + 1] * w, hi[i], lo[i]);
+          uint8_t* tile = smem + (q ? kOffL : kOffT);
+          store_half_row_sw128(tile, s, half, hi);
+          store_half_row_sw128(tile + 8192, s, half, lo);
+        }
+      }
+      fence_async_smem();
+      named_sync(3, 128);
+      if (tid == 0) {
+        tc_fence_after();
+        issue_t2(tbase, smem, c);
+        umma_commit(&bars.w_done[c & 1]);
+        GDN_TRACE(12, c);
+      }
+      // --- W pass: W^T (lane = key row k) -> -W as [k][t], hi and lo tiles
+      const bool wready = wait_c_warp(bars.w_done, c, p.status, kDevTimeoutMma);
+      if (wready) {
+        tc_fence_after();
+        uint32_t row[64];
+        tmem_ld64(lb + kColQW, row);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            split_pack(-__uint_as_float(row[32 * half + 2 * j]), -__uint_as_float(row[32 * half + 2 * j + 1]), hi[j],
+                       lo[j]);
+          store_half_row_sw128(smem + kOffW, tid, half, hi);
+          store_half_row_sw128(smem + kOffW + 16384, tid, half, lo);
+        }
+        fence_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bars.w_ready[c & 1]);
+      }
+      // every thread has read W^T out of the QW region: T1(c+1) may overwrite it
+      if (!named_sync_and(3, 128, wready)) { ok = false; break; }
+      if (tid == 0) {
+        GDN_TRACE(13, c);
+        const int n = c + 1;
+        if (n < N) {
+          ok = mbar_wait(&bars.in_full[n % kSlots], (n / kSlots) & 1, p.status, kDevTimeoutTma);
+          if (ok) {
+            tc_fence_after();
+            issue_t1(tbase, smem, n);
+            umma_commit(&bars.qk_done[n & 1]);
+            GDN_TRACE(14, n);
           }
         }
       }
-      // every MMA issued by this thread completes before TMEM is released (bounded)
-      umma_commit(&drain_bar);
-      mbar_drain(&drain_bar, 0);
     }
-    __syncwarp();
+    if (tid == 0) {
+      umma_commit(&bars.drain[1]);
+      mbar_drain(&bars.drain[1], 0);
+    }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpMma) {
+  if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tbase, 512);
   }
