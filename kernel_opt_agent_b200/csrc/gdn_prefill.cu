@@ -24,13 +24,14 @@
 // chain is sequential: Delta(c) -> S(c+1) -> Delta(c+1).  Everything that does not depend on the
 // state (decay sums, Q K^T / K K^T, the triangular solve, W) is prepared for chunk c+1 while the
 // chain works on chunk c.  Warp roles (384 threads):
-//   warps 0-3   state chain, thread = value row: issues the state-dependent MMAs, Delta pass
-//               (Delta -> bf16 operands in TMEM), state pass (S -> hi/lo copies, decay for the
-//               next chunk), initial / final state; thread 0 also issues every TMA load
-//   warps 4-7   operands, each warp polling on its own: decay prefix sums (warp 4), Q K^T / K K^T
-//               read-out (P tile, e^G-scaled Q in place, rows of L), output pass (O^T -> global)
-//   warps 8-11  triangular solve (16x16 blocks), T / T diag(e^G) tiles, W pass (W^T -> -W
-//               tiles); thread 0 issues the preparation MMAs (Q K^T, W)
+//   warps 0-3   state chain, thread = value row: Delta pass (Delta -> bf16 operands in TMEM),
+//               state pass (S -> hi/lo copies, decay for the next chunk), initial / final
+//               state; thread 0 issues the state-dependent MMAs and every TMA load
+//   warps 4-7   operands, each warp polling on its own: K K^T / Q K^T read-out (warps 4-5: rows
+//               of L; warps 6-7: P tile and e^G-scaled Q in place), output pass (O^T ->
+//               global), decay prefix sums (warp 7)
+//   warps 8-11  triangular solve, T / T diag(e^G) tiles, W pass (W^T -> -W tiles); thread 0
+//               issues the preparation MMAs (Q K^T, W, T V)
 // Hand-off barriers are two-slot arrays indexed by chunk parity (the Q/K ring has three).  Every
 // producer of chunk c+2's event causally follows every waiter of chunk c's event, so no waiter
 // can fall two phases behind (argued next to each barrier below).  All waits are bounded.
@@ -54,14 +55,16 @@ constexpr int kSlots = 3;  // Q/K chunk tiles in flight
 constexpr uint32_t kColS = 0;      // state S[v][k] fp32, 128 cols
 constexpr uint32_t kColShi = 128;  // state hi copy, bf16 pairs along k, 64 cols
 constexpr uint32_t kColSlo = 192;  // state lo copy
-constexpr uint32_t kColX = 256;    // Delta^T fp32 (64 cols), then Delta'hi | Delta'lo | Delta bf16 (32 each)
-constexpr uint32_t kColO = 352;    // O^T fp32, 64 cols
-constexpr uint32_t kColQW = 416;   // Q K^T (lanes 0-63) / K K^T (lanes 64-127), later W^T (lane = key row)
+constexpr uint32_t kColX = 256;    // Delta^T as two fp32 halves (64 + 64 cols, summed by the Delta pass),
+                                   // then Delta'hi | Delta'lo | Delta bf16 (32 cols each)
+constexpr uint32_t kColO = 384;    // O^T fp32, 64 cols
+constexpr uint32_t kColQW = 448;   // K K^T (lanes 0-63) / Q K^T (lanes 64-127), later W^T (lane = key row)
 
 // shared memory layout (bytes; every MMA tile starts on a 1024-byte boundary)
-constexpr int kSlotBytes = 32768;                  // stacked [Q;K] chunk tile: 2 boxes of 128 rows x 128 B
-constexpr int kOffSlots = 0;                       //   rows 0-63 of a box: Q (scaled in place to scale e^G Q)
-                                                   //   rows 64-127: K
+constexpr int kSlotBytes = 32768;                  // stacked [K;Q] chunk tile: 2 boxes of 128 rows x 128 B
+constexpr int kOffSlots = 0;
+constexpr int kKRows = 0;                          //   rows 0-63 of a box: K
+constexpr int kQRows = 8192;                       //   rows 64-127: Q (scaled in place to scale e^G Q)
 constexpr int kOffV = kSlots * kSlotBytes;         // V chunk tile: 2 boxes of 64 rows x 128 B
 constexpr int kOffP = kOffV + 16384;               // P [t][s] bf16, 2 x 8 KB (chunk parity)
 constexpr int kOffT = kOffP + 16384;               // T hi [s][t] (8 KB), T lo (8 KB)
@@ -70,8 +73,7 @@ constexpr int kOffL = kOffT + 16384;               // L fp32 [t][s] (row stride 
                                                    //   solve: T diag(e^G) hi [s][t], lo (8 KB each)
 constexpr int kOffX = kOffL + 64 * kLds * 4;       // (I + L)^-1 fp32 [t][s] (row stride kLds)
 constexpr int kOffW = kOffX + 64 * kLds * 4;       // -W hi as [k][t] (16 KB), -W lo (16 KB)
-constexpr int kOffStage = kOffW + 32768;           // output staging, 4 warps x 32 tokens x 64 B
-constexpr int kOffParams = kOffStage + 8192;
+constexpr int kOffParams = kOffW + 32768;
 constexpr int kParamsBytes = 1280;
 constexpr int kSmemBytes = kOffParams + 2 * kParamsBytes;
 static_assert(kOffL % 1024 == 0 && kOffX % 1024 == 0 && kOffW % 1024 == 0, "tile alignment");
@@ -102,19 +104,23 @@ struct Params {
 };
 
 // Hand-off barriers.  Event of chunk c lives in slot c & 1 (in_full: c % 3) and completes the
-// slot's (c >> 1)-th (c / 3-th) phase.
+// slot's (c >> 1)-th (c / 3-th) phase.  For each: who waits, and why the event of chunk c+2
+// cannot complete before every waiter has seen chunk c's.
 struct Barriers {
-  uint64_t in_full[kSlots];  // TMA Q/K(c) landed.   waiter: solve t0 (T1).  next phase needs T4(c)
-  uint64_t v_full[2];        // TMA V(c) landed.     waiter: chain t0 (T3).  V(c+2) issued after T3(c+1)
-  uint64_t qk_done[2];       // T1(c) complete.      waiters: operand warps; T1(c+2) follows readout(c+1)
-  uint64_t qk_read[2];       // read-out(c) done (128). waiters: solve; readout(c+2) follows T1(c+2) <- solve(c+1)
-  uint64_t g_ready[2];       // decay sums(c) (32).  waiters: operand warps, chain; scan(c+2) follows output(c)
-  uint64_t w_done[2];        // T2(c) complete.      waiters: solve; T2(c+2) follows their W pass(c+1)
-  uint64_t w_ready[2];       // W/T tiles(c) (128).  waiter: chain t0; W pass(c+2) follows T3(c+1)
-  uint64_t x_ready[2];       // T3(c) complete.      waiters: chain, solve; T3(c+2) follows both
-  uint64_t s_new[2];         // T3b(c), T4(c) complete. waiters: chain
-  uint64_t o_done[2];        // T5(c) complete.      waiters: operand warps, chain t0
-  uint64_t o_read[2];        // O(c) read out (128). waiter: chain t0 (T3b(c+1))
+  uint64_t in_full[kSlots];  // TMA Q/K(c).          solve t0 (T1).          Q/K(c+3) is loaded after T4(c)
+  uint64_t v_full[2];        // TMA V(c).            solve t0 (TV).          V(c+2) is loaded after TV(c+1)
+  uint64_t qk_done[2];       // T1(c).               operand warps.          T1(c+2) follows their read-out(c+1)
+  uint64_t qk_ld[2];         // QK(c) loaded (128).  solve t0 (T2).          read-out(c+2) follows T2(c+1)
+  uint64_t l_ready[2];       // L(c) rows (64).      solve.                  read-out(c+2) follows T1(c+2) <- solve(c+1)
+  uint64_t pq_ready[2];      // P(c), e^G Q (64).    chain t0 (T3b, T5).     read-out(c+2) follows output pass(c) <- T5(c)
+  uint64_t g_ready[2];       // decay sums(c) (32).  operand warps, chain.   scan(c+2) follows output pass(c)
+  uint64_t w_done[2];        // T2(c).               solve.                  T2(c+2) follows their W pass(c+1)
+  uint64_t w_ready[2];       // W/T tiles(c) (128).  chain t0 (state terms). W pass(c+2) follows x_ready(c+1)
+  uint64_t tv_done[2];       // TV(c).               chain t0.               TV(c+2) follows o_done(c+1)
+  uint64_t x_ready[2];       // state terms(c).      chain, solve.           state terms(c+2) follow both
+  uint64_t s_new[2];         // T4(c).               chain.
+  uint64_t o_done[2];        // T3b(c), T5(c).       operand warps, chain, solve t0.  T5(c+2) follows all
+  uint64_t o_read[2];        // O(c) read (128).     chain t0 (T3b(c+1)).    output pass(c+2) follows T5(c+2)
   uint64_t drain[2];         // retirement of the two MMA-issuing threads
 };
 
@@ -126,16 +132,22 @@ __device__ __forceinline__ bool test_c(uint64_t* bars, int c) { return mbar_test
 __device__ __forceinline__ bool wait_c_warp(uint64_t* bars, int c, uint32_t* status, uint32_t code) {
   return __all_sync(0xffffffffu, wait_c(bars, c, status, code));
 }
+// The whole warp arrives once (lane 0, count 32) after its lanes' prior writes are ordered by
+// __syncwarp.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31u) == 0u) mbar_arrive_count(bar, 32);
+}
 
-// Optional phase trace (build with -DTOKMIX_GDN_TRACE): %globaltimer stamps of CTA 0, indexed
+// Optional phase trace (build with -DTOKMIX_GDN_TRACE): SM clock stamps of CTA 0, indexed
 // by event and chunk, read back with tokmix_gdn_trace_read().  Compiled out otherwise.
 #ifdef TOKMIX_GDN_TRACE
 constexpr int kTraceChunks = 64;
-constexpr int kTraceEvents = 24;
+constexpr int kTraceEvents = 48;
 __device__ unsigned long long g_trace[kTraceEvents * kTraceChunks];
-#define GDN_TRACE(ev, c)                                                          \
-  do {                                                                            \
-    if (blockIdx.x == 0 && (c) < kTraceChunks) g_trace[(ev) * kTraceChunks + (c)] = global_timer_ns(); \
+#define GDN_TRACE(ev, c)                                                                          \
+  do {                                                                                            \
+    if (blockIdx.x == 0 && (c) < kTraceChunks) g_trace[(ev) * kTraceChunks + (c)] = clock64();   \
   } while (0)
 #else
 #define GDN_TRACE(ev, c) \
@@ -191,19 +203,19 @@ __device__ __forceinline__ uint32_t slot_addr(const uint8_t* smem, int c) {
   return smem_u32(smem + kOffSlots + (c % kSlots) * kSlotBytes);
 }
 
-// T1  [Q;K] K^T   (M=128 rows of the stacked tile, N=64 keys s, K=128)
+// T1  [K;Q] K^T   (M=128 rows of the stacked tile, N=64 keys s, K=128)
 __device__ __forceinline__ void issue_t1(uint32_t tbase, const uint8_t* smem, int c) {
   const uint32_t id = make_idesc(128, 64, 1, 0, 0);
   const uint32_t slot = slot_addr(smem, c);
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
-    umma_bf16_ss(tbase + kColQW, kmaj_desc(slot, kk), kmaj_desc(slot + 8192, kk), id, kk > 0 ? 1u : 0u);
+    umma_bf16_ss(tbase + kColQW, kmaj_desc(slot, kk), kmaj_desc(slot + kKRows, kk), id, kk > 0 ? 1u : 0u);
 }
 
 // T2  W^T = K^T (TG_hi + TG_lo)^T   (M=128 k, N=64 t, K=64 s; both operands MN-major)
 __device__ __forceinline__ void issue_t2(uint32_t tbase, const uint8_t* smem, int c) {
   const uint32_t id = make_idesc(128, 64, 1, 1, 1);
-  const uint32_t kt = slot_addr(smem, c) + 8192;
+  const uint32_t kt = slot_addr(smem, c) + kKRows;
   const uint32_t tg = smem_u32(smem + kOffL);
 #pragma unroll
   for (int part = 0; part < 2; ++part)
@@ -213,26 +225,28 @@ __device__ __forceinline__ void issue_t2(uint32_t tbase, const uint8_t* smem, in
                    make_sdesc_sw128(tg + part * 8192 + kk * 2048, 16384, 1024), id, (part > 0 || kk > 0) ? 1u : 0u);
 }
 
-// T3  Delta^T = V^T (T_hi + T_lo)^T + S_hi (-W_hi)^T + S_lo (-W_hi)^T + S_hi (-W_lo)^T
-//     (M=128 v, N=64 t; the state terms take S from TMEM)
-__device__ __forceinline__ void issue_t3(uint32_t tbase, const uint8_t* smem) {
-  const uint32_t id_v = make_idesc(128, 64, 1, 1, 1);  // A = V^T MN-major, B = T [s][t] MN-major
-  const uint32_t id_s = make_idesc(128, 64, 1, 0, 1);  // A = S (TMEM), B = -W [k][t] MN-major
-  const uint32_t a_v = smem_u32(smem + kOffV), a_t = smem_u32(smem + kOffT), a_w = smem_u32(smem + kOffW);
+// TV  [U_hi^T | U_lo^T] = V^T [T_hi | T_lo]^T   (M=128 v, N=128 (two 64-token halves), K=64 s)
+__device__ __forceinline__ void issue_tv(uint32_t tbase, const uint8_t* smem) {
+  const uint32_t id = make_idesc(128, 128, 1, 1, 1);  // A = V^T MN-major, B = T [s][t] MN-major, 2 chunks
+  const uint32_t a_v = smem_u32(smem + kOffV), a_t = smem_u32(smem + kOffT);
 #pragma unroll
-  for (int part = 0; part < 2; ++part)
+  for (int kk = 0; kk < 4; ++kk)
+    umma_bf16_ss(tbase + kColX, make_sdesc_sw128(a_v + kk * 2048, 8192, 1024),
+                 make_sdesc_sw128(a_t + kk * 2048, 8192, 1024), id, kk > 0 ? 1u : 0u);
+}
+
+// state terms  X += S_hi [-W_hi | -W_lo]^T  (N=128) ;  X[:, 0:64] += S_lo (-W_hi)^T  (N=64)
+//   (M=128 v, K=128 k; A = S from TMEM, B = -W [k][t] MN-major, hi and lo tiles 16 KB apart)
+__device__ __forceinline__ void issue_state_terms(uint32_t tbase, const uint8_t* smem) {
+  const uint32_t id128 = make_idesc(128, 128, 1, 0, 1);
+  const uint32_t id64 = make_idesc(128, 64, 1, 0, 1);
+  const uint32_t a_w = smem_u32(smem + kOffW);
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
-      umma_bf16_ss(tbase + kColX, make_sdesc_sw128(a_v + kk * 2048, 8192, 1024),
-                   make_sdesc_sw128(a_t + part * 8192 + kk * 2048, 16384, 1024), id_v, (part > 0 || kk > 0) ? 1u : 0u);
+  for (int kk = 0; kk < 8; ++kk)
+    umma_bf16_ts(tbase + kColX, tbase + kColShi + 8 * kk, make_sdesc_sw128(a_w + kk * 2048, 16384, 1024), id128, 1u);
 #pragma unroll
-  for (int term = 0; term < 3; ++term) {
-    const uint32_t sa = tbase + (term == 1 ? kColSlo : kColShi);
-    const uint32_t wb = a_w + (term == 2 ? 16384 : 0);
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-      umma_bf16_ts(tbase + kColX, sa + 8 * kk, make_sdesc_sw128(wb + kk * 2048, 16384, 1024), id_s, 1u);
-  }
+  for (int kk = 0; kk < 8; ++kk)
+    umma_bf16_ts(tbase + kColX, tbase + kColSlo + 8 * kk, make_sdesc_sw128(a_w + kk * 2048, 16384, 1024), id64, 1u);
 }
 
 // T3b  O^T = S_hi (scale e^G Q)^T   (M=128 v, N=64 t, K=128 k; A from TMEM)
@@ -241,13 +255,13 @@ __device__ __forceinline__ void issue_t3b(uint32_t tbase, const uint8_t* smem, i
   const uint32_t slot = slot_addr(smem, c);
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
-    umma_bf16_ts(tbase + kColO, tbase + kColShi + 8 * kk, kmaj_desc(slot, kk), id, kk > 0 ? 1u : 0u);
+    umma_bf16_ts(tbase + kColO, tbase + kColShi + 8 * kk, kmaj_desc(slot + kQRows, kk), id, kk > 0 ? 1u : 0u);
 }
 
 // T4  S += Delta'_hi^T K + Delta'_lo^T K   (M=128 v, N=128 k, K=64 t; A from TMEM)
 __device__ __forceinline__ void issue_t4(uint32_t tbase, const uint8_t* smem, int c) {
   const uint32_t id = make_idesc(128, 128, 1, 0, 1);
-  const uint32_t kt = slot_addr(smem, c) + 8192;
+  const uint32_t kt = slot_addr(smem, c) + kKRows;
 #pragma unroll
   for (int part = 0; part < 2; ++part)
 #pragma unroll
@@ -291,7 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* all = reinterpret_cast<uint64_t*>(&bars);
     for (int i = 0; i < static_cast<int>(sizeof(Barriers) / 8); ++i) mbar_init(&all[i], 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars.qk_read[i], 128);
+      mbar_init(&bars.qk_ld[i], 128);
+      mbar_init(&bars.l_ready[i], 64);
+      mbar_init(&bars.pq_ready[i], 64);
       mbar_init(&bars.g_ready[i], 32);
       mbar_init(&bars.w_ready[i], 128);
       mbar_init(&bars.o_read[i], 128);
@@ -328,8 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* slot = smem + kOffSlots + s * kSlotBytes;
       mbar_arrive_expect_tx(&bars.in_full[s], kSlotBytes);
       for (int bx = 0; bx < 2; ++bx) {
-        tma_load_3d(slot + bx * 16384, &map_q, &bars.in_full[s], bx * 64, kh, tok0 + c * kC);
-        tma_load_3d(slot + bx * 16384 + 8192, &map_k, &bars.in_full[s], bx * 64, kh, tok0 + c * kC);
+        tma_load_3d(slot + bx * 16384 + kQRows, &map_q, &bars.in_full[s], bx * 64, kh, tok0 + c * kC);
+        tma_load_3d(slot + bx * 16384 + kKRows, &map_k, &bars.in_full[s], bx * 64, kh, tok0 + c * kC);
       }
       qk_issued = c + 1;
     };
@@ -374,46 +390,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     ok = named_sync_and(1, 128, ok);
     for (int c = 0; ok && c < N; ++c) {
-      // --- (thread 0) T3 as soon as the W/T tiles and V of chunk c exist and T5(c-1) has read
-      //     the X region; then T3b once the output pass has read O(c-1)
+      // --- (thread 0) state terms once W(c) exists and T V(c) is in the X region
+      //     (every exit from this loop goes through a named_sync_and, so the four warps leave together)
       if (v == 0) {
-        bool r = wait_c(bars.w_ready, c, p.status, kDevTimeoutPipe) &&
-                 wait_c(bars.v_full, c, p.status, kDevTimeoutTma) &&
-                 (c == 0 || wait_c(bars.o_done, c - 1, p.status, kDevTimeoutMma));
+        const bool r = wait_c(bars.w_ready, c, p.status, kDevTimeoutPipe) &&
+                       wait_c(bars.tv_done, c, p.status, kDevTimeoutMma);
         if (r) {
+          if (c + 1 < N) load_v(c + 1);  // V(c) has been read by TV(c)
           tc_fence_after();
-          issue_t3(tbase, smem);
+          GDN_TRACE(28, c);
+          issue_state_terms(tbase, smem);
           umma_commit(&bars.x_ready[c & 1]);
           GDN_TRACE(0, c);
         }
-        if (r && c >= 1) r = wait_c(bars.o_read, c - 1, p.status, kDevTimeoutPipe);
-        if (r) {
-          tc_fence_after();
-          issue_t3b(tbase, smem, c);
-        }
       }
-      // --- Delta pass: Delta^T (fp32) -> Delta'hi | Delta'lo | Delta bf16
-      // (every exit from this loop goes through a named_sync_and, so the four warps leave together)
+      // --- Delta pass: X halves (fp32) -> Delta'hi | Delta'lo | Delta bf16
+      if (v == 64) GDN_TRACE(40, c);
       const bool xr = wait_c_warp(bars.x_ready, c, p.status, kDevTimeoutMma);
+      if (v == 64) GDN_TRACE(41, c);
       tc_fence_after();
-      if (xr && v == 0) {
-        GDN_TRACE(1, c);
-        if (c + 1 < N) load_v(c + 1);  // V(c) has been read by T3(c)
-      }
       if (xr) {
+        if (v == 0) GDN_TRACE(1, c);
         const ChunkParams& pc = params[c & 1];
         uint32_t d[64];
         tmem_ld64(lb + kColX, d);
-        uint32_t hi[32], lo[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          split_pack(__uint_as_float(d[2 * j]) * pc.egr[2 * j], __uint_as_float(d[2 * j + 1]) * pc.egr[2 * j + 1],
-                     hi[j], lo[j]);
-        tmem_st32(lb + kColX, hi);
-        tmem_st32(lb + kColX + 32, lo);
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t e[32];
+          tmem_ld32(lb + kColX + 64 + 32 * hf, e);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) hi[j] = pack_bf16x2(__uint_as_float(d[2 * j]), __uint_as_float(d[2 * j + 1]));
-        tmem_st32(lb + kColX + 64, hi);
+          for (int j = 0; j < 32; ++j)
+            d[32 * hf + j] = __float_as_uint(__uint_as_float(d[32 * hf + j]) + __uint_as_float(e[j]));
+        }
+        if (v == 0) GDN_TRACE(18, c);
+        // (every fp32 column is in registers, so the bf16 operands may overwrite the X region)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const int t = 32 * hf + 2 * j;
+            const float4 e4 = *reinterpret_cast<const float4*>(&pc.egr[t]);
+            split_pack(__uint_as_float(d[t]) * e4.x, __uint_as_float(d[t + 1]) * e4.y, hi[j], lo[j]);
+            split_pack(__uint_as_float(d[t + 2]) * e4.z, __uint_as_float(d[t + 3]) * e4.w, hi[j + 1], lo[j + 1]);
+          }
+          tmem_st16(lb + kColX + 16 * hf, hi);
+          tmem_st16(lb + kColX + 32 + 16 * hf, lo);
+        }
+        {
+          uint32_t pk[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) pk[j] = pack_bf16x2(__uint_as_float(d[2 * j]), __uint_as_float(d[2 * j + 1]));
+          tmem_st32(lb + kColX + 64, pk);
+        }
         tmem_wait_st();
       }
       tc_fence_before();
@@ -423,39 +452,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         issue_t4(tbase, smem, c);
         umma_commit(&bars.s_new[c & 1]);
-        issue_t5(tbase, smem, c);
-        umma_commit(&bars.o_done[c & 1]);
+        // T3b and T5 (output of chunk c) once P(c) and e^G Q(c) exist and O(c-1) has been read
+        if (wait_c(bars.pq_ready, c, p.status, kDevTimeoutPipe) &&
+            (c == 0 || wait_c(bars.o_read, c - 1, p.status, kDevTimeoutPipe))) {
+          tc_fence_after();
+          issue_t3b(tbase, smem, c);
+          GDN_TRACE(31, c);
+          issue_t5(tbase, smem, c);
+          umma_commit(&bars.o_done[c & 1]);
+        }
       }
-      // --- state pass: S(c+1) -> hi/lo copies, pre-scaled fp32 state for the next update
+      // --- state pass: S(c+1) -> hi/lo copies, pre-scaled fp32 state for the next update.  The
+      //     copies are overwritten only after T3b(c), their last reader, has completed (o_done).
       const bool last = (c == N - 1);
+      if (v == 64) GDN_TRACE(42, c);
       bool sr = wait_c_warp(bars.s_new, c, p.status, kDevTimeoutMma);
+      if (v == 64) GDN_TRACE(43, c);
       tc_fence_after();
       if (sr && v == 0) {
         GDN_TRACE(3, c);
-        if (c + kSlots < N) load_qk(c + kSlots);  // every reader of Q/K(c) has completed
+        if (c + kSlots < N) load_qk(c + kSlots);  // every reader of Q/K(c) has completed (T3b(c) too)
       }
       float gam = 1.0f;
       if (sr && !last) {
-        sr = wait_c_warp(bars.g_ready, c + 1, p.status, kDevTimeoutPipe);
+        sr = wait_c_warp(bars.g_ready, c + 1, p.status, kDevTimeoutPipe) &&
+             wait_c_warp(bars.o_done, c, p.status, kDevTimeoutMma);
         gam = params[(c + 1) & 1].gamma_c;
       }
 #pragma unroll 1
-      for (int half = 0; sr && half < 2; ++half) {
-        uint32_t sv[64];
-        tmem_ld64(lb + kColS + half * 64, sv);
+      for (int qt = 0; sr && qt < 4; ++qt) {  // 32 state columns at a time
+        uint32_t sv[32];
+        tmem_ld32(lb + kColS + qt * 32, sv);
+        if (v == 0 && qt == 0) GDN_TRACE(16, c);
         if (last) {
-          float* dst = p.state_out + state_off + v * kD + half * 64;
+          float* dst = p.state_out + state_off + v * kD + qt * 32;
 #pragma unroll
-          for (int j = 0; j < 64; j += 4)
+          for (int j = 0; j < 32; j += 4)
             *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
                                                               __uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3]));
         } else {
-          store_split32<0>(lb + kColShi + 32 * half, lb + kColSlo + 32 * half, sv);
-          store_split32<32>(lb + kColShi + 32 * half + 16, lb + kColSlo + 32 * half + 16, sv);
+          uint32_t hi[16], lo[16];
 #pragma unroll
-          for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
-          tmem_st32(lb + kColS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-          tmem_st32(lb + kColS + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          for (int j = 0; j < 16; ++j)
+            split_pack(__uint_as_float(sv[2 * j]), __uint_as_float(sv[2 * j + 1]), hi[j], lo[j]);
+          tmem_st16(lb + kColShi + 16 * qt, hi);
+          tmem_st16(lb + kColSlo + 16 * qt, lo);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
+          tmem_st32(lb + kColS + qt * 32, sv);
+          if (v == 0 && qt == 1) GDN_TRACE(17, c);
         }
       }
       if (!last) {
@@ -476,15 +521,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 8) {
     // =========================================================== operand warps
-    // Each warp polls on its own (lane 0 tests, the warp follows): output pass of chunk co once
-    // T5(co) is done, decay sums of chunk cg (warp 4), read-out of chunk cr once T1(cr) is done.
+    // Each warp polls on its own (lane 0 tests, the warp follows).  In order of priority: (warp
+    // 7) decay sums of chunk cg; the read-out of chunk cr once T1(cr) is done (it gates the next
+    // chunk's preparation); the output pass of chunk co once T5(co) is done.
     const int r = threadIdx.x - 128;  // TMEM lane / row owned by this thread
     const int wq = warp & 3;
     const uint32_t lb = tmem_addr(tbase, wq * 32, 0);
     float* Ls = reinterpret_cast<float*>(smem + kOffL);
-    uint8_t* stage = smem + kOffStage + wq * 2048;
-    int cr = 0, co = 0, cg = (warp == 4) ? 0 : N;
-    // decay inputs of chunk cg, two tokens per lane, loaded one chunk ahead (warp 4)
+    int cr = 0, co = 0;
+    int cg = (warp == 7) ? 0 : N;
+    // decay inputs of chunk cg, two tokens per lane, loaded one chunk ahead (warp 7)
     float ga = 0.f, gb = 0.f, ba = 0.f, bb = 0.f;
     auto load_g = [&](int c) {
       const int n_valid = min(kC, len - c * kC);
@@ -495,44 +541,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       ba = t0 < n_valid ? p.beta[(base + t0) * p.hv + h] : 0.0f;
       bb = t1 < n_valid ? p.beta[(base + t1) * p.hv + h] : 0.0f;
     };
-    if (warp == 4) load_g(0);
+    if (warp == 7) load_g(0);
     unsigned long long idle_since = 0;
     uint32_t idle_polls = 0;
     while (co < N) {
       bool did = false;
-      // (1) output pass of chunk co
-      if (co < cr && __shfl_sync(0xffffffffu, lane == 0 ? test_c(bars.o_done, co) : false, 0)) {
-        tc_fence_after();
-        if (r == 0) GDN_TRACE(7, co);
-        uint32_t o[64];
-        tmem_ld64(lb + kColO, o);
-        tc_fence_before();
-        mbar_arrive(&bars.o_read[co & 1]);
-        const int nv = min(kC, len - co * kC);
-        __nv_bfloat16* dst = p.out + (static_cast<size_t>(tok0 + co * kC) * p.hv + h) * kD + wq * 32;
-        const size_t tstride = static_cast<size_t>(p.hv) * kD;
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          // stage[i][v] for 32 tokens i, 16-byte chunks XOR-swizzled by (i >> 1) & 3
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            *reinterpret_cast<__nv_bfloat16*>(stage + i * 64 + ((((lane >> 3) ^ (i >> 1)) & 3) << 4) +
-                                              ((lane & 7) << 1)) = __float2bfloat16_rn(__uint_as_float(o[32 * hf + i]));
-          __syncwarp();
-          const int t = 32 * hf + lane;
-          if (t < nv) {
-            const uint8_t* src = stage + lane * 64;
-            uint4* g = reinterpret_cast<uint4*>(dst + t * tstride);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) g[j] = *reinterpret_cast<const uint4*>(src + (((j ^ (lane >> 1)) & 3) << 4));
-          }
-          __syncwarp();
-        }
-        if (r == 0) GDN_TRACE(8, co);
-        ++co;
-        did = true;
-      } else if (cg < N && cg <= co + 1) {
-        // (2) decay prefix sums of chunk cg (warp 4).  Its params slot held chunk cg-2, whose
+      if (cg < N && cg <= co + 1) {
+        // (1) decay prefix sums of chunk cg (warp 7).  Its params slot held chunk cg-2, whose
         //     last readers (Delta pass, state pass) finished before T5(cg-2) and so before the
         //     output pass of cg-2 that this warp has done.
         ChunkParams& pc = params[cg & 1];
@@ -561,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           pc.n_valid = n_valid;
         }
         __syncwarp();
-        mbar_arrive(&bars.g_ready[cg & 1]);
+        warp_arrive(&bars.g_ready[cg & 1]);
         if (lane == 0) GDN_TRACE(15, cg);
         ++cg;
         if (cg < N) load_g(cg);
@@ -569,65 +584,110 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else if (cr < N && cr <= co + 1 &&
                  __shfl_sync(0xffffffffu, lane == 0 ? (test_c(bars.qk_done, cr) && test_c(bars.g_ready, cr)) : false,
                              0)) {
-        // (3) read-out of chunk cr: P row (scale folded in), scale e^G Q in place, L row.  The P
-        //     slot was last read by T5(cr-2) (output pass cr-2 done); the L region by T2(cr-1),
-        //     which completed before T1(cr) was issued.
+        // (2) read-out of chunk cr.  The P slot was last read by T5(cr-2) (output pass cr-2 done);
+        //     the L region by T2(cr-1), which completed before T1(cr) was issued.
         tc_fence_after();
         if (r == 0) GDN_TRACE(5, cr);
+        if (r == 64) GDN_TRACE(36, cr);
         const ChunkParams& pc = params[cr & 1];
         uint32_t row[64];
         tmem_ld64(lb + kColQW, row);
+        if (r == 96) GDN_TRACE(37, cr);
+        if (r == 64) GDN_TRACE(39, cr);
+        if (r == 32) GDN_TRACE(38, cr);
+        tc_fence_before();
+        if (r == 64) GDN_TRACE(44, cr);
+        warp_arrive(&bars.qk_ld[cr & 1]);
+        if (r == 64) GDN_TRACE(45, cr);
+        if (r == 0) GDN_TRACE(24, cr);
+        if (r == 64) GDN_TRACE(32, cr);
         if (r < 64) {
+          // row t of L = beta_t exp(G_t - G_s) (k_t . k_s), s < t
           const int t = r;
+          const float gt = pc.g2[t];
+          const float bt = pc.beta[t];
+          float* lrow = Ls + t * kLds;
+#pragma unroll
+          for (int s4 = 0; s4 < 64; s4 += 4) {
+            const float4 g4 = *reinterpret_cast<const float4*>(&pc.g2[s4]);
+            float4 val;
+            val.x = s4 + 0 < t ? bt * ex2_approx(gt - g4.x) * __uint_as_float(row[s4 + 0]) : 0.0f;
+            val.y = s4 + 1 < t ? bt * ex2_approx(gt - g4.y) * __uint_as_float(row[s4 + 1]) : 0.0f;
+            val.z = s4 + 2 < t ? bt * ex2_approx(gt - g4.z) * __uint_as_float(row[s4 + 2]) : 0.0f;
+            val.w = s4 + 3 < t ? bt * ex2_approx(gt - g4.w) * __uint_as_float(row[s4 + 3]) : 0.0f;
+            *reinterpret_cast<float4*>(lrow + s4) = val;
+          }
+          warp_arrive(&bars.l_ready[cr & 1]);
+          if (r == 0) GDN_TRACE(33, cr);
+        } else {
+          // P row t (scale folded in), then scale e^G q_t in place
+          const int t = r - 64;
           const float gt = pc.g2[t];
           uint32_t prow[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int s0 = 2 * j, s1 = 2 * j + 1;
-            const float p0 = s0 <= t ? __uint_as_float(row[s0]) * ex2_approx(gt - pc.g2[s0]) * p.scale : 0.0f;
-            const float p1 = s1 <= t ? __uint_as_float(row[s1]) * ex2_approx(gt - pc.g2[s1]) * p.scale : 0.0f;
+          for (int j = 0; j < 32; j += 2) {
+            const int s0 = 2 * j;
+            const float4 g4 = *reinterpret_cast<const float4*>(&pc.g2[s0]);
+            const float p0 = s0 + 0 <= t ? __uint_as_float(row[s0 + 0]) * ex2_approx(gt - g4.x) * p.scale : 0.0f;
+            const float p1 = s0 + 1 <= t ? __uint_as_float(row[s0 + 1]) * ex2_approx(gt - g4.y) * p.scale : 0.0f;
+            const float p2 = s0 + 2 <= t ? __uint_as_float(row[s0 + 2]) * ex2_approx(gt - g4.z) * p.scale : 0.0f;
+            const float p3 = s0 + 3 <= t ? __uint_as_float(row[s0 + 3]) * ex2_approx(gt - g4.w) * p.scale : 0.0f;
             prow[j] = pack_bf16x2(p0, p1);
+            prow[j + 1] = pack_bf16x2(p2, p3);
           }
           store_row_sw128(smem + kOffP + (cr & 1) * 8192, t, prow);
-          // Q row t lives in rows 0..63 of the stacked slot, 2 boxes of 64 columns
+          if (r == 64) GDN_TRACE(25, cr);
           uint8_t* slot = smem + kOffSlots + (cr % kSlots) * kSlotBytes;
           const float f = pc.eg[t] * p.scale;
 #pragma unroll
           for (int bx = 0; bx < 2; ++bx) {
+            uint4 q8[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) q8[j] = *reinterpret_cast<const uint4*>(slot + bx * 16384 + kQRows + t * 128 + (j << 4));
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              uint4* ptr = reinterpret_cast<uint4*>(slot + bx * 16384 + t * 128 + ((j ^ (t & 7)) << 4));
-              uint4 val = *ptr;
-              uint32_t* w = reinterpret_cast<uint32_t*>(&val);
+              uint32_t* w = reinterpret_cast<uint32_t*>(&q8[j]);
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 __nv_bfloat162 b2 = *reinterpret_cast<__nv_bfloat162*>(&w[e]);
                 const float2 fl = __bfloat1622float2(b2);
                 w[e] = pack_bf16x2(fl.x * f, fl.y * f);
               }
-              *ptr = val;
             }
-          }
-        } else {
-          const int t = r - 64;
-          const float gt = pc.g2[t];
-          const float bt = pc.beta[t];
-          float* lrow = Ls + t * kLds;
 #pragma unroll
-          for (int s4 = 0; s4 < 64; s4 += 4) {
-            float4 val;
-            val.x = s4 + 0 < t ? bt * ex2_approx(gt - pc.g2[s4 + 0]) * __uint_as_float(row[s4 + 0]) : 0.0f;
-            val.y = s4 + 1 < t ? bt * ex2_approx(gt - pc.g2[s4 + 1]) * __uint_as_float(row[s4 + 1]) : 0.0f;
-            val.z = s4 + 2 < t ? bt * ex2_approx(gt - pc.g2[s4 + 2]) * __uint_as_float(row[s4 + 2]) : 0.0f;
-            val.w = s4 + 3 < t ? bt * ex2_approx(gt - pc.g2[s4 + 3]) * __uint_as_float(row[s4 + 3]) : 0.0f;
-            *reinterpret_cast<float4*>(lrow + s4) = val;
+            for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(slot + bx * 16384 + kQRows + t * 128 + (j << 4)) = q8[j];
           }
+          fence_async_smem();
+          warp_arrive(&bars.pq_ready[cr & 1]);
         }
-        fence_async_smem();
-        tc_fence_before();
-        mbar_arrive(&bars.qk_read[cr & 1]);
         if (r == 0) GDN_TRACE(6, cr);
         ++cr;
+        did = true;
+      } else if (co < cr && __shfl_sync(0xffffffffu, lane == 0 ? test_c(bars.o_done, co) : false, 0)) {
+        // (3) output pass of chunk co (scale already folded into P and e^G Q)
+        tc_fence_after();
+        if (r == 0) GDN_TRACE(7, co);
+        uint32_t o[64];
+        tmem_ld64(lb + kColO, o);
+        if (r == 0) GDN_TRACE(26, co);
+        tc_fence_before();
+        warp_arrive(&bars.o_read[co & 1]);
+        // token pair (2i, 2i+1): the even lane of a lane pair stores (O[2i][v], O[2i][v+1]), the
+        // odd lane (O[2i+1][v-1], O[2i+1][v]), one 4-byte store each
+        const int nv = min(kC, len - co * kC);
+        const bool odd = (lane & 1) != 0;
+        const size_t tstride = static_cast<size_t>(p.hv) * kD;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (static_cast<size_t>(tok0 + co * kC) * p.hv + h) * kD +
+                                                    (r & ~1)) + (odd ? tstride / 2 : 0);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float a = __uint_as_float(o[2 * i]), b = __uint_as_float(o[2 * i + 1]);
+          const float other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
+          const uint32_t packed = odd ? pack_bf16x2(other, b) : pack_bf16x2(a, other);
+          if (2 * i + (odd ? 1 : 0) < nv) dst[i * tstride] = packed;
+        }
+        if (r == 0) GDN_TRACE(8, co);
+        ++co;
         did = true;
       }
       if (did) {
@@ -651,10 +711,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // =========================================================== triangular solve and W
-    // X = (I + L)^-1 by 16x16 blocks: the four diagonal blocks by forward substitution (one
-    // column per thread), then block rows i = 1..3 as X[i, <i] = -D_i (L[i, <i] X[<i, <i]).
-    // X's diagonal blocks hold explicit zeros above the diagonal; the blocks above the block
-    // diagonal are never read.
+    // X = (I + L)^-1 by recursive doubling over 16x16 blocks: the four diagonal blocks D_b by
+    // forward substitution (one column per thread); the two 32x32 diagonal blocks E_0, E_1 from
+    // X[2p+1, 2p] = -D_{2p+1} L[2p+1, 2p] D_{2p}; the lower 32x32 block as -E_1 L[1, 0] E_0.
+    // Products are staged in X's strictly upper blocks, which nothing else reads; the diagonal
+    // blocks hold explicit zeros above their diagonal.
     const int tid = threadIdx.x - 256;
     const uint32_t lb = tmem_addr(tbase, (warp & 3) * 32, 0);
     float* Ls = reinterpret_cast<float*>(smem + kOffL);
@@ -669,13 +730,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         GDN_TRACE(14, 0);
       }
     }
+    // TV(c): V^T T^T into the X region once it is free (T4(c-1), T5(c-1) complete) and V(c) landed
+    auto issue_tv_c = [&](int c) {  // thread 0 only
+      tc_fence_after();
+      issue_tv(tbase, smem);
+      umma_commit(&bars.tv_done[c & 1]);
+      GDN_TRACE(29, c);
+    };
     for (int c = 0; c < N; ++c) {
-      const bool ready = wait_c(bars.qk_read, c, p.status, kDevTimeoutPipe);
+      const bool ready = wait_c_warp(bars.l_ready, c, p.status, kDevTimeoutPipe);
+      if (tid == 0) GDN_TRACE(34, c);
+      if (tid == 64) GDN_TRACE(35, c);
       if (!named_sync_and(3, 128, ready && ok)) { ok = false; break; }
       if (tid == 0) GDN_TRACE(9, c);
-      // --- diagonal blocks D_b = (I + L_bb)^-1, column j per thread
-      if (tid < 64) {
-        const int b = tid >> 4, j = tid & 15;
+      // --- step 1: diagonal blocks D_b = (I + L_bb)^-1, column j per thread
+      if (tid >= 64) {  // warps 10-11 (their schedulers carry the lighter read-out warps)
+        const int b = (tid - 64) >> 4, j = tid & 15;
         const float* lb16 = Ls + 16 * b * kLds + 16 * b;
         float acc[16];
 #pragma unroll
@@ -690,71 +760,103 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; ++i) Xs[(16 * b + i) * kLds + 16 * b + j] = acc[i];
       }
       named_sync(3, 128);
-      // --- block rows 1..3; thread = (row rr of the block row, column pair cg of each block)
+      if (tid == 0) GDN_TRACE(11, c);
+      // --- step 2: pairs p: X[R + rr][C + c4..c4+3], R = 16(2p+1), C = 32p
       {
-        const int rr = tid >> 3, cg = tid & 7;
+        const int pr = tid >> 6, q = tid & 63, rr = q >> 2, c4 = (q & 3) * 4;
+        const int R = 16 * (2 * pr + 1), C = 32 * pr;
+        float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int i = 1; i < 4; ++i) {
-          float2 y[3];
-          const float* lrow = Ls + (16 * i + rr) * kLds;
-#pragma unroll
-          for (int cb = 0; cb < i; ++cb) {
-            const int c0 = 16 * cb + 2 * cg;
-            float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-            for (int k4 = 16 * cb; k4 < 16 * i; k4 += 4) {
-              const float4 l = *reinterpret_cast<const float4*>(lrow + k4);
-              const float2 x0 = *reinterpret_cast<const float2*>(Xs + (k4 + 0) * kLds + c0);
-              const float2 x1 = *reinterpret_cast<const float2*>(Xs + (k4 + 1) * kLds + c0);
-              const float2 x2 = *reinterpret_cast<const float2*>(Xs + (k4 + 2) * kLds + c0);
-              const float2 x3 = *reinterpret_cast<const float2*>(Xs + (k4 + 3) * kLds + c0);
-              a0 = fmaf(l.x, x0.x, a0);
-              a1 = fmaf(l.x, x0.y, a1);
-              a0 = fmaf(l.y, x1.x, a0);
-              a1 = fmaf(l.y, x1.y, a1);
-              a0 = fmaf(l.z, x2.x, a0);
-              a1 = fmaf(l.z, x2.y, a1);
-              a0 = fmaf(l.w, x3.x, a0);
-              a1 = fmaf(l.w, x3.y, a1);
-            }
-            y[cb] = make_float2(a0, a1);
-          }
-          // Y = L[i, <i] X[<i, <i] goes to X's block row i (not read by this step)
-#pragma unroll
-          for (int cb = 0; cb < i; ++cb) *reinterpret_cast<float2*>(Xs + (16 * i + rr) * kLds + 16 * cb + 2 * cg) = y[cb];
-          named_sync(3, 128);
-          float dr[16];
-#pragma unroll
-          for (int m4 = 0; m4 < 16; m4 += 4) {
-            const float4 d4 = *reinterpret_cast<const float4*>(Xs + (16 * i + rr) * kLds + 16 * i + m4);
-            dr[m4] = d4.x;
-            dr[m4 + 1] = d4.y;
-            dr[m4 + 2] = d4.z;
-            dr[m4 + 3] = d4.w;
-          }
-          float2 z[3];
-#pragma unroll
-          for (int cb = 0; cb < i; ++cb) {
-            float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-            for (int m = 0; m < 16; ++m) {
-              const float2 ym = *reinterpret_cast<const float2*>(Xs + (16 * i + m) * kLds + 16 * cb + 2 * cg);
-              a0 = fmaf(dr[m], ym.x, a0);
-              a1 = fmaf(dr[m], ym.y, a1);
-            }
-            z[cb] = make_float2(-a0, -a1);
-          }
-          named_sync(3, 128);
-#pragma unroll
-          for (int cb = 0; cb < i; ++cb) *reinterpret_cast<float2*>(Xs + (16 * i + rr) * kLds + 16 * cb + 2 * cg) = z[cb];
-          named_sync(3, 128);
+        for (int k = 0; k < 16; ++k) {  // Y = L[R.., C..] D_{2p}
+          const float l = Ls[(R + rr) * kLds + C + k];
+          const float4 d = *reinterpret_cast<const float4*>(Xs + (C + k) * kLds + C + c4);
+          y.x = fmaf(l, d.x, y.x);
+          y.y = fmaf(l, d.y, y.y);
+          y.z = fmaf(l, d.z, y.z);
+          y.w = fmaf(l, d.w, y.w);
         }
+        *reinterpret_cast<float4*>(Xs + (C + rr) * kLds + R + c4) = y;  // staged in block (2p, 2p+1)
+        named_sync(3, 128);
+        float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {  // X[R.., C..] = -D_{2p+1} Y
+          const float dm = Xs[(R + rr) * kLds + R + m];
+          const float4 ym = *reinterpret_cast<const float4*>(Xs + (C + m) * kLds + R + c4);
+          z.x = fmaf(dm, ym.x, z.x);
+          z.y = fmaf(dm, ym.y, z.y);
+          z.z = fmaf(dm, ym.z, z.z);
+          z.w = fmaf(dm, ym.w, z.w);
+        }
+        *reinterpret_cast<float4*>(Xs + (R + rr) * kLds + C + c4) = make_float4(-z.x, -z.y, -z.z, -z.w);
+      }
+      named_sync(3, 128);
+      if (tid == 0) GDN_TRACE(20, c);
+      // --- step 3: lower 32x32 block.  Thread: row r of 32, columns 4q..4q+3 and 16+4q..16+4q+3.
+      {
+        const int r = tid >> 2, q4 = (tid & 3) * 4;
+        float4 ya = make_float4(0.f, 0.f, 0.f, 0.f), yb = ya;
+        const float* lrow = Ls + (32 + r) * kLds;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {  // Y = L[32.., 0..32] E_0   (E_0 block (0,1) is not read)
+          const float l = lrow[k];
+          const float4 xa = *reinterpret_cast<const float4*>(Xs + k * kLds + q4);
+          ya.x = fmaf(l, xa.x, ya.x);
+          ya.y = fmaf(l, xa.y, ya.y);
+          ya.z = fmaf(l, xa.z, ya.z);
+          ya.w = fmaf(l, xa.w, ya.w);
+          if (k >= 16) {
+            const float4 xb = *reinterpret_cast<const float4*>(Xs + k * kLds + 16 + q4);
+            yb.x = fmaf(l, xb.x, yb.x);
+            yb.y = fmaf(l, xb.y, yb.y);
+            yb.z = fmaf(l, xb.z, yb.z);
+            yb.w = fmaf(l, xb.w, yb.w);
+          }
+        }
+        *reinterpret_cast<float4*>(Xs + r * kLds + 32 + q4) = ya;  // staged in rows 0-31, cols 32-63
+        *reinterpret_cast<float4*>(Xs + r * kLds + 48 + q4) = yb;
+        named_sync(3, 128);
+        if (tid == 0) GDN_TRACE(21, c);
+        float4 za = make_float4(0.f, 0.f, 0.f, 0.f), zb = za;
+        const float* erow = Xs + (32 + r) * kLds + 32;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {  // X[32.., 0..32] = -E_1 Y   (rows 32-47: D_2 only)
+          const float e = erow[m];
+          const float4 a = *reinterpret_cast<const float4*>(Xs + m * kLds + 32 + q4);
+          const float4 b = *reinterpret_cast<const float4*>(Xs + m * kLds + 48 + q4);
+          za.x = fmaf(e, a.x, za.x);
+          za.y = fmaf(e, a.y, za.y);
+          za.z = fmaf(e, a.z, za.z);
+          za.w = fmaf(e, a.w, za.w);
+          zb.x = fmaf(e, b.x, zb.x);
+          zb.y = fmaf(e, b.y, zb.y);
+          zb.z = fmaf(e, b.z, zb.z);
+          zb.w = fmaf(e, b.w, zb.w);
+        }
+        if (r >= 16) {  // warp-uniform: rows 48-63 also take X[3, 2] and D_3
+#pragma unroll
+          for (int m = 16; m < 32; ++m) {
+            const float e = erow[m];
+            const float4 a = *reinterpret_cast<const float4*>(Xs + m * kLds + 32 + q4);
+            const float4 b = *reinterpret_cast<const float4*>(Xs + m * kLds + 48 + q4);
+            za.x = fmaf(e, a.x, za.x);
+            za.y = fmaf(e, a.y, za.y);
+            za.z = fmaf(e, a.z, za.z);
+            za.w = fmaf(e, a.w, za.w);
+            zb.x = fmaf(e, b.x, zb.x);
+            zb.y = fmaf(e, b.y, zb.y);
+            zb.z = fmaf(e, b.z, zb.z);
+            zb.w = fmaf(e, b.w, zb.w);
+          }
+        }
+        *reinterpret_cast<float4*>(Xs + (32 + r) * kLds + q4) = make_float4(-za.x, -za.y, -za.z, -za.w);
+        *reinterpret_cast<float4*>(Xs + (32 + r) * kLds + 16 + q4) = make_float4(-zb.x, -zb.y, -zb.z, -zb.w);
       }
       if (tid == 0) GDN_TRACE(10, c);
       // --- T = X diag(beta) and T diag(e^G) as MN-major hi/lo tiles (row s, tokens t of one
-      //     half).  The T tiles and the W tiles were last read by T3(c-1).
-      const bool free_tiles = (c == 0) || wait_c(bars.x_ready, c - 1, p.status, kDevTimeoutMma);
+      //     half).  The T tiles were last read by TV(c-1), the W tiles by the state terms(c-1).
+      const bool free_tiles = (c == 0) || wait_c_warp(bars.x_ready, c - 1, p.status, kDevTimeoutMma);
       if (!named_sync_and(3, 128, free_tiles)) { ok = false; break; }
+      if (tid == 0) GDN_TRACE(22, c);
       {
         const ChunkParams& pc = params[c & 1];
         const int s = tid & 63, half = tid >> 6;
@@ -767,28 +869,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float w0 = pc.beta[s];
         const float w1 = w0 * pc.eg[s];
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {  // q = 0: T, q = 1: T diag(e^G) (over the dead L)
-          const float w = q ? w1 : w0;
+        for (int qq = 0; qq < 2; ++qq) {  // qq = 0: T, qq = 1: T diag(e^G) (over the dead L)
+          const float w = qq ? w1 : w0;
           uint32_t hi[16], lo[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) split_pack(xv[2 * i] * w, xv[2 * i + 1] * w, hi[i], lo[i]);
-          uint8_t* tile = smem + (q ? kOffL : kOffT);
+          uint8_t* tile = smem + (qq ? kOffL : kOffT);
           store_half_row_sw128(tile, s, half, hi);
           store_half_row_sw128(tile + 8192, s, half, lo);
         }
       }
+      if (tid == 0) GDN_TRACE(27, c);
       fence_async_smem();
       named_sync(3, 128);
+      bool tv_issued = false;
       if (tid == 0) {
-        tc_fence_after();
-        issue_t2(tbase, smem, c);
-        umma_commit(&bars.w_done[c & 1]);
-        GDN_TRACE(12, c);
+        // T2 once every operand warp has read Q K^T(c) out of the QW region
+        if (wait_c(bars.qk_ld, c, p.status, kDevTimeoutPipe)) {
+          tc_fence_after();
+          GDN_TRACE(30, c);
+          issue_t2(tbase, smem, c);
+          umma_commit(&bars.w_done[c & 1]);
+          GDN_TRACE(12, c);
+        }
+        if (test_c(bars.v_full, c) && (c == 0 || test_c(bars.o_done, c - 1))) {
+          issue_tv_c(c);
+          tv_issued = true;
+        }
       }
       // --- W pass: W^T (lane = key row k) -> -W as [k][t], hi and lo tiles
       const bool wready = wait_c_warp(bars.w_done, c, p.status, kDevTimeoutMma);
       if (wready) {
         tc_fence_after();
+        if (tid == 0) GDN_TRACE(23, c);
         uint32_t row[64];
         tmem_ld64(lb + kColQW, row);
 #pragma unroll
@@ -803,7 +916,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         fence_async_smem();
         tc_fence_before();
-        mbar_arrive(&bars.w_ready[c & 1]);
+        warp_arrive(&bars.w_ready[c & 1]);
       }
       // every thread has read W^T out of the QW region: T1(c+1) may overwrite it
       if (!named_sync_and(3, 128, wready)) { ok = false; break; }
@@ -818,6 +931,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_commit(&bars.qk_done[n & 1]);
             GDN_TRACE(14, n);
           }
+        }
+        if (ok && !tv_issued) {
+          ok = wait_c(bars.v_full, c, p.status, kDevTimeoutTma) &&
+               (c == 0 || wait_c(bars.o_done, c - 1, p.status, kDevTimeoutMma));
+          if (ok) issue_tv_c(c);
         }
       }
     }
