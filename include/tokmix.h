@@ -1,6 +1,7 @@
 /* tokmix.h -- C ABI of libtokmix.so, the sm_100a (B200) prefill token-mixer kernels.
  *
- * Two entry points replace the two kernel extensions the reference's plugin modules bind:
+ * Two entry points replace the two kernel extensions the reference's plugin modules bind (the
+ * GDN one has two further variants below):
  *
  *   tokmix_fa2_fwd      replaces  flash_attention_2_forward(q, k, v, sm_scale, causal)
  *                       kernels_optimized/flash_attention_2.cu:1121-1258, bound at
@@ -10,9 +11,8 @@
  *                       kernels_optimized/qwen35moe_gdn_prefill.py:149-161 (kernel_fn)
  *
  * Conventions (all entry points):
- *   - every pointer argument except `status` and the cu_seqlens host copy is DEVICE memory of
- *     the current device; the library allocates and frees no device memory (TMEM is allocated
- *     and released inside each kernel);
+ *   - every pointer argument is DEVICE memory of the current device; the library allocates and
+ *     frees no device memory (TMEM is allocated and released inside each kernel);
  *   - work is enqueued on `stream` (a cudaStream_t; NULL = legacy default stream) and the call
  *     returns without synchronising;
  *   - the return value is TOKMIX_OK or one of the TOKMIX_ERR_* codes; the text of the last
@@ -105,6 +105,25 @@ int tokmix_gdn_prefill_noalloc(const void* q, const void* k, const void* v, cons
                                const float* initial_state, void* out, float* final_state, int batch, int seqlen,
                                int heads_k, int heads_v, int head_dim_k, int head_dim_v, float scale, int io_dtype,
                                uint32_t* status, void* stream);
+
+/* Gated-delta-rule prefill in two launches, for problems with few (sequence, value head) units
+ * (fewer than the GPU has SMs): a chunk-parallel preparation kernel (one CTA per chunk and value
+ * head) writes every chunk's tensor-core operands to `workspace`; a state-chain kernel (one CTA
+ * per sequence and value head) consumes them.  Same maths, arguments and results as
+ * tokmix_gdn_prefill (up to fp32 summation order), plus:
+ *   chunk_base_dev:   device int32 [num_seqs + 1], chunk_base[n] = sum over m < n of
+ *                     ceil(len_m / 64); chunk_base[num_seqs] = total_chunks
+ *   workspace:        device memory of at least tokmix_gdn_split_workspace_bytes(total_chunks,
+ *                     heads_v) bytes, 16-byte aligned (contents need no initialisation)
+ * No counterpart in the reference (its prefill is one kernel chain per layer call). */
+int tokmix_gdn_prefill_split(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                             const float* initial_state, void* out, float* final_state, const int32_t* cu_seqlens_dev,
+                             const int32_t* chunk_base_dev, int num_seqs, int total_tokens, int total_chunks,
+                             int heads_k, int heads_v, int head_dim_k, int head_dim_v, float scale, int io_dtype,
+                             void* workspace, long long workspace_bytes, uint32_t* status, void* stream);
+
+/* Workspace size of tokmix_gdn_prefill_split in bytes (-1 for negative arguments). */
+long long tokmix_gdn_split_workspace_bytes(int total_chunks, int heads_v);
 
 /* Text of the last error reported on the calling thread ("" if none). */
 const char* tokmix_last_error(void);

@@ -1,0 +1,668 @@
+// gdn_split.cu -- GDN prefill in two launches, for problems with few (sequence, value head)
+// units, where one CTA per unit would leave most SMs idle and put a long per-chunk preparation
+// path in front of every step of the state chain.
+//
+//   1. gdn_prep_kernel: one CTA per (chunk, value head), all chunks at once, three CTAs per SM.
+//      Decay sums, Q K^T / K K^T (tcgen05), the read-out of L, P and e^G-scaled Q, the triangular
+//      solve, T and T diag(e^G), W = T diag(e^G) K (tcgen05).  The threads that produce the chunk's
+//      MMA operands write them straight to one record of kRecBytes in a workspace (L2-resident
+//      for the sizes this mode is used at), already in the 128-byte-swizzled shared-memory layout
+//      the chain kernel feeds to the tensor core.
+//   2. gdn_chain_kernel: one CTA per (sequence, value head).  A loader warp streams each chunk's
+//      record (bulk copies) and its K, V tiles (TMA) into a two-stage ring; the state chain and
+//      the output pass are those of gdn_prefill.cu without any preparation work.
+// Results equal gdn_prefill.cu's up to fp32 summation order (same operands, same splits).
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "gdn_common.cuh"
+#include "host_common.h"
+
+namespace tokmix {
+namespace gdn {
+namespace split {
+
+// ---- workspace record of one (chunk, value head)
+constexpr int kRecT = 0;                      // T hi | lo, MN-major [s][t], 8 KB each
+constexpr int kRecW = 16384;                  // -W hi | lo, [k][t], 16 KB each
+constexpr int kRecQ = 49152;                  // scale e^G Q, K-major [t][k]: two 64-column boxes of 8 KB
+constexpr int kRecP = 65536;                  // scale P, K-major [t][s], 8 KB
+constexpr int kRecParams = 73728;             // ChunkParams
+constexpr int kRecBytes = kRecParams + kParamsBytes;
+
+// ---- preparation kernel
+constexpr int kPrepThreads = 128;
+constexpr int kPSlot = 0;                     // [K;Q]: two boxes of 128 rows x 128 B (K rows 0-63, Q 64-127)
+constexpr int kPL = 32768;                    // L fp32 (row stride kLds); then T diag(e^G) hi | lo
+constexpr int kPX = kPL + 64 * kLds * 4;      // X = (I + L)^-1 fp32
+constexpr int kPParams = kPX + 64 * kLds * 4;
+constexpr int kPSmem = kPParams + kParamsBytes;
+static_assert(kPL % 1024 == 0 && 3 * (kPSmem + 1024 + 64) <= 228 * 1024, "prep layout: three CTAs per SM");
+
+// ---- chain kernel
+constexpr int kChainThreads = 288;            // warps 0-3 chain, 4-7 output, 8 loader
+constexpr int kSK = 75776;                    // K: two boxes of 64 rows x 128 B (after the record)
+constexpr int kSV = kSK + 16384;              // V: two boxes of 64 rows x 128 B
+constexpr int kStageBytes = kSV + 16384;
+constexpr int kCSmem = 2 * kStageBytes;
+static_assert(kRecBytes <= kSK && kSK % 1024 == 0 && kStageBytes % 1024 == 0, "chain layout");
+static_assert(kCSmem + 1024 + 256 <= 227 * 1024, "chain shared memory budget");
+
+constexpr uint32_t kColS = 0, kColShi = 128, kColSlo = 192, kColX = 256, kColO = 384;
+
+// Optional phase trace of the chain kernel (build with -DTOKMIX_GDN_TRACE): SM clock stamps of
+// CTA 0 by event and chunk, read back with tokmix_gdn_split_trace_read().
+#ifdef TOKMIX_GDN_TRACE
+constexpr int kTrChunks = 64, kTrEvents = 16;
+__device__ unsigned long long g_split_trace[kTrEvents * kTrChunks];
+#define SPLIT_TRACE(ev, c)                                                                               \
+  do {                                                                                                   \
+    if (blockIdx.x == 0 && (c) < kTrChunks) g_split_trace[(ev) * kTrChunks + (c)] = clock64();          \
+  } while (0)
+#else
+#define SPLIT_TRACE(ev, c) \
+  do {                     \
+  } while (0)
+#endif
+
+struct PrepParams {
+  const float* g;
+  const float* beta;
+  const int32_t* cu_seqlens;
+  const int32_t* chunk_base;  // [num_seqs + 1]: first global chunk of each sequence
+  uint8_t* ws;
+  int num_seqs, hk, hv;
+  float scale;
+  uint32_t* status;
+};
+
+struct ChainParams {
+  const float* state_in;
+  float* state_out;
+  __nv_bfloat16* out;
+  const int32_t* cu_seqlens;
+  const int32_t* chunk_base;
+  const uint8_t* ws;
+  int hk, hv;
+  uint32_t* status;
+};
+
+// bulk copy global -> shared, completing on an mbarrier (no multicast)
+__device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(sdst)),
+               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kPrepThreads, 3)
+    gdn_prep_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                    const PrepParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_in, bar_mma;
+  __shared__ uint32_t tmem_base_shared;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gc = blockIdx.x, h = blockIdx.y;
+  int lo = 0, hi = p.num_seqs;  // sequence of global chunk gc: chunk_base[lo] <= gc < chunk_base[lo + 1]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (p.chunk_base[mid] <= gc) lo = mid; else hi = mid;
+  }
+  const int seq = lo, c = gc - p.chunk_base[seq];
+  const int tok0 = p.cu_seqlens[seq];
+  const int n_valid = min(kC, p.cu_seqlens[seq + 1] - tok0 - c * kC);
+  const int row0 = tok0 + c * kC;
+  const int kh = h % p.hk;
+  ChunkParams& pc = *reinterpret_cast<ChunkParams*>(smem + kPParams);
+  float* Ls = reinterpret_cast<float*>(smem + kPL);
+  float* Xs = reinterpret_cast<float*>(smem + kPX);
+  uint8_t* rec = p.ws + (static_cast<size_t>(gc) * p.hv + h) * kRecBytes;
+
+  if (tid == 0) {
+    cta_abort_flag() = 0u;
+    mbar_init(&bar_in, 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_shared, 64);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base_shared;
+  if (tid == 0) {
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_k);
+    mbar_arrive_expect_tx(&bar_in, 32768);
+    for (int bx = 0; bx < 2; ++bx) {
+      tma_load_3d(smem + kPSlot + bx * 16384, &map_k, &bar_in, bx * 64, kh, row0);
+      tma_load_3d(smem + kPSlot + bx * 16384 + 8192, &map_q, &bar_in, bx * 64, kh, row0);
+    }
+  }
+  if (warp == 3) {
+    const int t0 = 2 * lane, t1 = 2 * lane + 1;
+    const size_t base = static_cast<size_t>(row0);
+    const float ga = t0 < n_valid ? p.g[(base + t0) * p.hv + h] : 0.0f;
+    const float gb = t1 < n_valid ? p.g[(base + t1) * p.hv + h] : 0.0f;
+    const float ba = t0 < n_valid ? p.beta[(base + t0) * p.hv + h] : 0.0f;
+    const float bb = t1 < n_valid ? p.beta[(base + t1) * p.hv + h] : 0.0f;
+    chunk_decay_params(pc, ga, gb, ba, bb, n_valid, lane);
+  }
+  __syncthreads();
+  if (tid < kParamsBytes / 16)
+    reinterpret_cast<uint4*>(rec + kRecParams)[tid] = reinterpret_cast<const uint4*>(smem + kPParams)[tid];
+  // --- T1: [K;Q] K^T
+  bool ok = true;
+  if (tid == 0) {
+    ok = mbar_wait(&bar_in, 0, p.status, kDevTimeoutTma);
+    if (ok) {
+      tc_fence_after();
+      const uint32_t id = make_idesc(128, 64, 1, 0, 0);
+      const uint32_t slot = smem_u32(smem + kPSlot);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16_ss(tbase, kmaj_desc(slot, kk, 16384), kmaj_desc(slot, kk, 16384), id, kk > 0 ? 1u : 0u);
+      umma_commit(&bar_mma);
+    }
+  }
+  // --- read-out: rows 0-63 (K K^T) -> L, rows 64-127 (Q K^T) -> P and scale e^G q in place
+  ok = __all_sync(0xffffffffu, mbar_wait(&bar_mma, 0, p.status, kDevTimeoutMma));
+  if (ok) {
+    tc_fence_after();
+    uint32_t row[64];
+    tmem_ld64(tmem_addr(tbase, warp * 32, 0), row);
+    if (tid < 64) {
+      l_row(row, pc, tid, Ls);
+    } else {
+      const int t = tid - 64;
+      p_row(row, pc, t, p.scale, rec + kRecP);
+      scale_row_copy(smem + kPSlot + 8192 + t * 128, 16384, rec + kRecQ + t * 128, 8192, pc.eg[t] * p.scale);
+    }
+  }
+  tc_fence_before();
+  ok = named_sync_and(1, 128, ok);
+  if (ok) {
+    solve_inverse(Ls, Xs, tid, 1);
+    write_t_tiles(Xs, pc, tid, rec + kRecT, smem + kPL);  // T to the record, T diag(e^G) over the dead L
+    fence_async_smem();
+    named_sync(1, 128);
+    // --- T2: W^T = K^T (TG_hi + TG_lo)^T
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t id = make_idesc(128, 64, 1, 1, 1);
+      const uint32_t kt = smem_u32(smem + kPSlot), tg = smem_u32(smem + kPL);
+#pragma unroll
+      for (int part = 0; part < 2; ++part)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16_ss(tbase, make_sdesc_sw128(kt + kk * 2048, 16384, 1024),
+                       make_sdesc_sw128(tg + part * 8192 + kk * 2048, 16384, 1024), id, (part > 0 || kk > 0) ? 1u : 0u);
+      umma_commit(&bar_mma);
+    }
+    ok = __all_sync(0xffffffffu, mbar_wait(&bar_mma, 1, p.status, kDevTimeoutMma));
+    if (ok) {
+      tc_fence_after();
+      uint32_t row[64];
+      tmem_ld64(tmem_addr(tbase, warp * 32, 0), row);
+      w_row(row, tid, rec + kRecW);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 64);
+  }
+}
+
+// Two-slot barrier helpers (event of chunk c in slot c & 1, phase (c >> 1) & 1)
+__device__ __forceinline__ bool wait2(uint64_t* bars, int c, uint32_t* status, uint32_t code) {
+  return mbar_wait(&bars[c & 1], (c >> 1) & 1, status, code);
+}
+__device__ __forceinline__ bool wait2_warp(uint64_t* bars, int c, uint32_t* status, uint32_t code) {
+  return __all_sync(0xffffffffu, wait2(bars, c, status, code));
+}
+
+// MMA issuers: the chain thread (t0, thread 0) issues the state terms and T4; the output
+// issuer (oi, lane 0 of warp 4) issues T V, T3b and T5, so that they run while the chain works
+// on the CUDA cores (T3b during the Delta pass, T V(c+1) during the state pass).
+struct ChainBarriers {
+  uint64_t full[2];     // stage of chunk c loaded.           waiters: oi (T V), chain (gamma), loader drain
+  uint64_t tv_done[2];  // T V(c) complete.                   waiter: t0
+  uint64_t x_ready[2];  // state terms(c) complete.           waiters: chain, oi
+  uint64_t dp_done[2];  // Delta operands of chunk c in TMEM. waiter: oi
+  uint64_t s_new[2];    // T4(c) complete.                    waiters: chain, oi, loader
+  uint64_t o_done[2];   // T3b(c), T5(c) complete.            waiters: output warps, chain, oi, loader
+  uint64_t o_read[2];   // O(c) read out (one arrival per output warp).  waiter: oi
+  uint64_t drain[2];
+};
+
+__global__ void __launch_bounds__(kChainThreads, 1)
+    gdn_chain_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                     const ChainParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ ChainBarriers bars;
+  __shared__ uint32_t tmem_base_shared;
+  const int warp = warp_id(), lane = lane_id();
+  const int unit = blockIdx.x;
+  const int seq = unit / p.hv, h = unit - seq * p.hv;
+  const int kh = h % p.hk;
+  const int tok0 = p.cu_seqlens[seq];
+  const int len = p.cu_seqlens[seq + 1] - tok0;
+  const int N = len > 0 ? (len + kC - 1) / kC : 0;
+  const int gc0 = p.chunk_base[seq];
+  const size_t state_off = (static_cast<size_t>(seq) * p.hv + h) * kD * kD;
+  auto stage = [&](int c) { return smem + (c & 1) * kStageBytes; };
+  auto params_of = [&](int c) -> const ChunkParams& {
+    return *reinterpret_cast<const ChunkParams*>(stage(c) + kRecParams);
+  };
+
+  if (threadIdx.x == 0) {
+    cta_abort_flag() = 0u;
+    uint64_t* all = reinterpret_cast<uint64_t*>(&bars);
+    for (int i = 0; i < static_cast<int>(sizeof(ChainBarriers) / 8); ++i) mbar_init(&all[i], 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&bars.o_read[i], 4);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_shared, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base_shared;
+
+  if (N == 0) {
+    if (warp < 4) {
+      const int v = threadIdx.x;
+      for (int kk = 0; kk < kD; kk += 4) {
+        float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (p.state_in) val = *reinterpret_cast<const float4*>(p.state_in + state_off + v * kD + kk);
+        *reinterpret_cast<float4*>(p.state_out + state_off + v * kD + kk) = val;
+      }
+    }
+  } else if (warp == 8) {
+    // ======================================================= loader: record + K + V per chunk
+    if (lane == 0) {
+      tma_prefetch_desc(&map_k);
+      tma_prefetch_desc(&map_v);
+      int issued = 0;
+      for (int c = 0; c < N; ++c) {
+        // the stage last held chunk c-2, whose MMAs (and so every read of its record, K and V)
+        // have completed, and whose decay factor was read by the state pass of chunk c-3
+        if (c >= 2 && !(wait2(bars.o_done, c - 2, p.status, kDevTimeoutPipe) &&
+                        wait2(bars.s_new, c - 2, p.status, kDevTimeoutPipe)))
+          break;
+        SPLIT_TRACE(9, c);
+        uint8_t* st = stage(c);
+        uint64_t* bar = &bars.full[c & 1];
+        const uint8_t* rec = p.ws + (static_cast<size_t>(gc0 + c) * p.hv + h) * kRecBytes;
+        mbar_arrive_expect_tx(bar, kRecBytes + 32768);
+        bulk_g2s(st, rec, kRecP, bar);  // T, W, e^G Q
+        bulk_g2s(st + kRecP, rec + kRecP, kRecBytes - kRecP, bar);  // P, params
+        for (int bx = 0; bx < 2; ++bx) {
+          tma_load_3d(st + kSK + bx * 8192, &map_k, bar, bx * 64, kh, tok0 + c * kC);
+          tma_load_3d(st + kSV + bx * 8192, &map_v, bar, bx * 64, h, tok0 + c * kC);
+        }
+        issued = c + 1;
+      }
+      for (int c = max(0, issued - 2); c < issued; ++c) mbar_drain(&bars.full[c & 1], (c >> 1) & 1);
+    }
+  } else if (warp < 4) {
+    // ======================================================= state chain (lane = value row)
+    const int v = threadIdx.x;
+    const uint32_t lb = tmem_addr(tbase, warp * 32, 0);
+    bool ok = wait2_warp(bars.full, 0, p.status, kDevTimeoutTma);
+    if (ok) {
+      const float gam = params_of(0).gamma_c;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sv[64];
+#pragma unroll
+        for (int j = 0; j < 64; j += 4) {
+          float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (p.state_in) val = *reinterpret_cast<const float4*>(p.state_in + state_off + v * kD + half * 64 + j);
+          sv[j] = __float_as_uint(val.x);
+          sv[j + 1] = __float_as_uint(val.y);
+          sv[j + 2] = __float_as_uint(val.z);
+          sv[j + 3] = __float_as_uint(val.w);
+        }
+        store_split32<0>(lb + kColShi + 32 * half, lb + kColSlo + 32 * half, sv);
+        store_split32<32>(lb + kColShi + 32 * half + 16, lb + kColSlo + 32 * half + 16, sv);
+#pragma unroll
+        for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
+        tmem_st32(lb + kColS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_st32(lb + kColS + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      }
+      tmem_wait_st();
+    }
+    tc_fence_before();
+    ok = named_sync_and(1, 128, ok);
+    for (int c = 0; ok && c < N; ++c) {
+      const uint32_t st = smem_u32(stage(c));
+      // --- (thread 0) the state terms once T V(c) is in the X region (every exit from this loop
+      //     goes through a named_sync_and, so the four warps leave together)
+      if (v == 0) {
+        const bool r = wait2(bars.tv_done, c, p.status, kDevTimeoutMma);
+        SPLIT_TRACE(0, c);
+        if (r) {
+          tc_fence_after();
+          const uint32_t id128 = make_idesc(128, 128, 1, 0, 1), id64 = make_idesc(128, 64, 1, 0, 1);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16_ts(tbase + kColX, tbase + kColShi + 8 * kk, make_sdesc_sw128(st + kRecW + kk * 2048, 16384, 1024),
+                         id128, 1u);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16_ts(tbase + kColX, tbase + kColSlo + 8 * kk, make_sdesc_sw128(st + kRecW + kk * 2048, 16384, 1024),
+                         id64, 1u);
+          umma_commit(&bars.x_ready[c & 1]);
+          SPLIT_TRACE(1, c);
+        }
+      }
+      // --- Delta pass
+      const bool xr = wait2_warp(bars.x_ready, c, p.status, kDevTimeoutMma);
+      tc_fence_after();
+      if (v == 0) SPLIT_TRACE(2, c);
+      if (xr) {
+        const ChunkParams& pc = params_of(c);
+        uint32_t d[64];
+        tmem_ld64(lb + kColX, d);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t e[32];
+          tmem_ld32(lb + kColX + 64 + 32 * hf, e);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            d[32 * hf + j] = __float_as_uint(__uint_as_float(d[32 * hf + j]) + __uint_as_float(e[j]));
+        }
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const int t = 32 * hf + 2 * j;
+            const float4 e4 = *reinterpret_cast<const float4*>(&pc.egr[t]);
+            split_pack(__uint_as_float(d[t]) * e4.x, __uint_as_float(d[t + 1]) * e4.y, hi[j], lo[j]);
+            split_pack(__uint_as_float(d[t + 2]) * e4.z, __uint_as_float(d[t + 3]) * e4.w, hi[j + 1], lo[j + 1]);
+          }
+          tmem_st16(lb + kColX + 16 * hf, hi);
+          tmem_st16(lb + kColX + 32 + 16 * hf, lo);
+        }
+        {
+          uint32_t pk[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) pk[j] = pack_bf16x2(__uint_as_float(d[2 * j]), __uint_as_float(d[2 * j + 1]));
+          tmem_st32(lb + kColX + 64, pk);
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      if (!named_sync_and(1, 128, xr)) { ok = false; break; }
+      if (v == 0) {
+        SPLIT_TRACE(3, c);
+        mbar_arrive(&bars.dp_done[c & 1]);  // T5(c) may read Delta (and T3b has S_hi(c) to itself)
+        tc_fence_after();
+        const uint32_t id_upd = make_idesc(128, 128, 1, 0, 1);
+#pragma unroll
+        for (int part = 0; part < 2; ++part)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16_ts(tbase + kColS, tbase + kColX + 32 * part + 8 * kk,
+                         make_sdesc_sw128(st + kSK + kk * 2048, 8192, 1024), id_upd, 1u);
+        umma_commit(&bars.s_new[c & 1]);
+        SPLIT_TRACE(4, c);
+      }
+      // --- state pass (the hi/lo copies are overwritten only after T3b(c) completed: o_done)
+      const bool last = (c == N - 1);
+      bool sr = wait2_warp(bars.s_new, c, p.status, kDevTimeoutMma);
+      tc_fence_after();
+      if (v == 0) SPLIT_TRACE(6, c);
+      float gam = 1.0f;
+      if (sr && !last) {
+        sr = wait2_warp(bars.full, c + 1, p.status, kDevTimeoutTma) &&
+             wait2_warp(bars.o_done, c, p.status, kDevTimeoutMma);
+        gam = params_of(c + 1).gamma_c;
+      }
+      if (v == 0) SPLIT_TRACE(7, c);
+#pragma unroll 1
+      for (int qt = 0; sr && qt < 4; ++qt) {
+        uint32_t sv[32];
+        tmem_ld32(lb + kColS + qt * 32, sv);
+        if (last) {
+          float* dst = p.state_out + state_off + v * kD + qt * 32;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
+                                                              __uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3]));
+        } else {
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) split_pack(__uint_as_float(sv[2 * j]), __uint_as_float(sv[2 * j + 1]), hi[j], lo[j]);
+          tmem_st16(lb + kColShi + 16 * qt, hi);
+          tmem_st16(lb + kColSlo + 16 * qt, lo);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
+          tmem_st32(lb + kColS + qt * 32, sv);
+        }
+      }
+      if (!last) {
+        tmem_wait_st();
+        tc_fence_before();
+        if (!named_sync_and(1, 128, sr)) { ok = false; break; }
+        if (v == 0) SPLIT_TRACE(8, c);
+      }
+    }
+    if (v == 0) {
+      umma_commit(&bars.drain[0]);
+      mbar_drain(&bars.drain[0], 0);
+    }
+  } else {
+    // ======================================================= output pass (warps 4-7)
+    const int r = threadIdx.x - 128;
+    const uint32_t lb = tmem_addr(tbase, (warp & 3) * 32, 0);
+    const bool oi = (warp == 4 && lane == 0);
+    bool ok = true;
+    // T V(c) = V^T [T_hi | T_lo]^T into the X region (accumulate 0)
+    auto issue_tv = [&](int c) {
+      const uint32_t st = smem_u32(stage(c));
+      const uint32_t id_v = make_idesc(128, 128, 1, 1, 1);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_bf16_ss(tbase + kColX, make_sdesc_sw128(st + kSV + kk * 2048, 8192, 1024),
+                     make_sdesc_sw128(st + kRecT + kk * 2048, 8192, 1024), id_v, kk > 0 ? 1u : 0u);
+      umma_commit(&bars.tv_done[c & 1]);
+    };
+    if (oi) {
+      ok = wait2(bars.full, 0, p.status, kDevTimeoutTma);
+      if (ok) {
+        tc_fence_after();
+        issue_tv(0);
+      }
+    }
+    for (int co = 0; co < N; ++co) {
+      if (oi && ok) {
+        // T3b(co) once the state terms have read S_hi(co)'s chunk (x_ready) and O(co-1) is read
+        const uint32_t st = smem_u32(stage(co));
+        ok = wait2(bars.x_ready, co, p.status, kDevTimeoutMma) &&
+             (co == 0 || wait2(bars.o_read, co - 1, p.status, kDevTimeoutPipe));
+        if (ok) {
+          tc_fence_after();
+          const uint32_t id = make_idesc(128, 64, 1, 0, 0);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16_ts(tbase + kColO, tbase + kColShi + 8 * kk, kmaj_desc(st + kRecQ, kk, 8192), id, kk > 0 ? 1u : 0u);
+          SPLIT_TRACE(11, co);
+          ok = wait2(bars.dp_done, co, p.status, kDevTimeoutPipe);
+        }
+        if (ok) {
+          // T5(co): O^T += Delta^T P^T
+          tc_fence_after();
+          const uint32_t id = make_idesc(128, 64, 1, 0, 0);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16_ts(tbase + kColO, tbase + kColX + 64 + 8 * kk, make_sdesc_sw128(st + kRecP + kk * 32, 16, 1024),
+                         id, 1u);
+          umma_commit(&bars.o_done[co & 1]);
+          SPLIT_TRACE(5, co);
+          // T V(co+1) once T4(co) and T5(co) have read the X region and the next stage is loaded
+          if (co + 1 < N) {
+            ok = wait2(bars.o_done, co, p.status, kDevTimeoutMma) && wait2(bars.s_new, co, p.status, kDevTimeoutMma) &&
+                 wait2(bars.full, co + 1, p.status, kDevTimeoutTma);
+            if (ok) {
+              tc_fence_after();
+              issue_tv(co + 1);
+              SPLIT_TRACE(12, co + 1);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (!wait2_warp(bars.o_done, co, p.status, kDevTimeoutMma)) break;
+      tc_fence_after();
+      if (r == 0) SPLIT_TRACE(10, co);
+      uint32_t o[64];
+      tmem_ld64(lb + kColO, o);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.o_read[co & 1]);
+      // token pair (2i, 2i+1): the even lane of a lane pair stores (O[2i][v], O[2i][v+1]), the
+      // odd lane (O[2i+1][v-1], O[2i+1][v]), one 4-byte store each
+      const int nv = min(kC, len - co * kC);
+      const bool odd = (lane & 1) != 0;
+      const size_t tstride = static_cast<size_t>(p.hv) * kD;
+      uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (static_cast<size_t>(tok0 + co * kC) * p.hv + h) * kD +
+                                                  (r & ~1)) + (odd ? tstride / 2 : 0);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = __uint_as_float(o[2 * i]), b = __uint_as_float(o[2 * i + 1]);
+        const float other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
+        const uint32_t packed = odd ? pack_bf16x2(other, b) : pack_bf16x2(a, other);
+        if (2 * i + (odd ? 1 : 0) < nv) dst[i * tstride] = packed;
+      }
+    }
+    if (oi) {
+      umma_commit(&bars.drain[1]);
+      mbar_drain(&bars.drain[1], 0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+}  // namespace split
+}  // namespace gdn
+}  // namespace tokmix
+
+#ifdef TOKMIX_GDN_TRACE
+extern "C" int tokmix_gdn_split_trace_read(unsigned long long* host, int n) {
+  using namespace tokmix::gdn::split;
+  const int count = n < kTrEvents * kTrChunks ? n : kTrEvents * kTrChunks;
+  return cudaMemcpyFromSymbol(host, g_split_trace, sizeof(unsigned long long) * count) == cudaSuccess ? count : -1;
+}
+#endif
+
+extern "C" long long tokmix_gdn_split_workspace_bytes(int total_chunks, int heads_v) {
+  if (total_chunks < 0 || heads_v < 0) return -1;
+  return static_cast<long long>(total_chunks) * heads_v * tokmix::gdn::split::kRecBytes;
+}
+
+extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void* v, const float* g,
+                                        const float* beta, const float* initial_state, void* out, float* final_state,
+                                        const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev, int num_seqs,
+                                        int total_tokens, int total_chunks, int heads_k, int heads_v, int head_dim_k,
+                                        int head_dim_v, float scale, int io_dtype, void* workspace,
+                                        long long workspace_bytes, uint32_t* status, void* stream) {
+  using namespace tokmix;
+  using namespace tokmix::gdn;
+  using namespace tokmix::gdn::split;
+  if (num_seqs < 0 || total_tokens < 0 || total_chunks < 0 || heads_k <= 0 || heads_v <= 0)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: negative or zero size");
+  if (num_seqs == 0) return TOKMIX_OK;
+  if (!q || !k || !v || !g || !beta || !out || !final_state || !cu_seqlens_dev || !chunk_base_dev || !status)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: null pointer argument");
+  if (heads_v % heads_k != 0)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT,
+                "tokmix_gdn_prefill_split: heads_v (%d) must be a multiple of heads_k (%d)", heads_v, heads_k);
+  if (head_dim_k != kD || head_dim_v != kD)
+    return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_gdn_prefill_split: head dims must be 128 (got %d, %d)", head_dim_k,
+                head_dim_v);
+  if (io_dtype != TOKMIX_DTYPE_BF16)
+    return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_gdn_prefill_split: only bf16 q/k/v/out are supported by the kernel");
+  if (!std::isfinite(scale)) return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: scale must be finite");
+  const long long need = tokmix_gdn_split_workspace_bytes(total_chunks, heads_v);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: workspace of %lld bytes needed (got %lld)", need,
+                workspace_bytes);
+  for (const void* ptr : {q, k, v, static_cast<const void*>(initial_state), static_cast<const void*>(final_state),
+                          static_cast<const void*>(workspace)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+      return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: tensors must be 16-byte aligned");
+  if (const int rc = check_device()) return rc;
+  const long long units = static_cast<long long>(num_seqs) * heads_v;
+  if (units > 0x7FFFFFFFll)
+    return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_gdn_prefill_split: problem too large");
+
+  const uint64_t rows = static_cast<uint64_t>(total_tokens > 0 ? total_tokens : 1);
+  CUtensorMap mq, mk, mv;
+  {
+    uint64_t dims_k[3] = {kD, static_cast<uint64_t>(heads_k), rows};
+    uint64_t strides_k[2] = {kD * 2, static_cast<uint64_t>(heads_k) * kD * 2};
+    uint64_t dims_v[3] = {kD, static_cast<uint64_t>(heads_v), rows};
+    uint64_t strides_v[2] = {kD * 2, static_cast<uint64_t>(heads_v) * kD * 2};
+    uint32_t box[3] = {64, 1, 64};
+    if (!encode_tiled(&mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, dims_k, strides_k, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tiled(&mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, k, dims_k, strides_k, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tiled(&mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, v, dims_v, strides_v, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+      return TOKMIX_ERR_INVALID_ARGUMENT;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (total_chunks > 0) {
+    PrepParams pp{};
+    pp.g = g;
+    pp.beta = beta;
+    pp.cu_seqlens = cu_seqlens_dev;
+    pp.chunk_base = chunk_base_dev;
+    pp.ws = static_cast<uint8_t*>(workspace);
+    pp.num_seqs = num_seqs;
+    pp.hk = heads_k;
+    pp.hv = heads_v;
+    pp.scale = scale;
+    pp.status = status;
+    const int smem = kPSmem + 1024;
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_prep_kernel), smem))
+      return check_launch("tokmix_gdn_prefill_split: cudaFuncSetAttribute (prep)");
+    gdn_prep_kernel<<<dim3(static_cast<unsigned>(total_chunks), static_cast<unsigned>(heads_v)), kPrepThreads, smem, s>>>(
+        mq, mk, pp);
+    if (const int rc = check_launch("tokmix_gdn_prefill_split (prep)")) return rc;
+  }
+  ChainParams cp{};
+  cp.state_in = initial_state;
+  cp.state_out = final_state;
+  cp.out = static_cast<__nv_bfloat16*>(out);
+  cp.cu_seqlens = cu_seqlens_dev;
+  cp.chunk_base = chunk_base_dev;
+  cp.ws = static_cast<const uint8_t*>(workspace);
+  cp.hk = heads_k;
+  cp.hv = heads_v;
+  cp.status = status;
+  const int smem = kCSmem + 1024;
+  if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_chain_kernel), smem))
+    return check_launch("tokmix_gdn_prefill_split: cudaFuncSetAttribute (chain)");
+  gdn_chain_kernel<<<static_cast<unsigned>(units), kChainThreads, smem, s>>>(mk, mv, cp);
+  return check_launch("tokmix_gdn_prefill_split (chain)");
+}

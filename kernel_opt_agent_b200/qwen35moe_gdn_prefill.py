@@ -4,8 +4,11 @@
     KERNEL_TYPE, kernel_fn(q, k, v, g, beta, state, scale=None) -> [out, final_state],
     get_inputs, get_flops, get_bytes
 
-``kernel_fn`` runs the sm_100a chunked kernel in libtokmix.so (``tokmix_gdn_prefill``); there is
-no fallback.  Argument meaning follows the reference (``kernels/qwen35moe_gdn_prefill.py:107-151``):
+``kernel_fn`` runs the sm_100a chunked kernels in libtokmix.so; there is no fallback.  Two
+schedules compute the same result: one CTA per (sequence, value head) doing everything
+(``tokmix_gdn_prefill``), or, when there are fewer such units than SMs, a chunk-parallel
+preparation launch followed by a state-chain launch (``tokmix_gdn_prefill_split``, which needs a
+workspace of about 73 KB per (chunk, value head), taken from PyTorch's caching allocator).  Argument meaning follows the reference (``kernels/qwen35moe_gdn_prefill.py:107-151``):
 q, k [B,T,Hk,128]; v [B,T,Hv,128]; g (log decay), beta [B,T,Hv]; state [B,Hv,128(v),128(k)];
 value head h reads key head h % Hk; default scale 128**-0.5; returns [out like v, final_state fp32].
 
@@ -16,6 +19,8 @@ Extensions over the reference module:
 * ``cu_seqlens`` (keyword): variable-length sequences packed along T with q.shape[0] == 1 and
   one initial state per sequence (state [N,Hv,128,128]); ``state=None`` means zero states.
 * any Hk dividing Hv (the reference fixes Hk=16, Hv=32).
+* ``mode`` (keyword): "auto" (default), "fused" or "split" selects the schedule; the environment
+  variable TOKMIX_GDN_MODE overrides "auto".
 """
 
 from __future__ import annotations
@@ -31,22 +36,26 @@ D = 128
 H_K = 16
 H_V = 32
 _CHECK_STATUS = os.environ.get("TOKMIX_CHECK_STATUS", "0") == "1"
+_SPLIT_MAX_WORKSPACE = 1 << 30  # bytes; larger problems use the one-launch schedule
 
 _meta_cache: dict = {}
 
 
 def _device_meta(lengths: tuple[int, ...], device: torch.device):
-    """cu_seqlens (int32) and the longest-first scheduling order, uploaded once per shape."""
+    """cu_seqlens (int32), the longest-first scheduling order and the per-sequence first chunk
+    (int32, for the split schedule) with the chunk count, uploaded once per shape."""
     key = (lengths, device)
     hit = _meta_cache.get(key)
     if hit is None:
-        cu = [0]
+        cu, cb = [0], [0]
         for n in lengths:
             cu.append(cu[-1] + n)
+            cb.append(cb[-1] + (n + 63) // 64)
         order = sorted(range(len(lengths)), key=lambda i: -lengths[i])
         cu_t = torch.tensor(cu, dtype=torch.int32).to(device)
         order_t = torch.tensor(order, dtype=torch.int32).to(device) if len(set(lengths)) > 1 else None
-        hit = (cu_t, order_t)
+        cb_t = torch.tensor(cb, dtype=torch.int32).to(device)
+        hit = (cu_t, order_t, cb_t, cb[-1])
         if len(_meta_cache) > 256:
             _meta_cache.clear()
         _meta_cache[key] = hit
@@ -107,6 +116,7 @@ def kernel_fn(
     scale: float | None = None,
     *,
     cu_seqlens=None,
+    mode: str = "auto",
 ) -> list[torch.Tensor]:
     nseq, hk, hv = _validate(q, k, v, g, beta, state, cu_seqlens)
     if scale is None:
@@ -123,7 +133,7 @@ def kernel_fn(
         out = torch.empty(v.shape, dtype=io_dtype, device=dev)
         fs = state.to(torch.float32).clone() if state is not None else torch.zeros((nseq, hv, D, D), device=dev)
         return [out, fs]
-    cu_t, order_t = _device_meta(lengths, dev)
+    cu_t, order_t, cb_t, total_chunks = _device_meta(lengths, dev)
     qb = q.to(torch.bfloat16).contiguous()
     kb = k.to(torch.bfloat16).contiguous()
     vb = v.to(torch.bfloat16).contiguous()
@@ -134,18 +144,42 @@ def kernel_fn(
     final_state = torch.empty((nseq, hv, D, D), dtype=torch.float32, device=dev)
     lib = _lib.load()
     word = _lib.status_word(dev)
+    use_split = _use_split(mode, nseq * hv, total_chunks, hv, dev)
     with torch.cuda.device(dev):
-        rc = lib.tokmix_gdn_prefill(
-            qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
-            st.data_ptr() if st is not None else None, out.data_ptr(), final_state.data_ptr(),
-            cu_t.data_ptr(), order_t.data_ptr() if order_t is not None else None,
-            nseq, total, hk, hv, D, D, float(scale), _lib.DTYPE_BF16, word.data_ptr(), _lib.stream_ptr(dev))
+        if use_split:
+            nbytes = int(lib.tokmix_gdn_split_workspace_bytes(total_chunks, hv))
+            ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+            rc = lib.tokmix_gdn_prefill_split(
+                qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
+                st.data_ptr() if st is not None else None, out.data_ptr(), final_state.data_ptr(),
+                cu_t.data_ptr(), cb_t.data_ptr(), nseq, total, total_chunks, hk, hv, D, D, float(scale),
+                _lib.DTYPE_BF16, ws.data_ptr(), ws.numel(), word.data_ptr(), _lib.stream_ptr(dev))
+        else:
+            rc = lib.tokmix_gdn_prefill(
+                qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
+                st.data_ptr() if st is not None else None, out.data_ptr(), final_state.data_ptr(),
+                cu_t.data_ptr(), order_t.data_ptr() if order_t is not None else None,
+                nseq, total, hk, hv, D, D, float(scale), _lib.DTYPE_BF16, word.data_ptr(), _lib.stream_ptr(dev))
     _lib.check(rc, "qwen35moe_gdn_prefill")
     if _CHECK_STATUS:
         _lib.raise_on_device_status(word, "qwen35moe_gdn_prefill")
     if io_dtype != torch.bfloat16:
         out = out.to(io_dtype)
     return [out, final_state]
+
+
+def _use_split(mode: str, units: int, total_chunks: int, hv: int, dev: torch.device) -> bool:
+    """Split schedule when the one-CTA-per-unit schedule would leave SMs idle."""
+    if mode == "auto":
+        mode = os.environ.get("TOKMIX_GDN_MODE", "auto")
+    if mode == "fused":
+        return False
+    if mode == "split":
+        return True
+    if mode != "auto":
+        raise ValueError(f"mode must be 'auto', 'fused' or 'split' (got {mode!r})")
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    return units < sms and _lib.load().tokmix_gdn_split_workspace_bytes(total_chunks, hv) <= _SPLIT_MAX_WORKSPACE
 
 
 def check_device_status(device: torch.device | None = None) -> None:

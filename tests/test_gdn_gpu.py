@@ -30,8 +30,8 @@ def _oracle(inp, threads):
                                 nthreads=threads)
 
 
-def _check(inp, threads, out_tol=OUT_TOL, state_tol=STATE_TOL):
-    out, fs = gdn.kernel_fn(**inp)
+def _check(inp, threads, out_tol=OUT_TOL, state_tol=STATE_TOL, mode="auto"):
+    out, fs = gdn.kernel_fn(**inp, mode=mode)
     gdn.check_device_status(out.device)
     o_ref, s_ref = _oracle(inp, threads)
     got_o, got_s = _np(out), _np(fs)
@@ -59,6 +59,28 @@ def test_gdn_matches_oracle(cuda_device, oracle_threads, b, t, hk, hv, state_std
 def test_gdn_varlen_with_empty_and_tail_sequences(cuda_device, oracle_threads):
     inp = gcfg.random_inputs(1, 0, lengths=[1, 63, 64, 65, 200, 0, 129], seed=5, state_std=0.02)
     _check(inp, oracle_threads)
+
+
+# Both schedules (one CTA per unit; chunk-parallel preparation + state-chain launch) on the same
+# inputs: each against the oracle, and against each other.
+@pytest.mark.parametrize("mode", ["fused", "split"])
+@pytest.mark.parametrize("b,t,hk,hv,state_std,lengths", [
+    (1, 1, 16, 32, 0.0, None),
+    (2, 65, 2, 4, 0.02, None),
+    (3, 129, 4, 8, 0.02, None),
+    (1, 0, 2, 4, 0.02, [1, 63, 64, 65, 200, 0, 129]),
+])
+def test_gdn_schedules_match_oracle(cuda_device, oracle_threads, mode, b, t, hk, hv, state_std, lengths):
+    inp = gcfg.random_inputs(b, t, seed=t + hk + 1, state_std=state_std, hk=hk, hv=hv, lengths=lengths)
+    _check(inp, oracle_threads, mode=mode)
+
+
+def test_gdn_schedules_agree(cuda_device):
+    inp = gcfg.random_inputs(2, 300, seed=9, state_std=0.02, hk=4, hv=8)
+    o1, s1 = gdn.kernel_fn(**inp, mode="fused")
+    o2, s2 = gdn.kernel_fn(**inp, mode="split")
+    np.testing.assert_allclose(_np(o1), _np(o2), atol=1e-2, rtol=1e-2)
+    np.testing.assert_allclose(_np(s1), _np(s2), atol=2e-5, rtol=2e-4)
 
 
 def test_gdn_reference_fixture_fp32_io(cuda_device, oracle_threads):
@@ -107,10 +129,11 @@ def test_gdn_matches_reference_kernel_golden(cuda_device, name):
     np.testing.assert_allclose(_np(fs)[:, meta["state_heads"]], ref["final_state"], **tol_s)
 
 
-def test_gdn_config1_full(cuda_device, oracle_threads):
+@pytest.mark.parametrize("mode", ["fused", "split"])
+def test_gdn_config1_full(cuda_device, oracle_threads, mode):
     """B=1, T=2048, Hk=16, Hv=32, zero state: every output and the fp32 final state."""
     inp = gcfg.random_inputs(1, 2048, seed=0)
-    _check(inp, oracle_threads)
+    _check(inp, oracle_threads, mode=mode)
 
 
 def test_gdn_state_continuation_is_exact(cuda_device):
