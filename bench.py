@@ -196,7 +196,8 @@ def run_gdn_batch(device, rank, world, steps, warmup, batch=1):
     algo = gdn.algorithmic_bytes(2048 * batch, batch)
     ms = total_s / steps * 1e3
     return {"tokens_per_step": tokens, "ms": ms, "value": tokens * steps / total_s / 1e6, "unit": "Mtok/s",
-            "kernel_ms_local": statistics.mean(per), "algo_bytes": algo, "inp": inp}
+            "kernel_ms_local": statistics.mean(per), "algo_bytes": algo, "inp": inp,
+            "schedule": gdn.schedule(inp["q"], inp["v"])}
 
 
 def headline_config(world: int) -> dict:
@@ -223,6 +224,7 @@ def run_gdn_varlen(device, rank, world, steps, warmup, verify=False):
     algo = gdn.algorithmic_bytes(tokens, len(lengths), hk=b - a, hv=2 * (b - a))
     res = {"tokens_per_step": tokens, "ms": total_s / steps * 1e3, "value": tokens * steps / total_s / 1e6,
            "unit": "Mtok/s", "kernel_ms_local": statistics.mean(per), "algo_bytes": algo,
+           "schedule": gdn.schedule(inp["q"], inp["v"], inp.get("cu_seqlens")),
            "config": {"workload": "gdn_varlen", "n_seqs": 8, "lengths": lengths, "total_tokens": tokens,
                       "hk": HK, "hv": HV, "head_dim": D, "chunk": 64, "initial_state": "N(0,0.02)",
                       "shard": f"key heads {HK // world}/rank (+ the value heads reading them)"}}
@@ -408,10 +410,14 @@ def main():
                     "traffic": NCU_TRAFFIC_BYTES.get(w), "kernel": "tokmix::fa2::fa2_fwd_kernel<128>",
                     "kernel_ms": kms}
         ach = r["algo_bytes"] / (kms / 1e3) / 1e9
+        if r.get("schedule") == "split":  # one step = the preparation launch + the state-chain launch
+            kern = "tokmix::gdn::split::gdn_prep_kernel + tokmix::gdn::split::gdn_chain_kernel (one step)"
+        else:
+            kern = "tokmix::gdn::gdn_prefill_kernel"
         return {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": ach / peaks["hbm_gbs"], "peak_source": peaks["source"] + " copy bandwidth",
                 "traffic": NCU_TRAFFIC_BYTES.get(w), "algorithmic_bytes": r["algo_bytes"],
-                "kernel": "tokmix::gdn::gdn_prefill_kernel", "kernel_ms": kms}
+                "kernel": kern, "kernel_ms": kms, "schedule": r.get("schedule", "fused")}
 
     if rank == 0:
         hr = results[head]
@@ -424,7 +430,7 @@ def main():
                 "data": "synthetic (seeded, B200 config shapes)", "config": cfg,
                 "roofline": roofline(head, hr), "cpu_baseline": cpu,
                 "e2e": e2e if e2e is not None else None,
-                "gpu_launches": args.steps, "clocks": clocks,
+                "gpu_launches": args.steps * (2 if hr.get("schedule") == "split" else 1), "clocks": clocks,
                 "also": {w: {"value": r["value"], "unit": r["unit"], "ms_per_step": r["ms"],
                              "roofline": roofline(w, r), **({"config": r["config"]} if "config" in r else {}),
                              **({"verified_vs_one_gpu": r["verified_vs_one_gpu"]}

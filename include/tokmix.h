@@ -113,14 +113,21 @@ int tokmix_gdn_prefill_noalloc(const void* q, const void* k, const void* v, cons
  * tokmix_gdn_prefill (up to fp32 summation order), plus:
  *   chunk_base_dev:   device int32 [num_seqs + 1], chunk_base[n] = sum over m < n of
  *                     ceil(len_m / 64); chunk_base[num_seqs] = total_chunks
+ *   record_order_dev: device int32 [total_chunks * heads_v] or NULL: the records
+ *                     (global chunk * heads_v + value head) in chunk-major order (chunk 0 of every
+ *                     sequence and head first).  When given and the device can run it, both
+ *                     stages share ONE cooperative launch: chain CTAs consume each chunk's record
+ *                     as soon as preparation CTAs on the other SMs have written it.  NULL (or a
+ *                     device where the cooperative launch is refused) gives two ordinary launches.
  *   workspace:        device memory of at least tokmix_gdn_split_workspace_bytes(total_chunks,
  *                     heads_v) bytes, 16-byte aligned (contents need no initialisation)
  * No counterpart in the reference (its prefill is one kernel chain per layer call). */
 int tokmix_gdn_prefill_split(const void* q, const void* k, const void* v, const float* g, const float* beta,
                              const float* initial_state, void* out, float* final_state, const int32_t* cu_seqlens_dev,
-                             const int32_t* chunk_base_dev, int num_seqs, int total_tokens, int total_chunks,
-                             int heads_k, int heads_v, int head_dim_k, int head_dim_v, float scale, int io_dtype,
-                             void* workspace, long long workspace_bytes, uint32_t* status, void* stream);
+                             const int32_t* chunk_base_dev, const int32_t* record_order_dev, int num_seqs,
+                             int total_tokens, int total_chunks, int heads_k, int heads_v, int head_dim_k,
+                             int head_dim_v, float scale, int io_dtype, void* workspace, long long workspace_bytes,
+                             uint32_t* status, void* stream);
 
 /* Workspace size of tokmix_gdn_prefill_split in bytes (-1 for negative arguments). */
 long long tokmix_gdn_split_workspace_bytes(int total_chunks, int heads_v);

@@ -56,6 +56,7 @@ constexpr uint32_t kColS = 0, kColShi = 128, kColSlo = 192, kColX = 256, kColO =
 #ifdef TOKMIX_GDN_TRACE
 constexpr int kTrChunks = 64, kTrEvents = 16;
 __device__ unsigned long long g_split_trace[kTrEvents * kTrChunks];
+__device__ unsigned long long g_cta_end[1024];  // %globaltimer at the end of each CTA
 #define SPLIT_TRACE(ev, c)                                                                               \
   do {                                                                                                   \
     if (blockIdx.x == 0 && (c) < kTrChunks) g_split_trace[(ev) * kTrChunks + (c)] = clock64();          \
@@ -63,6 +64,16 @@ __device__ unsigned long long g_split_trace[kTrEvents * kTrChunks];
 #else
 #define SPLIT_TRACE(ev, c) \
   do {                     \
+  } while (0)
+#endif
+#ifdef TOKMIX_GDN_TRACE
+#define CTA_END_TRACE()                                                                  \
+  do {                                                                                   \
+    if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_end[blockIdx.x] = global_timer_ns(); \
+  } while (0)
+#else
+#define CTA_END_TRACE() \
+  do {                  \
   } while (0)
 #endif
 
@@ -96,15 +107,15 @@ __device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t 
                : "memory");
 }
 
-__global__ void __launch_bounds__(kPrepThreads, 3)
-    gdn_prep_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                    const PrepParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar_in, bar_mma;
-  __shared__ uint32_t tmem_base_shared;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gc = blockIdx.x, h = blockIdx.y;
+// One record: the preparation of chunk gc of value head h by a group of 128 threads (group-local
+// `tid`; the group's warp w must sit on TMEM lane quadrant w).  `smem` is the group's 1024-byte
+// aligned region of kPSmem bytes, `tbase` its 64 TMEM columns, `bar_id` its named barrier;
+// bar_in completes once per record (`in_parity`), bar_mma twice (parities 0, 1).  Returns false
+// if a wait ran out.  The record (T, -W, e^G Q, P, params) is written to p.ws directly.
+__device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUtensorMap* map_k, const PrepParams& p,
+                                            int gc, int h, uint8_t* smem, uint64_t* bar_in, uint32_t in_parity,
+                                            uint64_t* bar_mma, uint32_t tbase, int tid, int bar_id) {
+  const int warp = tid >> 5, lane = tid & 31;
   int lo = 0, hi = p.num_seqs;  // sequence of global chunk gc: chunk_base[lo] <= gc < chunk_base[lo + 1]
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
@@ -121,26 +132,10 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
   uint8_t* rec = p.ws + (static_cast<size_t>(gc) * p.hv + h) * kRecBytes;
 
   if (tid == 0) {
-    cta_abort_flag() = 0u;
-    mbar_init(&bar_in, 1);
-    mbar_init(&bar_mma, 1);
-    fence_barrier_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(&tmem_base_shared, 64);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = tmem_base_shared;
-  if (tid == 0) {
-    tma_prefetch_desc(&map_q);
-    tma_prefetch_desc(&map_k);
-    mbar_arrive_expect_tx(&bar_in, 32768);
+    mbar_arrive_expect_tx(bar_in, 32768);
     for (int bx = 0; bx < 2; ++bx) {
-      tma_load_3d(smem + kPSlot + bx * 16384, &map_k, &bar_in, bx * 64, kh, row0);
-      tma_load_3d(smem + kPSlot + bx * 16384 + 8192, &map_q, &bar_in, bx * 64, kh, row0);
+      tma_load_3d(smem + kPSlot + bx * 16384, map_k, bar_in, bx * 64, kh, row0);
+      tma_load_3d(smem + kPSlot + bx * 16384 + 8192, map_q, bar_in, bx * 64, kh, row0);
     }
   }
   if (warp == 3) {
@@ -152,25 +147,21 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
     const float bb = t1 < n_valid ? p.beta[(base + t1) * p.hv + h] : 0.0f;
     chunk_decay_params(pc, ga, gb, ba, bb, n_valid, lane);
   }
-  __syncthreads();
+  named_sync(bar_id, 128);
   if (tid < kParamsBytes / 16)
     reinterpret_cast<uint4*>(rec + kRecParams)[tid] = reinterpret_cast<const uint4*>(smem + kPParams)[tid];
   // --- T1: [K;Q] K^T
-  bool ok = true;
-  if (tid == 0) {
-    ok = mbar_wait(&bar_in, 0, p.status, kDevTimeoutTma);
-    if (ok) {
-      tc_fence_after();
-      const uint32_t id = make_idesc(128, 64, 1, 0, 0);
-      const uint32_t slot = smem_u32(smem + kPSlot);
+  if (tid == 0 && mbar_wait(bar_in, in_parity, p.status, kDevTimeoutTma)) {
+    tc_fence_after();
+    const uint32_t id = make_idesc(128, 64, 1, 0, 0);
+    const uint32_t slot = smem_u32(smem + kPSlot);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        umma_bf16_ss(tbase, kmaj_desc(slot, kk, 16384), kmaj_desc(slot, kk, 16384), id, kk > 0 ? 1u : 0u);
-      umma_commit(&bar_mma);
-    }
+    for (int kk = 0; kk < 8; ++kk)
+      umma_bf16_ss(tbase, kmaj_desc(slot, kk, 16384), kmaj_desc(slot, kk, 16384), id, kk > 0 ? 1u : 0u);
+    umma_commit(bar_mma);
   }
-  // --- read-out: rows 0-63 (K K^T) -> L, rows 64-127 (Q K^T) -> P and scale e^G q in place
-  ok = __all_sync(0xffffffffu, mbar_wait(&bar_mma, 0, p.status, kDevTimeoutMma));
+  // --- read-out: rows 0-63 (K K^T) -> L, rows 64-127 (Q K^T) -> P and e^G-scaled Q
+  bool ok = __all_sync(0xffffffffu, mbar_wait(bar_mma, 0, p.status, kDevTimeoutMma));
   if (ok) {
     tc_fence_after();
     uint32_t row[64];
@@ -184,33 +175,61 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
     }
   }
   tc_fence_before();
-  ok = named_sync_and(1, 128, ok);
-  if (ok) {
-    solve_inverse(Ls, Xs, tid, 1);
-    write_t_tiles(Xs, pc, tid, rec + kRecT, smem + kPL);  // T to the record, T diag(e^G) over the dead L
-    fence_async_smem();
-    named_sync(1, 128);
-    // --- T2: W^T = K^T (TG_hi + TG_lo)^T
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t id = make_idesc(128, 64, 1, 1, 1);
-      const uint32_t kt = smem_u32(smem + kPSlot), tg = smem_u32(smem + kPL);
+  ok = named_sync_and(bar_id, 128, ok);
+  if (!ok) return false;
+  solve_inverse(Ls, Xs, tid, bar_id);
+  write_t_tiles(Xs, pc, tid, rec + kRecT, smem + kPL);  // T to the record, T diag(e^G) over the dead L
+  fence_async_smem();
+  named_sync(bar_id, 128);
+  // --- T2: W^T = K^T (TG_hi + TG_lo)^T
+  if (tid == 0) {
+    tc_fence_after();
+    const uint32_t id = make_idesc(128, 64, 1, 1, 1);
+    const uint32_t kt = smem_u32(smem + kPSlot), tg = smem_u32(smem + kPL);
 #pragma unroll
-      for (int part = 0; part < 2; ++part)
+    for (int part = 0; part < 2; ++part)
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_bf16_ss(tbase, make_sdesc_sw128(kt + kk * 2048, 16384, 1024),
-                       make_sdesc_sw128(tg + part * 8192 + kk * 2048, 16384, 1024), id, (part > 0 || kk > 0) ? 1u : 0u);
-      umma_commit(&bar_mma);
-    }
-    ok = __all_sync(0xffffffffu, mbar_wait(&bar_mma, 1, p.status, kDevTimeoutMma));
-    if (ok) {
-      tc_fence_after();
-      uint32_t row[64];
-      tmem_ld64(tmem_addr(tbase, warp * 32, 0), row);
-      w_row(row, tid, rec + kRecW);
-    }
+      for (int kk = 0; kk < 4; ++kk)
+        umma_bf16_ss(tbase, make_sdesc_sw128(kt + kk * 2048, 16384, 1024),
+                     make_sdesc_sw128(tg + part * 8192 + kk * 2048, 16384, 1024), id, (part > 0 || kk > 0) ? 1u : 0u);
+    umma_commit(bar_mma);
   }
+  ok = __all_sync(0xffffffffu, mbar_wait(bar_mma, 1, p.status, kDevTimeoutMma));
+  if (ok) {
+    tc_fence_after();
+    uint32_t row[64];
+    tmem_ld64(tmem_addr(tbase, warp * 32, 0), row);
+    w_row(row, tid, rec + kRecW);
+  }
+  tc_fence_before();
+  return named_sync_and(bar_id, 128, ok);  // every TMEM read and smem use of this record is done
+}
+
+__global__ void __launch_bounds__(kPrepThreads, 3)
+    gdn_prep_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                    const PrepParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_in, bar_mma;
+  __shared__ uint32_t tmem_base_shared;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (tid == 0) {
+    cta_abort_flag() = 0u;
+    mbar_init(&bar_in, 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_k);
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_shared, 64);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base_shared;
+  prep_record(&map_q, &map_k, p, blockIdx.x, blockIdx.y, smem, &bar_in, 0, &bar_mma, tbase, tid, 1);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -241,15 +260,53 @@ struct ChainBarriers {
   uint64_t drain[2];
 };
 
-__global__ void __launch_bounds__(kChainThreads, 1)
-    gdn_chain_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
-                     const ChainParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ ChainBarriers bars;
-  __shared__ uint32_t tmem_base_shared;
+// Barrier initialisation and TMEM allocation of a chain CTA (whole CTA); returns the TMEM base.
+__device__ __forceinline__ uint32_t chain_setup(ChainBarriers& bars, uint32_t* tmem_base_shared) {
+  if (threadIdx.x == 0) {
+    cta_abort_flag() = 0u;
+    uint64_t* all = reinterpret_cast<uint64_t*>(&bars);
+    for (int i = 0; i < static_cast<int>(sizeof(ChainBarriers) / 8); ++i) mbar_init(&all[i], 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&bars.o_read[i], 4);
+    fence_barrier_init();
+  }
+  if (warp_id() == 0) {
+    tmem_alloc(tmem_base_shared, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  return *tmem_base_shared;
+}
+
+// Bounded wait for a record's ready flag (written by a preparation CTA of the same launch with
+// release semantics); afterwards the record may be read through the async proxy.
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t* status) {
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v != 0u) break;
+    if (cta_abort_flag() != 0u) return false;
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      record_status(status, kDevTimeoutPipe);
+      cta_abort_flag() = 1u;
+      return false;
+    }
+    __nanosleep(128);
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
+// The state chain of one (sequence, value head) unit: warps 0-3 chain, 4-7 output, 8 loader
+// (lane 0), with `bars` initialised and 512 TMEM columns at `tbase`.  With `flags` non-null the
+// loader waits (bounded) for flags[record] before it reads a record: the records are then being
+// written by other CTAs of the same cooperative launch.
+__device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUtensorMap* map_v, const ChainParams& p,
+                                           uint8_t* smem, ChainBarriers& bars, uint32_t tbase, int unit,
+                                           const uint32_t* flags) {
   const int warp = warp_id(), lane = lane_id();
-  const int unit = blockIdx.x;
   const int seq = unit / p.hv, h = unit - seq * p.hv;
   const int kh = h % p.hk;
   const int tok0 = p.cu_seqlens[seq];
@@ -261,22 +318,6 @@ __global__ void __launch_bounds__(kChainThreads, 1)
   auto params_of = [&](int c) -> const ChunkParams& {
     return *reinterpret_cast<const ChunkParams*>(stage(c) + kRecParams);
   };
-
-  if (threadIdx.x == 0) {
-    cta_abort_flag() = 0u;
-    uint64_t* all = reinterpret_cast<uint64_t*>(&bars);
-    for (int i = 0; i < static_cast<int>(sizeof(ChainBarriers) / 8); ++i) mbar_init(&all[i], 1);
-    for (int i = 0; i < 2; ++i) mbar_init(&bars.o_read[i], 4);
-    fence_barrier_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(&tmem_base_shared, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = tmem_base_shared;
 
   if (N == 0) {
     if (warp < 4) {
@@ -290,8 +331,8 @@ __global__ void __launch_bounds__(kChainThreads, 1)
   } else if (warp == 8) {
     // ======================================================= loader: record + K + V per chunk
     if (lane == 0) {
-      tma_prefetch_desc(&map_k);
-      tma_prefetch_desc(&map_v);
+      tma_prefetch_desc(map_k);
+      tma_prefetch_desc(map_v);
       int issued = 0;
       for (int c = 0; c < N; ++c) {
         // the stage last held chunk c-2, whose MMAs (and so every read of its record, K and V)
@@ -302,13 +343,15 @@ __global__ void __launch_bounds__(kChainThreads, 1)
         SPLIT_TRACE(9, c);
         uint8_t* st = stage(c);
         uint64_t* bar = &bars.full[c & 1];
-        const uint8_t* rec = p.ws + (static_cast<size_t>(gc0 + c) * p.hv + h) * kRecBytes;
+        const size_t ridx = static_cast<size_t>(gc0 + c) * p.hv + h;
+        const uint8_t* rec = p.ws + ridx * kRecBytes;
+        if (flags != nullptr && !wait_flag(flags + ridx, p.status)) break;
         mbar_arrive_expect_tx(bar, kRecBytes + 32768);
         bulk_g2s(st, rec, kRecP, bar);  // T, W, e^G Q
         bulk_g2s(st + kRecP, rec + kRecP, kRecBytes - kRecP, bar);  // P, params
         for (int bx = 0; bx < 2; ++bx) {
-          tma_load_3d(st + kSK + bx * 8192, &map_k, bar, bx * 64, kh, tok0 + c * kC);
-          tma_load_3d(st + kSV + bx * 8192, &map_v, bar, bx * 64, h, tok0 + c * kC);
+          tma_load_3d(st + kSK + bx * 8192, map_k, bar, bx * 64, kh, tok0 + c * kC);
+          tma_load_3d(st + kSV + bx * 8192, map_v, bar, bx * 64, h, tok0 + c * kC);
         }
         issued = c + 1;
       }
@@ -553,11 +596,113 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     }
   }
 
+}
+
+__global__ void __launch_bounds__(kChainThreads, 1)
+    gdn_chain_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                     const ChainParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ ChainBarriers bars;
+  __shared__ uint32_t tmem_base_shared;
+  const uint32_t tbase = chain_setup(bars, &tmem_base_shared);
+  chain_unit(&map_k, &map_v, p, smem, bars, tbase, blockIdx.x, nullptr);
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp_id() == 0) {
     tc_fence_after();
     tmem_dealloc(tbase, 512);
+  }
+}
+
+// ---- one cooperative launch: chain CTAs and preparation CTAs side by side
+constexpr int kOverlapThreads = 384;
+constexpr int kPSmemA = (kPSmem + 1023) / 1024 * 1024;  // one preparation group's region
+constexpr int kOSmem = kCSmem > 3 * kPSmemA ? kCSmem : 3 * kPSmemA;
+static_assert(kOSmem + 1024 + 512 <= 227 * 1024, "overlap shared memory budget");
+
+struct OverlapParams {
+  const int32_t* record_order;  // [records]: record index (gc * heads_v + h) in chunk-major order
+  uint32_t* flags;              // [records]: zero at launch; 1 once the record has been written
+  int units;                    // CTAs [0, units) run the chain of one unit each
+  int records;
+};
+
+// CTAs [0, units): the chain kernel's work for one unit (warps 0-8), whose loader waits for each
+// record's flag.  The other CTAs: three preparation groups of 128 threads each, every group
+// working through the records in chunk-major order (so the chains' first chunks come first) and
+// publishing each finished record with a release store of its flag.  A cooperative launch keeps
+// every CTA resident, so the chain CTAs' (bounded) waits are on CTAs that are running.
+__global__ void __launch_bounds__(kOverlapThreads, 1)
+    gdn_overlap_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, const PrepParams pp, const ChainParams cp,
+                       const OverlapParams op) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ ChainBarriers bars;
+  __shared__ uint64_t pbar[3][2];
+  __shared__ uint64_t first_done;  // group 0 has published its first record
+  __shared__ uint32_t tmem_base_shared;
+  const int warp = warp_id();
+  if (static_cast<int>(blockIdx.x) < op.units) {
+    const uint32_t tbase = chain_setup(bars, &tmem_base_shared);
+    if (warp < kChainThreads / 32) chain_unit(&map_k, &map_v, cp, smem, bars, tbase, blockIdx.x, op.flags);
+    tc_fence_before();
+    __syncthreads();
+    CTA_END_TRACE();
+    if (warp == 0) {
+      tc_fence_after();
+      tmem_dealloc(tbase, 512);
+    }
+    return;
+  }
+  const int grp = threadIdx.x >> 7, tid = threadIdx.x & 127;
+  if (threadIdx.x == 0) {
+    cta_abort_flag() = 0u;
+    for (int g = 0; g < 3; ++g) {
+      mbar_init(&pbar[g][0], 1);
+      mbar_init(&pbar[g][1], 1);
+    }
+    mbar_init(&first_done, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_k);
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_shared, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base_shared + 64 * grp;
+  // Slot (group, CTA) takes records grp * nprep + cta, + stride, ...: the first records -- the
+  // chains' first chunk -- land one per SM, on groups 0.  Groups 1 and 2 start once their CTA's
+  // group 0 has published its first record, so that those records are not slowed down by them.
+  const int nprep = gridDim.x - op.units;
+  const int stride = nprep * 3;
+  const int first = grp * nprep + (blockIdx.x - op.units);
+  bool ok = true;
+  if (grp > 0) ok = __all_sync(0xffffffffu, mbar_wait(&first_done, 0, pp.status, kDevTimeoutPipe));
+  uint32_t k = 0;
+  for (int r = first; ok && r < op.records; r += stride, ++k) {
+    const int rid = op.record_order[r];
+    const int gc = rid / pp.hv, h = rid - gc * pp.hv;
+    ok = prep_record(&map_q, &map_k, pp, gc, h, smem + grp * kPSmemA, &pbar[grp][0], k & 1, &pbar[grp][1], tbase, tid,
+                     1 + grp);
+    if (ok && tid == 0) {  // every thread's record stores precede prep_record's final group barrier
+      __threadfence();
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(op.flags + rid), "r"(1u) : "memory");
+    }
+    if (grp == 0 && k == 0 && tid == 0) mbar_arrive(&first_done);
+  }
+  if (grp == 0 && tid == 0 && (first >= op.records || !ok)) mbar_arrive(&first_done);  // no first record
+  tc_fence_before();
+  __syncthreads();
+  CTA_END_TRACE();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base_shared, 256);
   }
 }
 
@@ -566,6 +711,11 @@ __global__ void __launch_bounds__(kChainThreads, 1)
 }  // namespace tokmix
 
 #ifdef TOKMIX_GDN_TRACE
+extern "C" int tokmix_gdn_split_cta_end_read(unsigned long long* host, int n) {
+  using namespace tokmix::gdn::split;
+  const int count = n < 1024 ? n : 1024;
+  return cudaMemcpyFromSymbol(host, g_cta_end, sizeof(unsigned long long) * count) == cudaSuccess ? count : -1;
+}
 extern "C" int tokmix_gdn_split_trace_read(unsigned long long* host, int n) {
   using namespace tokmix::gdn::split;
   const int count = n < kTrEvents * kTrChunks ? n : kTrEvents * kTrChunks;
@@ -573,15 +723,18 @@ extern "C" int tokmix_gdn_split_trace_read(unsigned long long* host, int n) {
 }
 #endif
 
+// records of kRecBytes, then one uint32 ready flag per record (used by the overlapped launch)
 extern "C" long long tokmix_gdn_split_workspace_bytes(int total_chunks, int heads_v) {
   if (total_chunks < 0 || heads_v < 0) return -1;
-  return static_cast<long long>(total_chunks) * heads_v * tokmix::gdn::split::kRecBytes;
+  const long long records = static_cast<long long>(total_chunks) * heads_v;
+  return records * tokmix::gdn::split::kRecBytes + ((records * 4 + 255) / 256) * 256;
 }
 
 extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void* v, const float* g,
                                         const float* beta, const float* initial_state, void* out, float* final_state,
-                                        const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev, int num_seqs,
-                                        int total_tokens, int total_chunks, int heads_k, int heads_v, int head_dim_k,
+                                        const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev,
+                                        const int32_t* record_order_dev, int num_seqs, int total_tokens,
+                                        int total_chunks, int heads_k, int heads_v, int head_dim_k,
                                         int head_dim_v, float scale, int io_dtype, void* workspace,
                                         long long workspace_bytes, uint32_t* status, void* stream) {
   using namespace tokmix;
@@ -631,25 +784,17 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
       return TOKMIX_ERR_INVALID_ARGUMENT;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (total_chunks > 0) {
-    PrepParams pp{};
-    pp.g = g;
-    pp.beta = beta;
-    pp.cu_seqlens = cu_seqlens_dev;
-    pp.chunk_base = chunk_base_dev;
-    pp.ws = static_cast<uint8_t*>(workspace);
-    pp.num_seqs = num_seqs;
-    pp.hk = heads_k;
-    pp.hv = heads_v;
-    pp.scale = scale;
-    pp.status = status;
-    const int smem = kPSmem + 1024;
-    if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_prep_kernel), smem))
-      return check_launch("tokmix_gdn_prefill_split: cudaFuncSetAttribute (prep)");
-    gdn_prep_kernel<<<dim3(static_cast<unsigned>(total_chunks), static_cast<unsigned>(heads_v)), kPrepThreads, smem, s>>>(
-        mq, mk, pp);
-    if (const int rc = check_launch("tokmix_gdn_prefill_split (prep)")) return rc;
-  }
+  PrepParams pp{};
+  pp.g = g;
+  pp.beta = beta;
+  pp.cu_seqlens = cu_seqlens_dev;
+  pp.chunk_base = chunk_base_dev;
+  pp.ws = static_cast<uint8_t*>(workspace);
+  pp.num_seqs = num_seqs;
+  pp.hk = heads_k;
+  pp.hv = heads_v;
+  pp.scale = scale;
+  pp.status = status;
   ChainParams cp{};
   cp.state_in = initial_state;
   cp.state_out = final_state;
@@ -660,6 +805,48 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   cp.hk = heads_k;
   cp.hv = heads_v;
   cp.status = status;
+  const long long records = static_cast<long long>(total_chunks) * heads_v;
+  // --- one cooperative launch when the chains leave SMs free for the preparation CTAs
+  if (record_order_dev != nullptr && records > 0) {
+    const int sms = device_sm_count();
+    const int smem = kOSmem + 1024;
+    int per_sm = 0;
+    if (units + 8 <= sms && ensure_smem_attr(reinterpret_cast<const void*>(&gdn_overlap_kernel), smem) &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gdn_overlap_kernel, kOverlapThreads, smem) ==
+            cudaSuccess &&
+        per_sm >= 1) {
+      OverlapParams op{};
+      op.record_order = record_order_dev;
+      op.flags = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + records * kRecBytes);
+      op.units = static_cast<int>(units);
+      op.records = static_cast<int>(records);
+      if (cudaMemsetAsync(op.flags, 0, static_cast<size_t>(records) * 4, s) != cudaSuccess)
+        return check_launch("tokmix_gdn_prefill_split: clearing the record flags");
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(static_cast<unsigned>(sms));
+      cfg.blockDim = dim3(kOverlapThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeCooperative;
+      attr[0].val.cooperative = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaLaunchKernelEx(&cfg, gdn_overlap_kernel, mq, mk, mv, pp, cp, op) == cudaSuccess)
+        return check_launch("tokmix_gdn_prefill_split (overlapped)");
+      cudaGetLastError();  // not launchable cooperatively here: two launches instead
+    } else {
+      cudaGetLastError();
+    }
+  }
+  if (total_chunks > 0) {
+    const int smem = kPSmem + 1024;
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_prep_kernel), smem))
+      return check_launch("tokmix_gdn_prefill_split: cudaFuncSetAttribute (prep)");
+    gdn_prep_kernel<<<dim3(static_cast<unsigned>(total_chunks), static_cast<unsigned>(heads_v)), kPrepThreads, smem, s>>>(
+        mq, mk, pp);
+    if (const int rc = check_launch("tokmix_gdn_prefill_split (prep)")) return rc;
+  }
   const int smem = kCSmem + 1024;
   if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_chain_kernel), smem))
     return check_launch("tokmix_gdn_prefill_split: cudaFuncSetAttribute (chain)");

@@ -19,8 +19,11 @@ Extensions over the reference module:
 * ``cu_seqlens`` (keyword): variable-length sequences packed along T with q.shape[0] == 1 and
   one initial state per sequence (state [N,Hv,128,128]); ``state=None`` means zero states.
 * any Hk dividing Hv (the reference fixes Hk=16, Hv=32).
-* ``mode`` (keyword): "auto" (default), "fused" or "split" selects the schedule; the environment
-  variable TOKMIX_GDN_MODE overrides "auto".
+* ``mode`` (keyword): "auto" (default), "fused", "split" (preparation launch, then state-chain
+  launch) or "overlap" (both stages in one cooperative launch, chain CTAs consuming each chunk as
+  preparation CTAs on the other SMs finish it; measured no faster than "split" on a B200 at the
+  B=1 T=2048 shape, so "auto" does not pick it) selects the schedule; the environment variable
+  TOKMIX_GDN_MODE overrides "auto".
 """
 
 from __future__ import annotations
@@ -55,7 +58,7 @@ def _device_meta(lengths: tuple[int, ...], device: torch.device):
         cu_t = torch.tensor(cu, dtype=torch.int32).to(device)
         order_t = torch.tensor(order, dtype=torch.int32).to(device) if len(set(lengths)) > 1 else None
         cb_t = torch.tensor(cb, dtype=torch.int32).to(device)
-        hit = (cu_t, order_t, cb_t, cb[-1])
+        hit = (cu_t, order_t, cb_t, cb[-1], cb)
         if len(_meta_cache) > 256:
             _meta_cache.clear()
         _meta_cache[key] = hit
@@ -133,7 +136,7 @@ def kernel_fn(
         out = torch.empty(v.shape, dtype=io_dtype, device=dev)
         fs = state.to(torch.float32).clone() if state is not None else torch.zeros((nseq, hv, D, D), device=dev)
         return [out, fs]
-    cu_t, order_t, cb_t, total_chunks = _device_meta(lengths, dev)
+    cu_t, order_t, cb_t, total_chunks, cb_host = _device_meta(lengths, dev)
     qb = q.to(torch.bfloat16).contiguous()
     kb = k.to(torch.bfloat16).contiguous()
     vb = v.to(torch.bfloat16).contiguous()
@@ -149,11 +152,13 @@ def kernel_fn(
         if use_split:
             nbytes = int(lib.tokmix_gdn_split_workspace_bytes(total_chunks, hv))
             ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+            rec_t = _record_order(lengths, cb_host, hv, dev) if _mode(mode) == "overlap" else None
             rc = lib.tokmix_gdn_prefill_split(
                 qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
                 st.data_ptr() if st is not None else None, out.data_ptr(), final_state.data_ptr(),
-                cu_t.data_ptr(), cb_t.data_ptr(), nseq, total, total_chunks, hk, hv, D, D, float(scale),
-                _lib.DTYPE_BF16, ws.data_ptr(), ws.numel(), word.data_ptr(), _lib.stream_ptr(dev))
+                cu_t.data_ptr(), cb_t.data_ptr(), rec_t.data_ptr() if rec_t is not None else None, nseq, total,
+                total_chunks, hk, hv, D, D, float(scale), _lib.DTYPE_BF16, ws.data_ptr(), ws.numel(),
+                word.data_ptr(), _lib.stream_ptr(dev))
         else:
             rc = lib.tokmix_gdn_prefill(
                 qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
@@ -168,18 +173,45 @@ def kernel_fn(
     return [out, final_state]
 
 
-def _use_split(mode: str, units: int, total_chunks: int, hv: int, dev: torch.device) -> bool:
-    """Split schedule when the one-CTA-per-unit schedule would leave SMs idle."""
+def _record_order(lengths: tuple[int, ...], chunk_base: list[int], hv: int, device: torch.device) -> torch.Tensor:
+    """Records (global chunk * hv + value head) in chunk-major order: the order in which the
+    overlapped split launch prepares them, so that every chain's next chunk is ready first."""
+    key = ("order", lengths, hv, device)
+    hit = _meta_cache.get(key)
+    if hit is None:
+        nch = [(n + 63) // 64 for n in lengths]
+        rec = [(chunk_base[s] + c) * hv + h for c in range(max(nch, default=0))
+               for s in range(len(lengths)) if c < nch[s] for h in range(hv)]
+        hit = torch.tensor(rec if rec else [0], dtype=torch.int32).to(device)
+        _meta_cache[key] = hit
+    return hit
+
+
+def _mode(mode: str) -> str:
     if mode == "auto":
         mode = os.environ.get("TOKMIX_GDN_MODE", "auto")
+    if mode not in ("auto", "fused", "split", "overlap"):
+        raise ValueError(f"mode must be 'auto', 'fused', 'split' or 'overlap' (got {mode!r})")
+    return mode
+
+
+def _use_split(mode: str, units: int, total_chunks: int, hv: int, dev: torch.device) -> bool:
+    """Split schedule when the one-CTA-per-unit schedule would leave SMs idle."""
+    mode = _mode(mode)
     if mode == "fused":
         return False
-    if mode == "split":
+    if mode in ("split", "overlap"):
         return True
-    if mode != "auto":
-        raise ValueError(f"mode must be 'auto', 'fused' or 'split' (got {mode!r})")
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     return units < sms and _lib.load().tokmix_gdn_split_workspace_bytes(total_chunks, hv) <= _SPLIT_MAX_WORKSPACE
+
+
+def schedule(q: torch.Tensor, v: torch.Tensor, cu_seqlens=None, mode: str = "auto") -> str:
+    """The schedule kernel_fn picks for these inputs: "fused" (one launch) or "split" (two)."""
+    B, T, hv = q.shape[0], q.shape[1], v.shape[2]
+    lengths = (T,) * B if cu_seqlens is None else _lengths(cu_seqlens, T)
+    chunks = sum((n + 63) // 64 for n in lengths)
+    return "split" if _use_split(mode, len(lengths) * hv, chunks, hv, q.device) else "fused"
 
 
 def check_device_status(device: torch.device | None = None) -> None:
