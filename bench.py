@@ -45,8 +45,15 @@ L2_BYTES = 126 * 1024 * 1024
 D = 128
 HK, HV = 16, 32
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of each workload's
-# kernel from one ncu capture; see profiles/*.md for the commands and the raw figures.
-NCU_TRAFFIC_BYTES = {}
+# kernel(s) from one ncu capture, keyed "workload/schedule"; profiles/*.md give the commands and
+# the raw figures.  ncu replays each kernel with flushed caches, so for the split GDN schedule the
+# chain kernel's reads of the records (which stay in L2 in a real run) count as DRAM reads.
+# FA2: captured at batch 1 (the batch-4 inputs exceed the capture size rule) and scaled by 4.
+NCU_TRAFFIC_BYTES = {
+    "gdn_b1_t2048/split": 17_700_864 + 23_319_552 + 104_131_072 + 7_580_416,  # prep + chain
+    "gdn_b1_t2048/fused": 36_302_848 + 54_016,
+    "fa2_b4_s8192/fused": 4 * (101_431_808 + 32_353_792),
+}
 
 
 def measured_peaks() -> dict:
@@ -407,7 +414,7 @@ def main():
             ach = r["local_flops"] / (kms / 1e3) / 1e12
             return {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                     "frac": ach / peaks["bf16_tflops"], "peak_source": peaks["source"] + " burst bf16",
-                    "traffic": NCU_TRAFFIC_BYTES.get(w), "kernel": "tokmix::fa2::fa2_fwd_kernel<128>",
+                    "traffic": NCU_TRAFFIC_BYTES.get(w + "/fused"), "kernel": "tokmix::fa2::fa2_fwd_kernel<128>",
                     "kernel_ms": kms}
         ach = r["algo_bytes"] / (kms / 1e3) / 1e9
         if r.get("schedule") == "split":  # one step = the preparation launch + the state-chain launch
@@ -416,7 +423,7 @@ def main():
             kern = "tokmix::gdn::gdn_prefill_kernel"
         return {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": ach / peaks["hbm_gbs"], "peak_source": peaks["source"] + " copy bandwidth",
-                "traffic": NCU_TRAFFIC_BYTES.get(w), "algorithmic_bytes": r["algo_bytes"],
+                "traffic": NCU_TRAFFIC_BYTES.get(f"{w}/{r.get('schedule', 'fused')}"), "algorithmic_bytes": r["algo_bytes"],
                 "kernel": kern, "kernel_ms": kms, "schedule": r.get("schedule", "fused")}
 
     if rank == 0:

@@ -41,15 +41,13 @@ constexpr int kPSmem = kPParams + kParamsBytes;
 static_assert(kPL % 1024 == 0 && 3 * (kPSmem + 1024 + 64) <= 228 * 1024, "prep layout: three CTAs per SM");
 
 // ---- chain kernel
-constexpr int kChainThreads = 288;            // warps 0-3 chain, 4-7 output, 8 loader
+constexpr int kChainThreads = 320;            // warps 0-7 passes, 8 loader, 9 MMA issuer
 constexpr int kSK = 75776;                    // K: two boxes of 64 rows x 128 B (after the record)
 constexpr int kSV = kSK + 16384;              // V: two boxes of 64 rows x 128 B
 constexpr int kStageBytes = kSV + 16384;
 constexpr int kCSmem = 2 * kStageBytes;
 static_assert(kRecBytes <= kSK && kSK % 1024 == 0 && kStageBytes % 1024 == 0, "chain layout");
 static_assert(kCSmem + 1024 + 256 <= 227 * 1024, "chain shared memory budget");
-
-constexpr uint32_t kColS = 0, kColShi = 128, kColSlo = 192, kColX = 256, kColO = 384;
 
 // Optional phase trace of the chain kernel (build with -DTOKMIX_GDN_TRACE): SM clock stamps of
 // CTA 0 by event and chunk, read back with tokmix_gdn_split_trace_read().
@@ -64,6 +62,20 @@ __device__ unsigned long long g_cta_end[1024];  // %globaltimer at the end of ea
 #else
 #define SPLIT_TRACE(ev, c) \
   do {                     \
+  } while (0)
+#endif
+#ifdef TOKMIX_GDN_TRACE
+// prep phases of CTAs (x < 8, y = 0) of the two-launch schedule, by thread 0 (SM clock)
+constexpr int kPrepTrCtas = 8, kPrepTrEvents = 16;
+__device__ unsigned long long g_prep_trace[kPrepTrCtas * kPrepTrEvents];
+#define PREP_TRACE(ev)                                                                         \
+  do {                                                                                         \
+    if (gridDim.y > 1 && blockIdx.y == 0 && blockIdx.x < kPrepTrCtas && tid == 0)              \
+      g_prep_trace[blockIdx.x * kPrepTrEvents + (ev)] = clock64();                             \
+  } while (0)
+#else
+#define PREP_TRACE(ev) \
+  do {                 \
   } while (0)
 #endif
 #ifdef TOKMIX_GDN_TRACE
@@ -116,6 +128,7 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
                                             int gc, int h, uint8_t* smem, uint64_t* bar_in, uint32_t in_parity,
                                             uint64_t* bar_mma, uint32_t tbase, int tid, int bar_id) {
   const int warp = tid >> 5, lane = tid & 31;
+  PREP_TRACE(0);
   int lo = 0, hi = p.num_seqs;  // sequence of global chunk gc: chunk_base[lo] <= gc < chunk_base[lo + 1]
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
@@ -148,6 +161,7 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
     chunk_decay_params(pc, ga, gb, ba, bb, n_valid, lane);
   }
   named_sync(bar_id, 128);
+  PREP_TRACE(1);
   if (tid < kParamsBytes / 16)
     reinterpret_cast<uint4*>(rec + kRecParams)[tid] = reinterpret_cast<const uint4*>(smem + kPParams)[tid];
   // --- T1: [K;Q] K^T
@@ -159,9 +173,11 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
     for (int kk = 0; kk < 8; ++kk)
       umma_bf16_ss(tbase, kmaj_desc(slot, kk, 16384), kmaj_desc(slot, kk, 16384), id, kk > 0 ? 1u : 0u);
     umma_commit(bar_mma);
+    PREP_TRACE(2);
   }
   // --- read-out: rows 0-63 (K K^T) -> L, rows 64-127 (Q K^T) -> P and e^G-scaled Q
   bool ok = __all_sync(0xffffffffu, mbar_wait(bar_mma, 0, p.status, kDevTimeoutMma));
+  PREP_TRACE(3);
   if (ok) {
     tc_fence_after();
     uint32_t row[64];
@@ -177,10 +193,13 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
   tc_fence_before();
   ok = named_sync_and(bar_id, 128, ok);
   if (!ok) return false;
+  PREP_TRACE(4);
   solve_inverse(Ls, Xs, tid, bar_id);
+  PREP_TRACE(5);
   write_t_tiles(Xs, pc, tid, rec + kRecT, smem + kPL);  // T to the record, T diag(e^G) over the dead L
   fence_async_smem();
   named_sync(bar_id, 128);
+  PREP_TRACE(6);
   // --- T2: W^T = K^T (TG_hi + TG_lo)^T
   if (tid == 0) {
     tc_fence_after();
@@ -193,8 +212,10 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
         umma_bf16_ss(tbase, make_sdesc_sw128(kt + kk * 2048, 16384, 1024),
                      make_sdesc_sw128(tg + part * 8192 + kk * 2048, 16384, 1024), id, (part > 0 || kk > 0) ? 1u : 0u);
     umma_commit(bar_mma);
+    PREP_TRACE(7);
   }
   ok = __all_sync(0xffffffffu, mbar_wait(bar_mma, 1, p.status, kDevTimeoutMma));
+  PREP_TRACE(8);
   if (ok) {
     tc_fence_after();
     uint32_t row[64];
@@ -202,7 +223,9 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
     w_row(row, tid, rec + kRecW);
   }
   tc_fence_before();
-  return named_sync_and(bar_id, 128, ok);  // every TMEM read and smem use of this record is done
+  ok = named_sync_and(bar_id, 128, ok);  // every TMEM read and smem use of this record is done
+  PREP_TRACE(9);
+  return ok;
 }
 
 __global__ void __launch_bounds__(kPrepThreads, 3)
@@ -246,19 +269,36 @@ __device__ __forceinline__ bool wait2_warp(uint64_t* bars, int c, uint32_t* stat
   return __all_sync(0xffffffffu, wait2(bars, c, status, code));
 }
 
-// MMA issuers: the chain thread (t0, thread 0) issues the state terms and T4; the output
-// issuer (oi, lane 0 of warp 4) issues T V, T3b and T5, so that they run while the chain works
-// on the CUDA cores (T3b during the Delta pass, T V(c+1) during the state pass).
+// Warp roles of a chain CTA.  Warps 0-7 are the pass warps: warp w and warp w + 4 share TMEM lane
+// quadrant w (value rows 32(w & 3) .. +31) and take one half each of every pass's columns.  Warp 8
+// (lane 0) loads, warp 9 (lane 0) issues every MMA: an issuing thread stalls for about as long as
+// its MMAs take, so no pass warp issues.  The pass warps and the issuer warp meet twice per chunk
+// on named barrier 1 (Delta pass done, state pass done).
+constexpr int kPassThreads = 256;
+constexpr int kSyncThreads = kPassThreads + 32;
+
+// Every waiter of event c on a two-slot barrier waits before event c + 2 can complete (each
+// producer of c + 2 causally follows each waiter of c), so a parity never goes two phases ahead.
 struct ChainBarriers {
-  uint64_t full[2];     // stage of chunk c loaded.           waiters: oi (T V), chain (gamma), loader drain
-  uint64_t tv_done[2];  // T V(c) complete.                   waiter: t0
-  uint64_t x_ready[2];  // state terms(c) complete.           waiters: chain, oi
-  uint64_t dp_done[2];  // Delta operands of chunk c in TMEM. waiter: oi
-  uint64_t s_new[2];    // T4(c) complete.                    waiters: chain, oi, loader
-  uint64_t o_done[2];   // T3b(c), T5(c) complete.            waiters: output warps, chain, oi, loader
-  uint64_t o_read[2];   // O(c) read out (one arrival per output warp).  waiter: oi
-  uint64_t drain[2];
+  uint64_t full[2];      // stage of chunk c loaded.                         waiters: issuer, pass warps, loader drain
+  uint64_t tv_done[2];   // T V(c) complete.                                 waiter: issuer
+  uint64_t x_ready[2];   // state terms(c) complete.                         waiters: pass warps
+  uint64_t t3b_done[2];  // T3b(c) complete: S_hi, S_lo no longer read.      waiters: pass warps
+  uint64_t s_new[2];     // T4(c) complete.                                  waiters: pass warps, loader
+  uint64_t o_done[2];    // T5(c) (and so T3b(c)) complete.                  waiters: pass warps, loader
+  uint64_t o_read[2];    // O(c) read out (one arrival per pass warp).       waiter: issuer
+  uint64_t drain;
 };
+
+// TMEM columns of a chain CTA: the fp32 state S (the accumulator T4 adds to), its bf16 hi/lo
+// copies (A operands of the state terms and T3b), X (T V, then the state terms: two 64-column
+// partial sums of Delta), O (T3b + T5), and the bf16 Delta operands written by the Delta pass.
+// The plain Delta (T5's A operand) lives in the first 32 S_lo columns: S_lo is dead from the end of
+// the state terms (x_ready) until the state pass rewrites it after T5 has completed (o_done), and
+// X is then free for T V(c+1) as soon as the Delta pass has read it.
+constexpr uint32_t kColS = 0, kColShi = 128, kColSlo = 192, kColX = 256, kColO = 384;
+constexpr uint32_t kColDhi = 448, kColDlo = 480;  // e^(G_C - G) Delta hi | lo (T4's A operand)
+constexpr uint32_t kColDp = kColSlo;              // plain bf16 Delta, tokens 2j, 2j+1 in column j
 
 // Barrier initialisation and TMEM allocation of a chain CTA (whole CTA); returns the TMEM base.
 __device__ __forceinline__ uint32_t chain_setup(ChainBarriers& bars, uint32_t* tmem_base_shared) {
@@ -266,7 +306,7 @@ __device__ __forceinline__ uint32_t chain_setup(ChainBarriers& bars, uint32_t* t
     cta_abort_flag() = 0u;
     uint64_t* all = reinterpret_cast<uint64_t*>(&bars);
     for (int i = 0; i < static_cast<int>(sizeof(ChainBarriers) / 8); ++i) mbar_init(&all[i], 1);
-    for (int i = 0; i < 2; ++i) mbar_init(&bars.o_read[i], 4);
+    for (int i = 0; i < 2; ++i) mbar_init(&bars.o_read[i], kPassThreads / 32);
     fence_barrier_init();
   }
   if (warp_id() == 0) {
@@ -299,10 +339,17 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t* status
   return true;
 }
 
-// The state chain of one (sequence, value head) unit: warps 0-3 chain, 4-7 output, 8 loader
-// (lane 0), with `bars` initialised and 512 TMEM columns at `tbase`.  With `flags` non-null the
-// loader waits (bounded) for flags[record] before it reads a record: the records are then being
-// written by other CTAs of the same cooperative launch.
+// The state chain of one (sequence, value head) unit on warps 0-9 (roles above), with `bars`
+// initialised and 512 TMEM columns at `tbase`.  With `flags` non-null the loader waits (bounded)
+// for flags[record] before it reads a record: the records are then being written by other CTAs
+// of the same cooperative launch.
+//
+// Per chunk c (the critical path is marked *):
+//   issuer  * state terms(c) once T V(c) is done; T3b(c) once O(c-1) is read out
+//   pass    gamma pass: S(c) -> gamma_c S(c) and read-out of O(c-1), beside the state terms
+//   pass    * Delta pass once x_ready(c)                                  -> barrier
+//   issuer  * T4(c) -> s_new;  T5(c) -> o_done;  T V(c+1) (X is dead once the Delta pass read it)
+//   pass    * state pass: S_hi of S(c+1) once s_new(c), t3b_done(c); S_lo once o_done(c) -> barrier
 __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUtensorMap* map_v, const ChainParams& p,
                                            uint8_t* smem, ChainBarriers& bars, uint32_t tbase, int unit,
                                            const uint32_t* flags) {
@@ -336,7 +383,7 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
       int issued = 0;
       for (int c = 0; c < N; ++c) {
         // the stage last held chunk c-2, whose MMAs (and so every read of its record, K and V)
-        // have completed, and whose decay factor was read by the state pass of chunk c-3
+        // have completed, and whose parameters the pass warps read before T4(c-2) was issued
         if (c >= 2 && !(wait2(bars.o_done, c - 2, p.status, kDevTimeoutPipe) &&
                         wait2(bars.s_new, c - 2, p.status, kDevTimeoutPipe)))
           break;
@@ -357,44 +404,37 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
       }
       for (int c = max(0, issued - 2); c < issued; ++c) mbar_drain(&bars.full[c & 1], (c >> 1) & 1);
     }
-  } else if (warp < 4) {
-    // ======================================================= state chain (lane = value row)
-    const int v = threadIdx.x;
-    const uint32_t lb = tmem_addr(tbase, warp * 32, 0);
-    bool ok = wait2_warp(bars.full, 0, p.status, kDevTimeoutTma);
-    if (ok) {
-      const float gam = params_of(0).gamma_c;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sv[64];
+  } else if (warp == 9) {
+    // ======================================================= MMA issuer (lane 0)
+    const bool l0 = (lane == 0);
+    // T V(c) = V^T [T_hi | T_lo]^T into the X region (accumulate 0)
+    auto issue_tv = [&](int c) {
+      const uint32_t st = smem_u32(stage(c));
+      const uint32_t id_v = make_idesc(128, 128, 1, 1, 1);
 #pragma unroll
-        for (int j = 0; j < 64; j += 4) {
-          float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (p.state_in) val = *reinterpret_cast<const float4*>(p.state_in + state_off + v * kD + half * 64 + j);
-          sv[j] = __float_as_uint(val.x);
-          sv[j + 1] = __float_as_uint(val.y);
-          sv[j + 2] = __float_as_uint(val.z);
-          sv[j + 3] = __float_as_uint(val.w);
-        }
-        store_split32<0>(lb + kColShi + 32 * half, lb + kColSlo + 32 * half, sv);
-        store_split32<32>(lb + kColShi + 32 * half + 16, lb + kColSlo + 32 * half + 16, sv);
-#pragma unroll
-        for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
-        tmem_st32(lb + kColS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_st32(lb + kColS + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      for (int kk = 0; kk < 4; ++kk)
+        umma_bf16_ss(tbase + kColX, make_sdesc_sw128(st + kSV + kk * 2048, 8192, 1024),
+                     make_sdesc_sw128(st + kRecT + kk * 2048, 8192, 1024), id_v, kk > 0 ? 1u : 0u);
+      umma_commit(&bars.tv_done[c & 1]);
+      SPLIT_TRACE(12, c);
+    };
+    bool ok = true;
+    if (l0) {
+      ok = wait2(bars.full, 0, p.status, kDevTimeoutTma);
+      if (ok) {
+        tc_fence_after();
+        issue_tv(0);
       }
-      tmem_wait_st();
     }
-    tc_fence_before();
-    ok = named_sync_and(1, 128, ok);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    ok = named_sync_and(1, kSyncThreads, ok);  // initial state and its hi/lo copies are in TMEM
     for (int c = 0; ok && c < N; ++c) {
       const uint32_t st = smem_u32(stage(c));
-      // --- (thread 0) the state terms once T V(c) is in the X region (every exit from this loop
-      //     goes through a named_sync_and, so the four warps leave together)
-      if (v == 0) {
-        const bool r = wait2(bars.tv_done, c, p.status, kDevTimeoutMma);
+      if (l0) {
+        // state terms(c): X += S_hi [-W_hi | -W_lo]^T (N = 128) + S_lo (-W_hi)^T (N = 64)
+        ok = wait2(bars.tv_done, c, p.status, kDevTimeoutMma);
         SPLIT_TRACE(0, c);
-        if (r) {
+        if (ok) {
           tc_fence_after();
           const uint32_t id128 = make_idesc(128, 128, 1, 0, 1), id64 = make_idesc(128, 64, 1, 0, 1);
 #pragma unroll
@@ -407,195 +447,209 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
                          id64, 1u);
           umma_commit(&bars.x_ready[c & 1]);
           SPLIT_TRACE(1, c);
+          // T3b(c): O^T = S_hi (e^G Q)^T into the O region, once O(c-1) has been read out
+          ok = (c == 0) || wait2(bars.o_read, c - 1, p.status, kDevTimeoutPipe);
         }
-      }
-      // --- Delta pass
-      const bool xr = wait2_warp(bars.x_ready, c, p.status, kDevTimeoutMma);
-      tc_fence_after();
-      if (v == 0) SPLIT_TRACE(2, c);
-      if (xr) {
-        const ChunkParams& pc = params_of(c);
-        uint32_t d[64];
-        tmem_ld64(lb + kColX, d);
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t e[32];
-          tmem_ld32(lb + kColX + 64 + 32 * hf, e);
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            d[32 * hf + j] = __float_as_uint(__uint_as_float(d[32 * hf + j]) + __uint_as_float(e[j]));
-        }
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int j = 0; j < 16; j += 2) {
-            const int t = 32 * hf + 2 * j;
-            const float4 e4 = *reinterpret_cast<const float4*>(&pc.egr[t]);
-            split_pack(__uint_as_float(d[t]) * e4.x, __uint_as_float(d[t + 1]) * e4.y, hi[j], lo[j]);
-            split_pack(__uint_as_float(d[t + 2]) * e4.z, __uint_as_float(d[t + 3]) * e4.w, hi[j + 1], lo[j + 1]);
-          }
-          tmem_st16(lb + kColX + 16 * hf, hi);
-          tmem_st16(lb + kColX + 32 + 16 * hf, lo);
-        }
-        {
-          uint32_t pk[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) pk[j] = pack_bf16x2(__uint_as_float(d[2 * j]), __uint_as_float(d[2 * j + 1]));
-          tmem_st32(lb + kColX + 64, pk);
-        }
-        tmem_wait_st();
-      }
-      tc_fence_before();
-      if (!named_sync_and(1, 128, xr)) { ok = false; break; }
-      if (v == 0) {
-        SPLIT_TRACE(3, c);
-        mbar_arrive(&bars.dp_done[c & 1]);  // T5(c) may read Delta (and T3b has S_hi(c) to itself)
-        tc_fence_after();
-        const uint32_t id_upd = make_idesc(128, 128, 1, 0, 1);
-#pragma unroll
-        for (int part = 0; part < 2; ++part)
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16_ts(tbase + kColS, tbase + kColX + 32 * part + 8 * kk,
-                         make_sdesc_sw128(st + kSK + kk * 2048, 8192, 1024), id_upd, 1u);
-        umma_commit(&bars.s_new[c & 1]);
-        SPLIT_TRACE(4, c);
-      }
-      // --- state pass (the hi/lo copies are overwritten only after T3b(c) completed: o_done)
-      const bool last = (c == N - 1);
-      bool sr = wait2_warp(bars.s_new, c, p.status, kDevTimeoutMma);
-      tc_fence_after();
-      if (v == 0) SPLIT_TRACE(6, c);
-      float gam = 1.0f;
-      if (sr && !last) {
-        sr = wait2_warp(bars.full, c + 1, p.status, kDevTimeoutTma) &&
-             wait2_warp(bars.o_done, c, p.status, kDevTimeoutMma);
-        gam = params_of(c + 1).gamma_c;
-      }
-      if (v == 0) SPLIT_TRACE(7, c);
-#pragma unroll 1
-      for (int qt = 0; sr && qt < 4; ++qt) {
-        uint32_t sv[32];
-        tmem_ld32(lb + kColS + qt * 32, sv);
-        if (last) {
-          float* dst = p.state_out + state_off + v * kD + qt * 32;
-#pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
-                                                              __uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3]));
-        } else {
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) split_pack(__uint_as_float(sv[2 * j]), __uint_as_float(sv[2 * j + 1]), hi[j], lo[j]);
-          tmem_st16(lb + kColShi + 16 * qt, hi);
-          tmem_st16(lb + kColSlo + 16 * qt, lo);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
-          tmem_st32(lb + kColS + qt * 32, sv);
-        }
-      }
-      if (!last) {
-        tmem_wait_st();
-        tc_fence_before();
-        if (!named_sync_and(1, 128, sr)) { ok = false; break; }
-        if (v == 0) SPLIT_TRACE(8, c);
-      }
-    }
-    if (v == 0) {
-      umma_commit(&bars.drain[0]);
-      mbar_drain(&bars.drain[0], 0);
-    }
-  } else {
-    // ======================================================= output pass (warps 4-7)
-    const int r = threadIdx.x - 128;
-    const uint32_t lb = tmem_addr(tbase, (warp & 3) * 32, 0);
-    const bool oi = (warp == 4 && lane == 0);
-    bool ok = true;
-    // T V(c) = V^T [T_hi | T_lo]^T into the X region (accumulate 0)
-    auto issue_tv = [&](int c) {
-      const uint32_t st = smem_u32(stage(c));
-      const uint32_t id_v = make_idesc(128, 128, 1, 1, 1);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        umma_bf16_ss(tbase + kColX, make_sdesc_sw128(st + kSV + kk * 2048, 8192, 1024),
-                     make_sdesc_sw128(st + kRecT + kk * 2048, 8192, 1024), id_v, kk > 0 ? 1u : 0u);
-      umma_commit(&bars.tv_done[c & 1]);
-    };
-    if (oi) {
-      ok = wait2(bars.full, 0, p.status, kDevTimeoutTma);
-      if (ok) {
-        tc_fence_after();
-        issue_tv(0);
-      }
-    }
-    for (int co = 0; co < N; ++co) {
-      if (oi && ok) {
-        // T3b(co) once the state terms have read S_hi(co)'s chunk (x_ready) and O(co-1) is read
-        const uint32_t st = smem_u32(stage(co));
-        ok = wait2(bars.x_ready, co, p.status, kDevTimeoutMma) &&
-             (co == 0 || wait2(bars.o_read, co - 1, p.status, kDevTimeoutPipe));
         if (ok) {
           tc_fence_after();
           const uint32_t id = make_idesc(128, 64, 1, 0, 0);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             umma_bf16_ts(tbase + kColO, tbase + kColShi + 8 * kk, kmaj_desc(st + kRecQ, kk, 8192), id, kk > 0 ? 1u : 0u);
-          SPLIT_TRACE(11, co);
-          ok = wait2(bars.dp_done, co, p.status, kDevTimeoutPipe);
+          umma_commit(&bars.t3b_done[c & 1]);
+          SPLIT_TRACE(11, c);
         }
-        if (ok) {
-          // T5(co): O^T += Delta^T P^T
-          tc_fence_after();
-          const uint32_t id = make_idesc(128, 64, 1, 0, 0);
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      tc_fence_before();
+      if (!named_sync_and(1, kSyncThreads, ok)) {  // Delta pass(c) done
+        ok = false;
+        break;
+      }
+      if (l0) {
+        tc_fence_after();
+        // T4(c): S^T += [Delta'_hi | Delta'_lo] [K; K] (gamma_c S(c) is in the S region)
+        const uint32_t id_upd = make_idesc(128, 128, 1, 0, 1);
+#pragma unroll
+        for (int part = 0; part < 2; ++part)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16_ts(tbase + kColO, tbase + kColX + 64 + 8 * kk, make_sdesc_sw128(st + kRecP + kk * 32, 16, 1024),
-                         id, 1u);
-          umma_commit(&bars.o_done[co & 1]);
-          SPLIT_TRACE(5, co);
-          // T V(co+1) once T4(co) and T5(co) have read the X region and the next stage is loaded
-          if (co + 1 < N) {
-            ok = wait2(bars.o_done, co, p.status, kDevTimeoutMma) && wait2(bars.s_new, co, p.status, kDevTimeoutMma) &&
-                 wait2(bars.full, co + 1, p.status, kDevTimeoutTma);
-            if (ok) {
-              tc_fence_after();
-              issue_tv(co + 1);
-              SPLIT_TRACE(12, co + 1);
-            }
+            umma_bf16_ts(tbase + kColS, tbase + kColDhi + 32 * part + 8 * kk,
+                         make_sdesc_sw128(st + kSK + kk * 2048, 8192, 1024), id_upd, 1u);
+        umma_commit(&bars.s_new[c & 1]);
+        SPLIT_TRACE(4, c);
+        // T5(c): O^T += Delta^T P^T (after T3b(c) and T4(c) in this thread's issue order)
+        const uint32_t id = make_idesc(128, 64, 1, 0, 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16_ts(tbase + kColO, tbase + kColDp + 8 * kk, make_sdesc_sw128(st + kRecP + kk * 32, 16, 1024), id,
+                       1u);
+        umma_commit(&bars.o_done[c & 1]);
+        SPLIT_TRACE(5, c);
+        // T V(c+1): X was last read by the Delta pass (before the barrier above)
+        if (c + 1 < N) {
+          ok = wait2(bars.full, c + 1, p.status, kDevTimeoutTma);
+          if (ok) {
+            tc_fence_after();
+            issue_tv(c + 1);
           }
         }
       }
-      __syncwarp();
-      if (!wait2_warp(bars.o_done, co, p.status, kDevTimeoutMma)) break;
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      tc_fence_before();
+      if (!named_sync_and(1, kSyncThreads, ok)) {  // state pass(c) done
+        ok = false;
+        break;
+      }
+    }
+    if (l0) {
+      umma_commit(&bars.drain);
+      mbar_drain(&bars.drain, 0);
+    }
+  } else {
+    // ======================================================= pass warps 0-7 (lane = value row)
+    const int q4 = warp & 3, hh = warp >> 2;
+    const int v = q4 * 32 + lane;
+    const uint32_t lb = tmem_addr(tbase, q4 * 32, 0);
+    bool ok = wait2_warp(bars.full, 0, p.status, kDevTimeoutTma);
+    if (ok) {  // initial state, key columns [64 hh, 64 hh + 64): hi/lo copies and gamma_0 S(0)
+      const float gam = params_of(0).gamma_c;
+      uint32_t sv[64];
+#pragma unroll
+      for (int j = 0; j < 64; j += 4) {
+        float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (p.state_in) val = *reinterpret_cast<const float4*>(p.state_in + state_off + v * kD + 64 * hh + j);
+        sv[j] = __float_as_uint(val.x);
+        sv[j + 1] = __float_as_uint(val.y);
+        sv[j + 2] = __float_as_uint(val.z);
+        sv[j + 3] = __float_as_uint(val.w);
+      }
+      store_split32<0>(lb + kColShi + 32 * hh, lb + kColSlo + 32 * hh, sv);
+      store_split32<32>(lb + kColShi + 32 * hh + 16, lb + kColSlo + 32 * hh + 16, sv);
+#pragma unroll
+      for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
+      tmem_st32(lb + kColS + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+      tmem_st32(lb + kColS + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      tmem_wait_st();
+    }
+    tc_fence_before();
+    ok = named_sync_and(1, kSyncThreads, ok);
+
+    // O(co) read-out, tokens [32 hh, 32 hh + 32) of the chunk: token pair (2i, 2i+1): the even
+    // lane of a lane pair stores (O[2i][v], O[2i][v+1]), the odd lane (O[2i+1][v-1], O[2i+1][v]),
+    // one 4-byte store each
+    auto read_out = [&](int co) -> bool {
+      if (!wait2_warp(bars.o_done, co, p.status, kDevTimeoutMma)) return false;
       tc_fence_after();
-      if (r == 0) SPLIT_TRACE(10, co);
-      uint32_t o[64];
-      tmem_ld64(lb + kColO, o);
+      if (threadIdx.x == 0) SPLIT_TRACE(10, co);
+      uint32_t o[32];
+      tmem_ld32(lb + kColO + 32 * hh, o);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.o_read[co & 1]);
-      // token pair (2i, 2i+1): the even lane of a lane pair stores (O[2i][v], O[2i][v+1]), the
-      // odd lane (O[2i+1][v-1], O[2i+1][v]), one 4-byte store each
-      const int nv = min(kC, len - co * kC);
+      const int nv = min(kC, len - co * kC) - 32 * hh;
       const bool odd = (lane & 1) != 0;
       const size_t tstride = static_cast<size_t>(p.hv) * kD;
-      uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (static_cast<size_t>(tok0 + co * kC) * p.hv + h) * kD +
-                                                  (r & ~1)) + (odd ? tstride / 2 : 0);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (static_cast<size_t>(tok0 + co * kC + 32 * hh) * p.hv + h) * kD +
+                                                  (v & ~1)) + (odd ? tstride / 2 : 0);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         const float a = __uint_as_float(o[2 * i]), b = __uint_as_float(o[2 * i + 1]);
         const float other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
         const uint32_t packed = odd ? pack_bf16x2(other, b) : pack_bf16x2(a, other);
         if (2 * i + (odd ? 1 : 0) < nv) dst[i * tstride] = packed;
       }
-    }
-    if (oi) {
-      umma_commit(&bars.drain[1]);
-      mbar_drain(&bars.drain[1], 0);
-    }
-  }
+      return true;
+    };
 
+    for (int c = 0; ok && c < N; ++c) {
+      if (c > 0) {
+        // gamma pass: S(c) -> gamma_c S(c), the accumulator T4(c) adds to; then O(c-1).  Both run
+        // beside the state-term MMAs, which read only S_hi, S_lo and write only X.
+        ok = wait2_warp(bars.full, c, p.status, kDevTimeoutTma);
+        if (threadIdx.x == 0) SPLIT_TRACE(7, c);
+        if (ok) {
+          const float gam = params_of(c).gamma_c;
+          uint32_t sv[64];
+          tmem_ld64(lb + kColS + 64 * hh, sv);
+#pragma unroll
+          for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
+          tmem_st32(lb + kColS + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_st32(lb + kColS + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tmem_wait_st();
+          ok = read_out(c - 1);
+        }
+      }
+      // --- Delta pass, tokens [32 hh, 32 hh + 32): Delta = X[t] + X[64 + t]; e^(G_C - G_t) Delta
+      //     as hi/lo into the Delta columns, plain bf16 Delta into S_lo (read last by the state
+      //     terms, complete at x_ready)
+      const bool xr = ok && wait2_warp(bars.x_ready, c, p.status, kDevTimeoutMma);
+      tc_fence_after();
+      if (threadIdx.x == 0) SPLIT_TRACE(2, c);
+      if (xr) {
+        const ChunkParams& pc = params_of(c);
+        uint32_t d[64];  // d[0..31] first partial sums, d[32..63] second
+        tmem_ld32x2(lb + kColX + 32 * hh, lb + kColX + 64 + 32 * hh, d);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) d[j] = __float_as_uint(__uint_as_float(d[j]) + __uint_as_float(d[32 + j]));
+        uint32_t hi[16], lo[16], pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+          const int t = 2 * j;
+          const float4 e4 = *reinterpret_cast<const float4*>(&pc.egr[32 * hh + t]);
+          split_pack(__uint_as_float(d[t]) * e4.x, __uint_as_float(d[t + 1]) * e4.y, hi[j], lo[j]);
+          split_pack(__uint_as_float(d[t + 2]) * e4.z, __uint_as_float(d[t + 3]) * e4.w, hi[j + 1], lo[j + 1]);
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(d[2 * j]), __uint_as_float(d[2 * j + 1]));
+        tmem_st16(lb + kColDhi + 16 * hh, hi);
+        tmem_st16(lb + kColDlo + 16 * hh, lo);
+        tmem_st16(lb + kColDp + 16 * hh, pk);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      if (!named_sync_and(1, kSyncThreads, xr)) {
+        ok = false;
+        break;
+      }
+      if (threadIdx.x == 0) SPLIT_TRACE(3, c);
+      // --- state pass, key columns [64 hh, 64 hh + 64): hi/lo copies of S(c+1) -- hi after T3b(c)
+      //     has read the old one, lo after T5(c) has read the plain Delta there -- or the final
+      //     state after the last chunk
+      const bool last = (c == N - 1);
+      bool sr = wait2_warp(bars.s_new, c, p.status, kDevTimeoutMma) &&
+                wait2_warp(bars.t3b_done, c, p.status, kDevTimeoutMma);
+      tc_fence_after();
+      if (threadIdx.x == 0) SPLIT_TRACE(6, c);
+      if (sr) {
+        uint32_t sv[64];
+        tmem_ld64(lb + kColS + 64 * hh, sv);
+        if (last) {
+          float* dst = p.state_out + state_off + v * kD + 64 * hh;
+#pragma unroll
+          for (int j = 0; j < 64; j += 4)
+            *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
+                                                              __uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3]));
+        } else {
+          uint32_t hi[32], lo[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) split_pack(__uint_as_float(sv[2 * j]), __uint_as_float(sv[2 * j + 1]), hi[j], lo[j]);
+          tmem_st32(lb + kColShi + 32 * hh, hi);
+          sr = wait2_warp(bars.o_done, c, p.status, kDevTimeoutMma);
+          tc_fence_after();
+          if (sr) tmem_st32(lb + kColSlo + 32 * hh, lo);
+          tmem_wait_st();
+        }
+      }
+      tc_fence_before();
+      if (!named_sync_and(1, kSyncThreads, sr)) {
+        ok = false;
+        break;
+      }
+      if (threadIdx.x == 0) SPLIT_TRACE(8, c);
+    }
+    if (ok) read_out(N - 1);
+  }
 }
 
 __global__ void __launch_bounds__(kChainThreads, 1)
@@ -715,6 +769,11 @@ extern "C" int tokmix_gdn_split_cta_end_read(unsigned long long* host, int n) {
   using namespace tokmix::gdn::split;
   const int count = n < 1024 ? n : 1024;
   return cudaMemcpyFromSymbol(host, g_cta_end, sizeof(unsigned long long) * count) == cudaSuccess ? count : -1;
+}
+extern "C" int tokmix_gdn_prep_trace_read(unsigned long long* host, int n) {
+  using namespace tokmix::gdn::split;
+  const int count = n < kPrepTrCtas * kPrepTrEvents ? n : kPrepTrCtas * kPrepTrEvents;
+  return cudaMemcpyFromSymbol(host, g_prep_trace, sizeof(unsigned long long) * count) == cudaSuccess ? count : -1;
 }
 extern "C" int tokmix_gdn_split_trace_read(unsigned long long* host, int n) {
   using namespace tokmix::gdn::split;

@@ -332,8 +332,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
-// two back-to-back 32-column loads (columns [c, c+32) and [c+32, c+64)) with a single wait
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+// two back-to-back 32-column loads (r[0..31] from column a, r[32..63] from column b) with a single wait
+__device__ __forceinline__ void tmem_ld32x2(uint32_t a, uint32_t b, uint32_t (&r)[64]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
       "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
@@ -342,9 +342,12 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
       "tcgen05.wait::ld.sync.aligned;\n"
       : TOKMIX_R8(0), TOKMIX_R8(8), TOKMIX_R8(16), TOKMIX_R8(24), TOKMIX_R8(32), TOKMIX_R8(40), TOKMIX_R8(48),
         TOKMIX_R8(56)
-      : "r"(taddr), "r"(taddr + 32u)
+      : "r"(a), "r"(b)
       : "memory");
 }
+
+// columns [c, c+64) with a single wait
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) { tmem_ld32x2(taddr, taddr + 32u, r); }
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
