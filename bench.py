@@ -419,6 +419,8 @@ def main():
         ach = r["algo_bytes"] / (kms / 1e3) / 1e9
         if r.get("schedule") == "split":  # one step = the preparation launch + the state-chain launch
             kern = "tokmix::gdn::split::gdn_prep_kernel + tokmix::gdn::split::gdn_chain_kernel (one step)"
+        elif r.get("schedule") == "overlap":  # one cooperative launch (after a memset of the record flags)
+            kern = "tokmix::gdn::split::gdn_overlap_kernel"
         else:
             kern = "tokmix::gdn::gdn_prefill_kernel"
         return {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",

@@ -48,10 +48,16 @@ __device__ __forceinline__ void store_row_sw128(uint8_t* tile, int row, const ui
 
 // x = hi + lo as two bf16 operands: hi = x truncated to bf16 (its top 16 bits, exact), lo =
 // the exact fp32 remainder rounded to bf16.  |x - hi - lo| <= 2^-16 |x|.
+__device__ __forceinline__ uint32_t hi_pack(float x0, float x1) {
+  return __byte_perm(__float_as_uint(x0), __float_as_uint(x1), 0x7632);
+}
+__device__ __forceinline__ uint32_t lo_pack(float x0, float x1) {
+  return pack_bf16x2(x0 - __uint_as_float(__float_as_uint(x0) & 0xFFFF0000u),
+                     x1 - __uint_as_float(__float_as_uint(x1) & 0xFFFF0000u));
+}
 __device__ __forceinline__ void split_pack(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-  const uint32_t b0 = __float_as_uint(x0), b1 = __float_as_uint(x1);
-  hi = __byte_perm(b0, b1, 0x7632);
-  lo = pack_bf16x2(x0 - __uint_as_float(b0 & 0xFFFF0000u), x1 - __uint_as_float(b1 & 0xFFFF0000u));
+  hi = hi_pack(x0, x1);
+  lo = lo_pack(x0, x1);
 }
 
 // 32 fp32 values x[OFF, OFF+32) (raw bits) -> hi and lo bf16 copies, 16 TMEM columns each
@@ -300,10 +306,10 @@ __device__ __forceinline__ void solve_inverse(const float* Ls, float* Xs, int ti
 }
 
 // T = X diag(beta) and TG = T diag(e^G) as MN-major ([s][t]) hi/lo bf16 tiles (hi at tile, lo at
-// tile + 8192; shared or global memory), 128 threads: thread = (row s, token half).  Entries
+// tile + lo_off; shared or global memory), 128 threads: thread = (row s, token half).  Entries
 // above the diagonal are 0.
 __device__ __forceinline__ void write_t_tiles(const float* Xs, const ChunkParams& pc, int tid, uint8_t* t_tile,
-                                              uint8_t* tg_tile) {
+                                              uint8_t* tg_tile, int t_lo_off = 8192, int tg_lo_off = 8192) {
   const int s = tid & 63, half = tid >> 6;
   float xv[32];
 #pragma unroll
@@ -321,7 +327,7 @@ __device__ __forceinline__ void write_t_tiles(const float* Xs, const ChunkParams
     for (int i = 0; i < 16; ++i) split_pack(xv[2 * i] * w, xv[2 * i + 1] * w, hi[i], lo[i]);
     uint8_t* tile = qq ? tg_tile : t_tile;
     store_half_row_sw128(tile, s, half, hi);
-    store_half_row_sw128(tile + 8192, s, half, lo);
+    store_half_row_sw128(tile + (qq ? tg_lo_off : t_lo_off), s, half, lo);
   }
 }
 

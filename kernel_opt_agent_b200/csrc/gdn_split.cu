@@ -54,7 +54,8 @@ static_assert(kCSmem + 1024 + 256 <= 227 * 1024, "chain shared memory budget");
 #ifdef TOKMIX_GDN_TRACE
 constexpr int kTrChunks = 64, kTrEvents = 16;
 __device__ unsigned long long g_split_trace[kTrEvents * kTrChunks];
-__device__ unsigned long long g_cta_end[1024];  // %globaltimer at the end of each CTA
+__device__ unsigned long long g_cta_end[1024];    // %globaltimer at the end of each CTA
+__device__ unsigned long long g_cta_start[1024];  // %globaltimer at the start of each CTA
 #define SPLIT_TRACE(ev, c)                                                                               \
   do {                                                                                                   \
     if (blockIdx.x == 0 && (c) < kTrChunks) g_split_trace[(ev) * kTrChunks + (c)] = clock64();          \
@@ -83,9 +84,16 @@ __device__ unsigned long long g_prep_trace[kPrepTrCtas * kPrepTrEvents];
   do {                                                                                   \
     if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_end[blockIdx.x] = global_timer_ns(); \
   } while (0)
+#define CTA_START_TRACE()                                                                  \
+  do {                                                                                     \
+    if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_start[blockIdx.x] = global_timer_ns(); \
+  } while (0)
 #else
 #define CTA_END_TRACE() \
   do {                  \
+  } while (0)
+#define CTA_START_TRACE() \
+  do {                    \
   } while (0)
 #endif
 
@@ -695,9 +703,9 @@ __global__ void __launch_bounds__(kOverlapThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ ChainBarriers bars;
   __shared__ uint64_t pbar[3][2];
-  __shared__ uint64_t first_done;  // group 0 has published its first record
   __shared__ uint32_t tmem_base_shared;
   const int warp = warp_id();
+  CTA_START_TRACE();
   if (static_cast<int>(blockIdx.x) < op.units) {
     const uint32_t tbase = chain_setup(bars, &tmem_base_shared);
     if (warp < kChainThreads / 32) chain_unit(&map_k, &map_v, cp, smem, bars, tbase, blockIdx.x, op.flags);
@@ -717,7 +725,6 @@ __global__ void __launch_bounds__(kOverlapThreads, 1)
       mbar_init(&pbar[g][0], 1);
       mbar_init(&pbar[g][1], 1);
     }
-    mbar_init(&first_done, 1);
     fence_barrier_init();
     tma_prefetch_desc(&map_q);
     tma_prefetch_desc(&map_k);
@@ -731,13 +738,11 @@ __global__ void __launch_bounds__(kOverlapThreads, 1)
   tc_fence_after();
   const uint32_t tbase = tmem_base_shared + 64 * grp;
   // Slot (group, CTA) takes records grp * nprep + cta, + stride, ...: the first records -- the
-  // chains' first chunk -- land one per SM, on groups 0.  Groups 1 and 2 start once their CTA's
-  // group 0 has published its first record, so that those records are not slowed down by them.
+  // chains' first chunk -- land one per SM, on groups 0; all groups start at once.
   const int nprep = gridDim.x - op.units;
   const int stride = nprep * 3;
   const int first = grp * nprep + (blockIdx.x - op.units);
   bool ok = true;
-  if (grp > 0) ok = __all_sync(0xffffffffu, mbar_wait(&first_done, 0, pp.status, kDevTimeoutPipe));
   uint32_t k = 0;
   for (int r = first; ok && r < op.records; r += stride, ++k) {
     const int rid = op.record_order[r];
@@ -748,9 +753,7 @@ __global__ void __launch_bounds__(kOverlapThreads, 1)
       __threadfence();
       asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(op.flags + rid), "r"(1u) : "memory");
     }
-    if (grp == 0 && k == 0 && tid == 0) mbar_arrive(&first_done);
   }
-  if (grp == 0 && tid == 0 && (first >= op.records || !ok)) mbar_arrive(&first_done);  // no first record
   tc_fence_before();
   __syncthreads();
   CTA_END_TRACE();
@@ -769,6 +772,11 @@ extern "C" int tokmix_gdn_split_cta_end_read(unsigned long long* host, int n) {
   using namespace tokmix::gdn::split;
   const int count = n < 1024 ? n : 1024;
   return cudaMemcpyFromSymbol(host, g_cta_end, sizeof(unsigned long long) * count) == cudaSuccess ? count : -1;
+}
+extern "C" int tokmix_gdn_split_cta_start_read(unsigned long long* host, int n) {
+  using namespace tokmix::gdn::split;
+  const int count = n < 1024 ? n : 1024;
+  return cudaMemcpyFromSymbol(host, g_cta_start, sizeof(unsigned long long) * count) == cudaSuccess ? count : -1;
 }
 extern "C" int tokmix_gdn_prep_trace_read(unsigned long long* host, int n) {
   using namespace tokmix::gdn::split;

@@ -4,11 +4,14 @@
     KERNEL_TYPE, kernel_fn(q, k, v, g, beta, state, scale=None) -> [out, final_state],
     get_inputs, get_flops, get_bytes
 
-``kernel_fn`` runs the sm_100a chunked kernels in libtokmix.so; there is no fallback.  Two
+``kernel_fn`` runs the sm_100a chunked kernels in libtokmix.so; there is no fallback.  Three
 schedules compute the same result: one CTA per (sequence, value head) doing everything
-(``tokmix_gdn_prefill``), or, when there are fewer such units than SMs, a chunk-parallel
-preparation launch followed by a state-chain launch (``tokmix_gdn_prefill_split``, which needs a
-workspace of about 73 KB per (chunk, value head), taken from PyTorch's caching allocator).  Argument meaning follows the reference (``kernels/qwen35moe_gdn_prefill.py:107-151``):
+(``tokmix_gdn_prefill``, "fused"), or, when there are fewer such units than SMs, chunk-parallel
+preparation of per-chunk operand records followed by one state chain per unit
+(``tokmix_gdn_prefill_split``, which needs a workspace of about 73 KB per (chunk, value head),
+taken from PyTorch's caching allocator): as two launches ("split"), or as one cooperative launch
+whose chain CTAs consume each chunk as the preparation CTAs on the other SMs finish it
+("overlap").  Argument meaning follows the reference (``kernels/qwen35moe_gdn_prefill.py:107-151``):
 q, k [B,T,Hk,128]; v [B,T,Hv,128]; g (log decay), beta [B,T,Hv]; state [B,Hv,128(v),128(k)];
 value head h reads key head h % Hk; default scale 128**-0.5; returns [out like v, final_state fp32].
 
@@ -19,11 +22,11 @@ Extensions over the reference module:
 * ``cu_seqlens`` (keyword): variable-length sequences packed along T with q.shape[0] == 1 and
   one initial state per sequence (state [N,Hv,128,128]); ``state=None`` means zero states.
 * any Hk dividing Hv (the reference fixes Hk=16, Hv=32).
-* ``mode`` (keyword): "auto" (default), "fused", "split" (preparation launch, then state-chain
-  launch) or "overlap" (both stages in one cooperative launch, chain CTAs consuming each chunk as
-  preparation CTAs on the other SMs finish it; measured no faster than "split" on a B200 at the
-  B=1 T=2048 shape, so "auto" does not pick it) selects the schedule; the environment variable
-  TOKMIX_GDN_MODE overrides "auto".
+* ``mode`` (keyword): "auto" (default), "fused", "split" or "overlap" selects the schedule; the
+  environment variable TOKMIX_GDN_MODE overrides "auto".  "auto" picks "fused" when the units
+  fill the SMs, else "overlap" when at least 8 SMs are left for the preparation CTAs, else
+  "split" (and the library itself falls back from "overlap" to two launches when the device
+  cannot hold the cooperative grid).
 """
 
 from __future__ import annotations
@@ -147,12 +150,12 @@ def kernel_fn(
     final_state = torch.empty((nseq, hv, D, D), dtype=torch.float32, device=dev)
     lib = _lib.load()
     word = _lib.status_word(dev)
-    use_split = _use_split(mode, nseq * hv, total_chunks, hv, dev)
+    sched = _schedule(mode, nseq * hv, total_chunks, hv, dev)
     with torch.cuda.device(dev):
-        if use_split:
+        if sched != "fused":
             nbytes = int(lib.tokmix_gdn_split_workspace_bytes(total_chunks, hv))
             ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
-            rec_t = _record_order(lengths, cb_host, hv, dev) if _mode(mode) == "overlap" else None
+            rec_t = _record_order(lengths, cb_host, hv, dev) if sched == "overlap" else None
             rc = lib.tokmix_gdn_prefill_split(
                 qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
                 st.data_ptr() if st is not None else None, out.data_ptr(), final_state.data_ptr(),
@@ -195,23 +198,24 @@ def _mode(mode: str) -> str:
     return mode
 
 
-def _use_split(mode: str, units: int, total_chunks: int, hv: int, dev: torch.device) -> bool:
-    """Split schedule when the one-CTA-per-unit schedule would leave SMs idle."""
+def _schedule(mode: str, units: int, total_chunks: int, hv: int, dev: torch.device) -> str:
+    """"fused" when one CTA per unit fills the SMs (or the workspace would be too large), else
+    "overlap" when the chains leave at least 8 SMs to the preparation CTAs, else "split"."""
     mode = _mode(mode)
-    if mode == "fused":
-        return False
-    if mode in ("split", "overlap"):
-        return True
+    if mode != "auto":
+        return mode
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    return units < sms and _lib.load().tokmix_gdn_split_workspace_bytes(total_chunks, hv) <= _SPLIT_MAX_WORKSPACE
+    if units >= sms or _lib.load().tokmix_gdn_split_workspace_bytes(total_chunks, hv) > _SPLIT_MAX_WORKSPACE:
+        return "fused"
+    return "overlap" if units + 8 <= sms else "split"
 
 
 def schedule(q: torch.Tensor, v: torch.Tensor, cu_seqlens=None, mode: str = "auto") -> str:
-    """The schedule kernel_fn picks for these inputs: "fused" (one launch) or "split" (two)."""
+    """The schedule kernel_fn picks for these inputs: "fused", "split" or "overlap"."""
     B, T, hv = q.shape[0], q.shape[1], v.shape[2]
     lengths = (T,) * B if cu_seqlens is None else _lengths(cu_seqlens, T)
     chunks = sum((n + 63) // 64 for n in lengths)
-    return "split" if _use_split(mode, len(lengths) * hv, chunks, hv, q.device) else "fused"
+    return _schedule(mode, len(lengths) * hv, chunks, hv, q.device)
 
 
 def check_device_status(device: torch.device | None = None) -> None:
