@@ -50,7 +50,7 @@ HK, HV = 16, 32
 # chain kernel's reads of the records (which stay in L2 in a real run) count as DRAM reads.
 # FA2: captured at batch 1 (the batch-4 inputs exceed the capture size rule) and scaled by 4.
 NCU_TRAFFIC_BYTES = {
-    "gdn_b1_t2048/split": 17_700_864 + 23_319_552 + 104_131_072 + 7_580_416,  # prep + chain
+    "gdn_b1_t2048/split": 17_699_072 + 23_969_536 + 104_127_488 + 7_339_264,  # prep + chain
     "gdn_b1_t2048/fused": 36_302_848 + 54_016,
     "fa2_b4_s8192/fused": 4 * (101_431_808 + 32_353_792),
 }
