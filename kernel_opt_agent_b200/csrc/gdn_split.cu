@@ -519,9 +519,9 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
     const int q4 = warp & 3, hh = warp >> 2;
     const int v = q4 * 32 + lane;
     const uint32_t lb = tmem_addr(tbase, q4 * 32, 0);
-    bool ok = wait2_warp(bars.full, 0, p.status, kDevTimeoutTma);
-    if (ok) {  // initial state, key columns [64 hh, 64 hh + 64): hi/lo copies and gamma_0 S(0)
-      const float gam = params_of(0).gamma_c;
+    bool ok = true;
+    {  // initial state S(0), key columns [64 hh, 64 hh + 64), and its hi/lo copies; gamma_0 is
+       // applied by the gamma pass of chunk 0, so this does not wait for the first record
       uint32_t sv[64];
 #pragma unroll
       for (int j = 0; j < 64; j += 4) {
@@ -534,8 +534,6 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
       }
       store_split32<0>(lb + kColShi + 32 * hh, lb + kColSlo + 32 * hh, sv);
       store_split32<32>(lb + kColShi + 32 * hh + 16, lb + kColSlo + 32 * hh + 16, sv);
-#pragma unroll
-      for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
       tmem_st32(lb + kColS + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
       tmem_st32(lb + kColS + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
       tmem_wait_st();
@@ -571,7 +569,7 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
     };
 
     for (int c = 0; ok && c < N; ++c) {
-      if (c > 0) {
+      {
         // gamma pass: S(c) -> gamma_c S(c), the accumulator T4(c) adds to; then O(c-1).  Both run
         // beside the state-term MMAs, which read only S_hi, S_lo and write only X.
         ok = wait2_warp(bars.full, c, p.status, kDevTimeoutTma);
@@ -585,7 +583,7 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
           tmem_st32(lb + kColS + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
           tmem_st32(lb + kColS + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
           tmem_wait_st();
-          ok = read_out(c - 1);
+          if (c > 0) ok = read_out(c - 1);
         }
       }
       // --- Delta pass, tokens [32 hh, 32 hh + 32): Delta = X[t] + X[64 + t]; e^(G_C - G_t) Delta
