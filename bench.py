@@ -38,6 +38,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from kernel_opt_agent_b200 import flash_attention_2 as fa2  # noqa: E402
+from kernel_opt_agent_b200 import qwen35moe_gdn_decode as gdn_dec  # noqa: E402
 from kernel_opt_agent_b200 import qwen35moe_gdn_prefill as gdn  # noqa: E402
 from kernel_opt_agent_b200 import sharding  # noqa: E402
 
@@ -53,6 +54,7 @@ NCU_TRAFFIC_BYTES = {
     "gdn_b1_t2048/split": 17_699_072 + 23_969_536 + 104_127_488 + 7_339_264,  # prep + chain
     "gdn_b1_t2048/fused": 36_302_848 + 54_016,
     "fa2_b4_s8192/fused": 4 * (101_431_808 + 32_353_792),
+    "gdn_decode_b128/decode": 270_583_808 + 210_555_648,
 }
 
 
@@ -249,6 +251,22 @@ def run_gdn_varlen(device, rank, world, steps, warmup, verify=False):
     return res
 
 
+def run_gdn_decode(device, rank, world, steps, warmup, batch=128):
+    """One decode token for each of `batch` sequences (split over the ranks), Hk16 Hv32, states
+    N(0, 0.02) updated in place every step as in a decode loop.  The 268 MB of fp32 state is
+    larger than L2, so no flush is needed between steps."""
+    local = batch // world
+    inp = gdn_dec.get_inputs(batch=local, seed=5000 + rank, device=str(device))
+    total_s, per = time_steps(lambda: gdn_dec.kernel_fn(**inp, inplace=True), steps, warmup, device,
+                              flush=input_bytes(inp) < L2_BYTES)
+    algo = gdn_dec.algorithmic_bytes(local)
+    return {"tokens_per_step": batch, "ms": total_s / steps * 1e3, "value": batch * steps / total_s / 1e6,
+            "unit": "Mtok/s", "kernel_ms_local": statistics.mean(per), "algo_bytes": algo, "schedule": "decode",
+            "config": {"workload": "gdn_decode_b128", "batch": batch, "tokens_per_sequence": 1, "hk": HK, "hv": HV,
+                       "head_dim": D, "state": "N(0,0.02) fp32, updated in place",
+                       "l2": "state (268 MB) larger than L2", "shard": f"sequences {local}/rank"}}
+
+
 def run_fa2(device, rank, world, steps, warmup, batch=4, verify=False):
     B, HQ, HKV, S, DD = batch, 32, 8, 8192, 128
     ranges = sharding.even_ranges(HKV, world)
@@ -317,6 +335,25 @@ def cpu_gdn_b1(repeats: int = 3):
     return 2048 / med / 1e6, cores, med
 
 
+def cpu_gdn_decode(batch: int = 128, repeats: int = 5):
+    """The oracle on the host cores over the full decode workload (one token for each of `batch`
+    sequences, Hk=16 Hv=32, N(0, 0.02) states); returns (Mtok/s median, cores, seconds)."""
+    sys.path.insert(0, ROOT)
+    import oracle  # the CPU restatement; only this leg of the benchmark uses it
+
+    cores = os.cpu_count() or 1
+    inp = gdn_dec.get_inputs(batch=batch, seed=5000, device="cpu")
+    args = [inp[k].float().numpy() for k in ("q", "k", "v", "g", "beta")]
+    st = inp["state"].numpy()
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        oracle.gdn_recurrent(*args, st, inp["scale"], nthreads=cores)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return batch / med / 1e6, cores, med
+
+
 def run_reference(args):
     """`--impl reference`: the reference has no CPU implementation of this path (its oracle is a
     CUDA kernel), so the reference arm is the oracle port timed on the host cores."""
@@ -351,7 +388,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="gdn_b1_t2048",
-                    choices=["gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_b4_t2048", "fa2_b1_s8192"],
+                    choices=["gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_decode_b128", "gdn_b4_t2048",
+                             "fa2_b1_s8192"],
                     help="gdn_b4_t2048 / fa2_b1_s8192 are profiling-size cases (inputs just above L2)")
     ap.add_argument("--no-also", action="store_true", help="skip the secondary workloads")
     ap.add_argument("--no-verify", action="store_true",
@@ -379,7 +417,7 @@ def main():
     sampler = ClockSampler(list(range(world))) if rank == 0 else None
     results = {}
     head = args.workload
-    order = [head] + ([w for w in ("gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen") if w != head]
+    order = [head] + ([w for w in ("gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_decode_b128") if w != head]
                       if not args.no_also else [])
     e2e = None
     for w in order:
@@ -395,6 +433,8 @@ def main():
         elif w in ("fa2_b4_s8192", "fa2_b1_s8192"):
             r = run_fa2(device, rank, world, steps_w, args.warmup, batch=4 if w == "fa2_b4_s8192" else 1,
                         verify=not args.no_verify)
+        elif w == "gdn_decode_b128":
+            r = run_gdn_decode(device, rank, world, steps_w, args.warmup)
         else:
             r = run_gdn_varlen(device, rank, world, steps_w, args.warmup, verify=not args.no_verify)
         results[w] = r
@@ -402,7 +442,12 @@ def main():
     clocks = sampler.stop() if sampler else None
 
     cpu = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and head == "gdn_decode_b128":
+        v, cores, sec = cpu_gdn_decode()
+        cpu = {"value": v, "unit": "Mtok/s", "cores": cores, "kind": "port",
+               "sample": f"full decode step, 128 sequences Hk=16 Hv=32, median of 5 runs ({sec:.4f} s each), fp32 "
+                         "recurrence (oracle/gdn_recurrent.c, OpenMP)"}
+    elif rank == 0 and world == 1:
         v, cores, sec = cpu_gdn_b1()
         cpu = {"value": v, "unit": "Mtok/s", "cores": cores, "kind": "port",
                "sample": f"full B=1 T=2048 Hk=16 Hv=32 workload, median of 3 runs ({sec:.3f} s each), fp32 "
@@ -421,6 +466,8 @@ def main():
             kern = "tokmix::gdn::split::gdn_prep_kernel + tokmix::gdn::split::gdn_chain_kernel (one step)"
         elif r.get("schedule") == "overlap":  # one cooperative launch (after a memset of the record flags)
             kern = "tokmix::gdn::split::gdn_overlap_kernel"
+        elif r.get("schedule") == "decode":
+            kern = "tokmix::gdn_decode::gdn_decode_kernel"
         else:
             kern = "tokmix::gdn::gdn_prefill_kernel"
         return {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -430,7 +477,8 @@ def main():
 
     if rank == 0:
         hr = results[head]
-        metric = HEADLINE_METRIC if head.startswith("gdn") else "FA2 fwd TFLOPS"
+        metric = ("FA2 fwd TFLOPS" if head.startswith("fa2") else
+                  "GDN decode Mtok/s" if head == "gdn_decode_b128" else HEADLINE_METRIC)
         cfg = hr["config"]
         line = {"metric": metric, "value": hr["value"], "unit": hr["unit"], "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": hr["ms"], "higher_is_better": True,

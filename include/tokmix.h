@@ -1,7 +1,7 @@
 /* tokmix.h -- C ABI of libtokmix.so, the sm_100a (B200) prefill token-mixer kernels.
  *
  * Two entry points replace the two kernel extensions the reference's plugin modules bind (the
- * GDN one has two further variants below):
+ * GDN one has two further variants below, and a single-token decode step follows them):
  *
  *   tokmix_fa2_fwd      replaces  flash_attention_2_forward(q, k, v, sm_scale, causal)
  *                       kernels_optimized/flash_attention_2.cu:1121-1258, bound at
@@ -131,6 +131,22 @@ int tokmix_gdn_prefill_split(const void* q, const void* k, const void* v, const 
 
 /* Workspace size of tokmix_gdn_prefill_split in bytes (-1 for negative arguments). */
 long long tokmix_gdn_split_workspace_bytes(int total_chunks, int heads_v);
+
+/* One decode step of the gated delta rule: one new token per sequence, bf16 in and out, fp32 state.
+ *
+ *   for every sequence b, value head h (key head h % heads_k) and value row c:
+ *   gamma = exp(g);  kv = S[c] . k;  delta = (v[c] - gamma kv) beta
+ *   S[c] = gamma S[c] + delta k;  out[c] = scale (S[c] . q)            (with the updated S)
+ *
+ * q, k: [batch, heads_k, 128]; v, out: [batch, heads_v, 128]; g, beta: [batch, heads_v] fp32;
+ * state_in (NULL = zero state) and state_out: [batch, heads_v, 128 (v), 128 (k)] fp32 -- the
+ * reference's [v_col, k_row] layout; state_out may equal state_in (update in place).  All
+ * tensors contiguous and 16-byte aligned.  Same maths as one token of tokmix_gdn_prefill.
+ * Replaces the single-token step the reference takes inside its prefill
+ * (kernels_optimized/qwen35moe_gdn_prefill.cu:865-934; maths kernels/qwen35moe_gdn_prefill.cu:55-99). */
+int tokmix_gdn_decode(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                      const float* state_in, float* state_out, void* out, int batch, int heads_k, int heads_v,
+                      int head_dim_k, int head_dim_v, float scale, int io_dtype, void* stream);
 
 /* Text of the last error reported on the calling thread ("" if none). */
 const char* tokmix_last_error(void);

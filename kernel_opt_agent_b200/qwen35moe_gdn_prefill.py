@@ -26,7 +26,9 @@ Extensions over the reference module:
   environment variable TOKMIX_GDN_MODE overrides "auto".  "auto" picks "fused" when the units
   fill the SMs, else "overlap" when at least 8 SMs are left for the preparation CTAs, else
   "split" (and the library itself falls back from "overlap" to two launches when the device
-  cannot hold the cooperative grid).
+  cannot hold the cooperative grid).  A batched call with one token per sequence (T = 1, the
+  decode step of a serving loop) runs ``qwen35moe_gdn_decode``'s one-pass kernel instead under
+  "auto" ("decode").
 """
 
 from __future__ import annotations
@@ -131,6 +133,10 @@ def kernel_fn(
     io_dtype = q.dtype
     B, T = q.shape[0], q.shape[1]
     total = B * T
+    if cu_seqlens is None and T == 1 and B > 0 and _mode(mode) == "auto":
+        from . import qwen35moe_gdn_decode
+
+        return qwen35moe_gdn_decode.kernel_fn(q, k, v, g, beta, state, scale)
     if cu_seqlens is None:
         lengths = (T,) * B
     else:
@@ -211,8 +217,10 @@ def _schedule(mode: str, units: int, total_chunks: int, hv: int, dev: torch.devi
 
 
 def schedule(q: torch.Tensor, v: torch.Tensor, cu_seqlens=None, mode: str = "auto") -> str:
-    """The schedule kernel_fn picks for these inputs: "fused", "split" or "overlap"."""
+    """The schedule kernel_fn picks for these inputs: "fused", "split", "overlap" or "decode"."""
     B, T, hv = q.shape[0], q.shape[1], v.shape[2]
+    if cu_seqlens is None and T == 1 and B > 0 and _mode(mode) == "auto":
+        return "decode"
     lengths = (T,) * B if cu_seqlens is None else _lengths(cu_seqlens, T)
     chunks = sum((n + 63) // 64 for n in lengths)
     return _schedule(mode, len(lengths) * hv, chunks, hv, q.device)

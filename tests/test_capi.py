@@ -118,3 +118,28 @@ def test_gdn_split_rejects_bad_arguments():
     bad = list(args)
     bad[11] = 0  # no sequences: no-op
     assert lib.tokmix_gdn_prefill_split(*bad) == _lib.TOKMIX_OK
+
+
+def test_gdn_decode_rejects_bad_arguments():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    # q k v g beta state_in state_out out batch hk hv dk dv scale io stream
+    args = [p, p, p, p, p, None, p, p, 4, 16, 32, 128, 128, 0.08, 0, None]
+    bad = list(args)
+    bad[6] = None  # state_out
+    assert lib.tokmix_gdn_decode(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "null" in _lib.last_error()
+    bad = list(args)
+    bad[10] = 24  # heads_v not a multiple of heads_k
+    assert lib.tokmix_gdn_decode(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    bad = list(args)
+    bad[11] = 64  # head dim
+    assert lib.tokmix_gdn_decode(*bad) == _lib.TOKMIX_ERR_UNSUPPORTED
+    bad = list(args)
+    bad[14] = 1  # fp32 io
+    assert lib.tokmix_gdn_decode(*bad) == _lib.TOKMIX_ERR_UNSUPPORTED
+    bad = list(args)
+    bad[1] = ctypes.c_void_p(24)  # misaligned k
+    assert lib.tokmix_gdn_decode(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "aligned" in _lib.last_error()
+    bad = list(args)
+    bad[8] = 0  # empty batch: no-op
+    assert lib.tokmix_gdn_decode(*bad) == _lib.TOKMIX_OK
