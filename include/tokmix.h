@@ -60,7 +60,7 @@ extern "C" {
  * q, o: [batch, heads_q, seqlen_q, head_dim] (BHSD) or [batch, seqlen_q, heads_q, head_dim] (BSHD)
  * k, v: same layout with heads_kv and seqlen_kv.  Contiguous; base pointers 16-byte aligned.
  * heads_q must be a multiple of heads_kv; query head h reads key/value head h / (heads_q/heads_kv).
- * head_dim in {64, 128}.  causal != 0 masks key j for query i when j > i (top-left aligned, as
+ * head_dim in {64, 128, 256}.  causal != 0 masks key j for query i when j > i (top-left aligned, as
  * torch's scaled_dot_product_attention(is_causal=True)).
  * Replaces flash_attention_2_forward (kernels_optimized/flash_attention_2.cu:1121-1258), which
  * supported only BHSD, heads_q == heads_kv and head_dim == 128. */

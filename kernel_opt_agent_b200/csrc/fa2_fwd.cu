@@ -23,6 +23,7 @@
 //     end divides O by l and stores the bf16 row.
 // TMEM columns: S_0 [0,128)  O_0 [128,128+D)  S_1 [256,384)  O_1 [384,384+D).
 // Every wait is bounded (sm100.cuh): a stuck pipeline sets a status bit and the CTA drains.
+// head_dim 256 has its own kernel (namespace d256 below): one query tile per CTA, S double-buffered.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -420,6 +421,317 @@ int launch(const void* q, const void* k, const void* v, void* o, int batch, int 
   return check_launch("tokmix_fa2_fwd");
 }
 
+// ---------------------------------------------------------------------------------------------
+// head_dim 256.  Two tiles' S and O (2 x (128 + 256) TMEM columns) do not fit in TMEM, so one CTA
+// takes one 128-row query tile and double-buffers S instead: the tensor core computes S(j+1)
+// while the softmax warps work on S(j).  Keys come in tiles of 64 (K and V 32 KB each, two-stage
+// rings; Q 64 KB: 192 KB of shared memory).  Order of the MMAs: S(0) S(1) | PV(0) S(2) | PV(1)
+// S(3) | ...; S(j+2) overwrites the buffer PV(j) read P(j) from, after PV(j) in issue order.
+// The lazy O rescale of step j needs PV(j-1) complete (it may still accumulate into O): the
+// softmax warps then wait for its commit, which a rescale makes rare.
+// Warps 0-3: softmax (thread = query row); warp 4: TMA; warp 5: TMEM owner and MMA issuer.
+// TMEM columns: S0 [0,64)  S1 [64,128)  O [128,384).
+// ---------------------------------------------------------------------------------------------
+namespace d256 {
+
+constexpr int kD = 256;
+constexpr int kBN = 64;                            // keys per kv tile
+constexpr int kThreads = 192;
+constexpr int kWarpTma = 4, kWarpMma = 5;
+constexpr int kQBytes = kBM * kD * 2;              // 64 KB: four boxes of 128 rows x 64 columns
+constexpr int kQBox = kBM * 128;                   // 16 KB
+constexpr int kKVBytes = kBN * kD * 2;             // 32 KB: four boxes of 64 rows x 64 columns
+constexpr int kKVBox = kBN * 128;                  // 8 KB
+constexpr int kQ = 0, kK = kQBytes, kV = kQBytes + 2 * kKVBytes, kBytes = kQBytes + 4 * kKVBytes;
+__device__ __forceinline__ uint32_t col_s(int st) { return st ? 64u : 0u; }  // S buffer st
+constexpr uint32_t kColO = 128;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fa2_fwd_d256_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                        const __grid_constant__ CUtensorMap map_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_q, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_s[2], bar_p[2], bar_pv[2];
+  __shared__ uint64_t bar_o, bar_drain;
+  __shared__ uint32_t tmem_base_shared;
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  // unit -> (query tile, batch, head); the heaviest (last) causal tiles first
+  const int per_row = p.batch * p.hq;
+  const int rev = blockIdx.x / per_row;
+  const int rem = blockIdx.x - rev * per_row;
+  const int b = rem / p.hq;
+  const int head = rem - b * p.hq;
+  const int kvh = head / (p.hq / p.hkv);
+  const int q0 = (p.n_qtiles - 1 - rev) * kBM;
+  const int kv_tiles_all = (p.skv + kBN - 1) / kBN;
+  const int n_kv = p.causal ? min(kv_tiles_all, (q0 + kBM - 1) / kBN + 1) : kv_tiles_all;
+
+  if (threadIdx.x == 0) {
+    cta_abort_flag() = 0u;
+    mbar_init(&bar_q, 1);
+    mbar_init(&bar_o, 1);
+    mbar_init(&bar_drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_kfull[i], 1);
+      mbar_init(&bar_kempty[i], 1);
+      mbar_init(&bar_vfull[i], 1);
+      mbar_init(&bar_vempty[i], 1);
+      mbar_init(&bar_s[i], 1);
+      mbar_init(&bar_p[i], 128);
+      mbar_init(&bar_pv[i], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(&tmem_base_shared, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base_shared;
+
+  if (warp == kWarpTma) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&map_q);
+      tma_prefetch_desc(&map_k);
+      tma_prefetch_desc(&map_v);
+      mbar_arrive_expect_tx(&bar_q, kQBytes);
+      for (int bx = 0; bx < kD / 64; ++bx) tma_load_4d(smem + kQ + bx * kQBox, &map_q, &bar_q, bx * 64, q0, head, b);
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait(&bar_kempty[st], ((j >> 1) - 1) & 1, p.status, kDevTimeoutPipe)) break;
+        mbar_arrive_expect_tx(&bar_kfull[st], kKVBytes);
+        for (int bx = 0; bx < kD / 64; ++bx)
+          tma_load_4d(smem + kK + st * kKVBytes + bx * kKVBox, &map_k, &bar_kfull[st], bx * 64, j * kBN, kvh, b);
+        if (j >= 2 && !mbar_wait(&bar_vempty[st], ((j >> 1) - 1) & 1, p.status, kDevTimeoutPipe)) break;
+        mbar_arrive_expect_tx(&bar_vfull[st], kKVBytes);
+        for (int bx = 0; bx < kD / 64; ++bx)
+          tma_load_4d(smem + kV + st * kKVBytes + bx * kKVBox, &map_v, &bar_vfull[st], bx * 64, j * kBN, kvh, b);
+        issued = j + 1;
+      }
+      mbar_drain(&bar_q, 0);
+      for (int j = max(0, issued - 2); j < issued; ++j) {
+        mbar_drain(&bar_kfull[j & 1], (j >> 1) & 1);
+        mbar_drain(&bar_vfull[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_s = make_idesc(kBM, kBN, 1, 0, 0);
+      const uint32_t idesc_o = make_idesc(kBM, kD, 1, 0, 1);
+      const uint32_t qa = smem_u32(smem + kQ);
+      // S(j) = Q K(j)^T into S buffer j & 1 (K in stage j & 1)
+      auto issue_s = [&](int j) {
+        const uint32_t ka = smem_u32(smem + kK + (j & 1) * kKVBytes);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          umma_bf16_ss(tbase + col_s(j & 1), make_sdesc_sw128(qa + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024),
+                       make_sdesc_sw128(ka + (kk >> 2) * kKVBox + (kk & 3) * 32, 16, 1024), idesc_s,
+                       kk > 0 ? 1u : 0u);
+        umma_commit(&bar_s[j & 1]);
+      };
+      bool ok = mbar_wait(&bar_q, 0, p.status, kDevTimeoutTma);
+      for (int j = 0; ok && j < min(2, n_kv); ++j) {
+        ok = mbar_wait(&bar_kfull[j], 0, p.status, kDevTimeoutTma);
+        if (ok) {
+          tc_fence_after();
+          issue_s(j);
+          umma_commit(&bar_kempty[j]);
+        }
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j & 1;
+        ok = mbar_wait(&bar_vfull[st], (j >> 1) & 1, p.status, kDevTimeoutTma) &&
+             mbar_wait(&bar_p[st], (j >> 1) & 1, p.status, kDevTimeoutPipe);
+        if (!ok) break;
+        tc_fence_after();
+        // O (+)= P(j) V(j): P read from TMEM (bf16 over S buffer j & 1), V MN-major in smem
+        const uint32_t va = smem_u32(smem + kV + st * kKVBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          umma_bf16_ts(tbase + kColO, tbase + col_s(st) + 8 * kk, make_sdesc_sw128(va + kk * 2048, kKVBox, 1024),
+                       idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&bar_pv[st]);
+        umma_commit(&bar_vempty[st]);
+        if (j == n_kv - 1) umma_commit(&bar_o);
+        if (j + 2 < n_kv) {
+          ok = mbar_wait(&bar_kfull[st], ((j + 2) >> 1) & 1, p.status, kDevTimeoutTma);
+          if (ok) {
+            tc_fence_after();
+            issue_s(j + 2);
+            umma_commit(&bar_kempty[st]);
+          }
+        }
+      }
+      umma_commit(&bar_drain);
+      mbar_drain(&bar_drain, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax warps 0-3
+    const int qrow_local = warp * 32 + lane;
+    const int qrow = q0 + qrow_local;
+    const uint32_t lane_base = tmem_addr(tbase, warp * 32, 0);
+    const float c = p.scale_log2;
+    float m = -INFINITY;
+    float l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int st = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_s[st], (j >> 1) & 1, p.status, kDevTimeoutMma))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t raw[64];
+      tmem_ld64(lane_base + col_s(st), raw);
+      float s[64];
+#pragma unroll
+      for (int cc = 0; cc < 64; ++cc) s[cc] = __uint_as_float(raw[cc]);
+      const int kv0 = j * kBN;
+      if ((p.causal && kv0 + kBN - 1 > q0) || (kv0 + kBN > p.skv)) {
+        const int lim = (p.causal ? min(qrow + 1, p.skv) : p.skv) - kv0;
+#pragma unroll
+        for (int cc = 0; cc < 64; ++cc)
+          if (cc >= lim) s[cc] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int cc = 1; cc < 64; ++cc) mx = fmaxf(mx, s[cc]);
+      const float mx_scaled = mx * c;
+      const bool grow = mx_scaled > m + kRescaleThreshold;
+      float alpha = 1.0f;
+      if (grow) {
+        alpha = ex2_approx(m - mx_scaled);
+        m = mx_scaled;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O holds sum_{<j} P V once PV(j-1) has completed
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar_pv[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status, kDevTimeoutMma))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int dc = 0; dc < kD; dc += 32) {
+          uint32_t o_raw[32];
+          tmem_ld32(lane_base + kColO + dc, o_raw);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * alpha);
+          tmem_st32(lane_base + kColO + dc, o_raw);
+        }
+      }
+      l *= alpha;
+      float rowsum = 0.0f;
+#pragma unroll
+      for (int chunk = 0; chunk < 2; ++chunk) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = ex2_approx(fmaf(s[chunk * 32 + 2 * e], c, -m));
+          const float p1 = ex2_approx(fmaf(s[chunk * 32 + 2 * e + 1], c, -m));
+          rowsum += p0 + p1;
+          packed[e] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(lane_base + col_s(st) + chunk * 16, packed);
+      }
+      l += rowsum;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar_p[st]);
+    }
+    if (ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&bar_o, 0, p.status, kDevTimeoutMma))) {
+      tc_fence_after();
+      const float inv_l = 1.0f / l;
+      __nv_bfloat16* orow = p.o + static_cast<long long>(b) * p.o_sb + static_cast<long long>(head) * p.o_sh +
+                            static_cast<long long>(qrow) * p.o_ss;
+#pragma unroll 1
+      for (int dc = 0; dc < kD; dc += 32) {
+        uint32_t o_raw[32];
+        tmem_ld32(lane_base + kColO + dc, o_raw);
+        uint32_t packed[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          packed[e] = pack_bf16x2(__uint_as_float(o_raw[2 * e]) * inv_l, __uint_as_float(o_raw[2 * e + 1]) * inv_l);
+        if (qrow < p.sq) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + dc);
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4)
+            dst[v4] = make_uint4(packed[4 * v4], packed[4 * v4 + 1], packed[4 * v4 + 2], packed[4 * v4 + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+int launch(const void* q, const void* k, const void* v, void* o, int batch, int hq, int hkv, int sq, int skv,
+           int layout, int causal, float sm_scale, uint32_t* status, cudaStream_t stream) {
+  auto make = [&](CUtensorMap* map, const void* base, int s, int h, uint32_t rows) {
+    uint64_t dims[4] = {static_cast<uint64_t>(kD), static_cast<uint64_t>(s), static_cast<uint64_t>(h),
+                        static_cast<uint64_t>(batch)};
+    uint64_t strides[3];
+    const uint64_t row = static_cast<uint64_t>(kD) * 2;
+    if (layout == TOKMIX_LAYOUT_BHSD) {
+      strides[0] = row;
+      strides[1] = row * s;
+      strides[2] = row * s * h;
+    } else {
+      strides[0] = row * h;
+      strides[1] = row;
+      strides[2] = row * s * h;
+    }
+    uint32_t box[4] = {64, rows, 1, 1};
+    return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  };
+  CUtensorMap mq, mk, mv;
+  if (!make(&mq, q, sq, hq, kBM) || !make(&mk, k, skv, hkv, kBN) || !make(&mv, v, skv, hkv, kBN))
+    return TOKMIX_ERR_INVALID_ARGUMENT;
+  Params p{};
+  p.o = static_cast<__nv_bfloat16*>(o);
+  if (layout == TOKMIX_LAYOUT_BHSD) {
+    p.o_ss = kD;
+    p.o_sh = static_cast<long long>(kD) * sq;
+    p.o_sb = static_cast<long long>(kD) * sq * hq;
+  } else {
+    p.o_sh = kD;
+    p.o_ss = static_cast<long long>(kD) * hq;
+    p.o_sb = static_cast<long long>(kD) * sq * hq;
+  }
+  p.batch = batch;
+  p.hq = hq;
+  p.hkv = hkv;
+  p.sq = sq;
+  p.skv = skv;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.n_qtiles = (sq + kBM - 1) / kBM;
+  p.status = status;
+  const long long units = static_cast<long long>(p.n_qtiles) * batch * hq;
+  if (units <= 0) return TOKMIX_OK;
+  if (units > 0x7FFFFFFFll) return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_fa2_fwd: too many tiles (%lld)", units);
+  const int smem_bytes = kBytes + 1024;
+  if (!ensure_smem_attr(reinterpret_cast<const void*>(&fa2_fwd_d256_kernel), smem_bytes))
+    return check_launch("tokmix_fa2_fwd: cudaFuncSetAttribute");
+  fa2_fwd_d256_kernel<<<static_cast<unsigned>(units), kThreads, smem_bytes, stream>>>(mq, mk, mv, p);
+  return check_launch("tokmix_fa2_fwd (head_dim 256)");
+}
+
+}  // namespace d256
+
 }  // namespace fa2
 }  // namespace tokmix
 
@@ -452,7 +764,10 @@ extern "C" int tokmix_fa2_fwd(const void* q, const void* k, const void* v, void*
     case 128:
       return fa2::launch<128>(q, k, v, o, batch, heads_q, heads_kv, seqlen_q, seqlen_kv, layout, causal, sm_scale,
                               status, s);
+    case 256:
+      return fa2::d256::launch(q, k, v, o, batch, heads_q, heads_kv, seqlen_q, seqlen_kv, layout, causal, sm_scale,
+                               status, s);
     default:
-      return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_fa2_fwd: head_dim %d not supported (64 or 128)", head_dim);
+      return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_fa2_fwd: head_dim %d not supported (64, 128 or 256)", head_dim);
   }
 }

@@ -5,7 +5,7 @@
 
 ``kernel_fn`` runs the sm_100a kernel in libtokmix.so (``tokmix_fa2_fwd``); there is no fallback.
 Compared with the reference module (``kernels_optimized/flash_attention_2.py:110-140``) it also
-accepts grouped-query attention (k/v with fewer heads), head_dim 64 and a ``layout="bshd"``
+accepts grouped-query attention (k/v with fewer heads), head_dim 64 and 256 and a ``layout="bshd"``
 keyword; with the reference's arguments it behaves the same: q, k, v bf16 CUDA tensors
 [batch, heads, seq, head_dim], default scale 1/sqrt(head_dim), returns a new bf16 tensor.
 """
@@ -21,7 +21,7 @@ from . import _lib
 
 KERNEL_TYPE = "flash_attention_2"
 _HEAD_DIM = 128
-_HEAD_DIMS = (64, 128)
+_HEAD_DIMS = (64, 128, 256)
 _DTYPE = torch.bfloat16
 _CHECK_STATUS = os.environ.get("TOKMIX_CHECK_STATUS", "0") == "1"
 

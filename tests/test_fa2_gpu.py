@@ -48,6 +48,11 @@ def _run_and_check(b, hq, hkv, s, d, causal, layout, seed=0, scale=None, tol=TOL
     (1, 2, 2, 1, 128, True, "bhsd"),
     (1, 2, 2, 127, 64, False, "bhsd"),
     (1, 4, 1, 640, 128, False, "bshd"),
+    (1, 2, 2, 128, 256, True, "bhsd"),      # head_dim 256: one query tile per CTA
+    (1, 4, 1, 333, 256, True, "bhsd"),
+    (2, 8, 1, 200, 256, True, "bshd"),      # config 4's 8:1 grouping
+    (1, 2, 2, 65, 256, False, "bhsd"),
+    (1, 2, 1, 1, 256, True, "bhsd"),
 ])
 def test_fa2_matches_oracle(cuda_device, b, hq, hkv, s, d, causal, layout):
     _run_and_check(b, hq, hkv, s, d, causal, layout, seed=s + hq)
@@ -107,6 +112,25 @@ def test_fa2_full_size_gqa_sampled_rows(cuda_device):
         q = inp["q"][b, h, i].float().cpu().numpy()
         kk = inp["k"][b, h // 4, : i + 1].float().cpu().numpy()
         vv = inp["v"][b, h // 4, : i + 1].float().cpu().numpy()
+        s = kk @ q * inp["sm_scale"]
+        p = np.exp(s - s.max())
+        ref = (p @ vv) / p.sum()
+        np.testing.assert_allclose(out[b, h, i].float().cpu().numpy(), ref, **TOL, err_msg=str((b, h, i)))
+
+
+def test_fa2_hybrid_config_d256_sampled_rows(cuda_device):
+    """The hybrid sweep's attention (Hq=16, Hkv=2, D=256, causal) at B=2 S=4096: sampled query
+    rows against the fp32 oracle."""
+    inp = fa2.get_inputs(2, 16, 4096, 256, seed=4, head_num_kv=2)
+    out = fa2.kernel_fn(**inp)
+    fa2.check_device_status(cuda_device)
+    rng = np.random.default_rng(1)
+    rows = [(0, 0, 0), (1, 15, 4095), (0, 7, 63), (1, 8, 64), (0, 3, 2047), (1, 12, 2048)]
+    rows += [(int(rng.integers(2)), int(rng.integers(16)), int(rng.integers(4096))) for _ in range(30)]
+    for b, h, i in rows:
+        q = inp["q"][b, h, i].float().cpu().numpy()
+        kk = inp["k"][b, h // 8, : i + 1].float().cpu().numpy()
+        vv = inp["v"][b, h // 8, : i + 1].float().cpu().numpy()
         s = kk @ q * inp["sm_scale"]
         p = np.exp(s - s.max())
         ref = (p @ vv) / p.sum()
