@@ -148,6 +148,12 @@ int tokmix_gdn_decode(const void* q, const void* k, const void* v, const float* 
                       const float* state_in, float* state_out, void* out, int batch, int heads_k, int heads_v,
                       int head_dim_k, int head_dim_v, float scale, int io_dtype, void* stream);
 
+/* Per-row L2 normalisation (the GDN qk_l2norm option): y[r] = x[r] / sqrt(sum x[r]^2 + eps), fp32
+ * arithmetic.  x: [rows, dim] bf16 (x_dtype TOKMIX_DTYPE_BF16) or fp32; y: [rows, dim] bf16; dim
+ * must be 128; both 16-byte aligned.  The reference leaves this step to its caller
+ * (kernels/qwen35moe_gdn_prefill.py:107-136 takes normalised q and k). */
+int tokmix_l2norm_rows(const void* x, int x_dtype, void* y, long long rows, int dim, float eps, void* stream);
+
 /* Text of the last error reported on the calling thread ("" if none). */
 const char* tokmix_last_error(void);
 

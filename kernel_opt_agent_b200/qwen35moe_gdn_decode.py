@@ -16,6 +16,7 @@ step its optimised prefill special-cases for one-token chunks
 may be bf16 (native) or fp32 (rounded to bf16 on the device; out is then returned as fp32).
 ``inplace=True`` (keyword) updates ``state`` itself and returns it as final_state: a decode
 loop then moves each state through HBM once per token and allocates nothing for it.
+``qk_l2norm=True`` L2-normalises q and k first, as in ``qwen35moe_gdn_prefill``.
 """
 
 from __future__ import annotations
@@ -23,7 +24,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .qwen35moe_gdn_prefill import D, H_K, H_V
+from .qwen35moe_gdn_prefill import D, H_K, H_V, l2norm_rows
 
 KERNEL_TYPE = "qwen35moe_gdn_decode"
 
@@ -66,14 +67,15 @@ def kernel_fn(
     scale: float | None = None,
     *,
     inplace: bool = False,
+    qk_l2norm: bool = False,
 ) -> list[torch.Tensor]:
     batch, hk, hv = _validate(q, k, v, g, beta, state)
     if scale is None:
         scale = D ** -0.5
     dev = q.device
     io_dtype = q.dtype
-    qb = q.to(torch.bfloat16).contiguous()
-    kb = k.to(torch.bfloat16).contiguous()
+    qb = l2norm_rows(q) if qk_l2norm else q.to(torch.bfloat16).contiguous()
+    kb = l2norm_rows(k) if qk_l2norm else k.to(torch.bfloat16).contiguous()
     vb = v.to(torch.bfloat16).contiguous()
     gf = g.to(torch.float32).contiguous()
     bf = beta.to(torch.float32).contiguous()

@@ -22,6 +22,10 @@ Extensions over the reference module:
 * ``cu_seqlens`` (keyword): variable-length sequences packed along T with q.shape[0] == 1 and
   one initial state per sequence (state [N,Hv,128,128]); ``state=None`` means zero states.
 * any Hk dividing Hv (the reference fixes Hk=16, Hv=32).
+* ``qk_l2norm`` (keyword, default False): L2-normalise q and k per (token, head) on the device
+  first, ``x / sqrt(sum x^2 + 1e-6)`` in fp32 (``l2norm_rows``), as the workloads' generators do
+  before calling the reference; the result is the kernels' bf16 operand, so with fp32 inputs the
+  normalisation replaces the conversion pass.
 * ``mode`` (keyword): "auto" (default), "fused", "split" or "overlap" selects the schedule; the
   environment variable TOKMIX_GDN_MODE overrides "auto".  "auto" picks "fused" when the units
   fill the SMs, else "overlap" when at least 8 SMs are left for the preparation CTAs, else
@@ -45,6 +49,7 @@ H_K = 16
 H_V = 32
 _CHECK_STATUS = os.environ.get("TOKMIX_CHECK_STATUS", "0") == "1"
 _SPLIT_MAX_WORKSPACE = 1 << 30  # bytes; larger problems use the one-launch schedule
+QK_L2NORM_EPS = 1e-6
 
 _meta_cache: dict = {}
 
@@ -125,6 +130,7 @@ def kernel_fn(
     *,
     cu_seqlens=None,
     mode: str = "auto",
+    qk_l2norm: bool = False,
 ) -> list[torch.Tensor]:
     nseq, hk, hv = _validate(q, k, v, g, beta, state, cu_seqlens)
     if scale is None:
@@ -136,7 +142,7 @@ def kernel_fn(
     if cu_seqlens is None and T == 1 and B > 0 and _mode(mode) == "auto":
         from . import qwen35moe_gdn_decode
 
-        return qwen35moe_gdn_decode.kernel_fn(q, k, v, g, beta, state, scale)
+        return qwen35moe_gdn_decode.kernel_fn(q, k, v, g, beta, state, scale, qk_l2norm=qk_l2norm)
     if cu_seqlens is None:
         lengths = (T,) * B
     else:
@@ -146,8 +152,8 @@ def kernel_fn(
         fs = state.to(torch.float32).clone() if state is not None else torch.zeros((nseq, hv, D, D), device=dev)
         return [out, fs]
     cu_t, order_t, cb_t, total_chunks, cb_host = _device_meta(lengths, dev)
-    qb = q.to(torch.bfloat16).contiguous()
-    kb = k.to(torch.bfloat16).contiguous()
+    qb = l2norm_rows(q) if qk_l2norm else q.to(torch.bfloat16).contiguous()
+    kb = l2norm_rows(k) if qk_l2norm else k.to(torch.bfloat16).contiguous()
     vb = v.to(torch.bfloat16).contiguous()
     gf = g.to(torch.float32).contiguous()
     bf = beta.to(torch.float32).contiguous()
@@ -180,6 +186,22 @@ def kernel_fn(
     if io_dtype != torch.bfloat16:
         out = out.to(io_dtype)
     return [out, final_state]
+
+
+def l2norm_rows(x: torch.Tensor, eps: float = QK_L2NORM_EPS) -> torch.Tensor:
+    """x / sqrt(sum(x^2, last dim) + eps) per 128-element row, fp32 arithmetic, bf16 result
+    (``tokmix_l2norm_rows``).  x: bf16 or fp32 CUDA tensor whose last dimension is 128."""
+    if x.shape[-1] != D or x.dtype not in (torch.bfloat16, torch.float32) or not x.is_cuda:
+        raise ValueError("l2norm_rows takes a bf16 or fp32 CUDA tensor with last dimension 128")
+    x = x.contiguous()
+    y = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    rows = x.numel() // D
+    with torch.cuda.device(x.device):
+        rc = _lib.load().tokmix_l2norm_rows(
+            x.data_ptr(), _lib.DTYPE_BF16 if x.dtype == torch.bfloat16 else _lib.DTYPE_FP32, y.data_ptr(), rows, D,
+            float(eps), _lib.stream_ptr(x.device))
+    _lib.check(rc, "l2norm_rows")
+    return y
 
 
 def _record_order(lengths: tuple[int, ...], chunk_base: list[int], hv: int, device: torch.device) -> torch.Tensor:

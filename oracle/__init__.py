@@ -100,6 +100,14 @@ def gdn_recurrent(q, k, v, g, beta, state=None, scale=None, cu_seqlens=None, nth
     return out, st_out
 
 
+def l2norm_rows(x, eps: float = 1e-6) -> np.ndarray:
+    """x / sqrt(sum(x^2, last axis) + eps) in fp32: the q/k normalisation the workloads apply
+    before the reference's GDN kernel (which takes normalised q, k:
+    ``kernels/qwen35moe_gdn_prefill.py:107-136``), restated for the ``qk_l2norm`` option."""
+    x = _f32(x)
+    return (x / np.sqrt((x * x).sum(axis=-1, keepdims=True, dtype=np.float32) + np.float32(eps))).astype(np.float32)
+
+
 def gdn_recurrent_numpy(q, k, v, g, beta, state=None, scale=None):
     """Row-vectorised numpy transcription of ``kernels/qwen35moe_gdn_prefill.cu:55-99`` (batched
     layout only; small cases).  fp32 throughout."""

@@ -143,3 +143,15 @@ def test_gdn_decode_rejects_bad_arguments():
     bad = list(args)
     bad[8] = 0  # empty batch: no-op
     assert lib.tokmix_gdn_decode(*bad) == _lib.TOKMIX_OK
+
+
+def test_l2norm_rows_rejects_bad_arguments():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    assert lib.tokmix_l2norm_rows(p, 0, p, 10, 64, 1e-6, None) == _lib.TOKMIX_ERR_UNSUPPORTED  # row length
+    assert lib.tokmix_l2norm_rows(p, 7, p, 10, 128, 1e-6, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT  # dtype
+    assert lib.tokmix_l2norm_rows(p, 0, None, 10, 128, 1e-6, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert lib.tokmix_l2norm_rows(p, 0, p, -1, 128, 1e-6, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert lib.tokmix_l2norm_rows(p, 0, p, 10, 128, -1.0, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert lib.tokmix_l2norm_rows(p, 0, p, 0, 128, 1e-6, None) == _lib.TOKMIX_OK  # nothing to do
+

@@ -176,3 +176,51 @@ def test_gdn_varlen_full_size(cuda_device, oracle_threads):
             o_ref, s_ref = _oracle({**one}, oracle_threads)
             np.testing.assert_allclose(_np(o1), o_ref, **OUT_TOL)
             np.testing.assert_allclose(_np(s1), s_ref, **STATE_TOL)
+
+
+def _raw_qk_inputs(b, t, seed, scale=3.0, dtype=torch.bfloat16, hk=16, hv=32):
+    """The random workload with q, k left unnormalised (N(0, scale^2))."""
+    inp = gcfg.random_inputs(b, t, dtype=dtype, seed=seed, state_std=0.02, hk=hk, hv=hv)
+    gen = torch.Generator().manual_seed(seed + 1)
+    for n in ("q", "k"):
+        inp[n] = (torch.randn(inp[n].shape, generator=gen) * scale).to(dtype).to(inp[n].device)
+    return inp
+
+
+def _normalised_for_oracle(inp):
+    """The kernel's operands: q/|q|, k/|k| in fp32 then rounded to bf16, v rounded to bf16."""
+    ref = dict(inp)
+    for n in ("q", "k"):
+        ref[n] = torch.from_numpy(oracle.l2norm_rows(_np(inp[n]))).to(torch.bfloat16)
+    ref["v"] = inp["v"].to(torch.bfloat16)
+    return ref
+
+
+@pytest.mark.parametrize("b,t,dtype", [(1, 200, torch.bfloat16), (2, 65, torch.float32), (3, 1, torch.bfloat16)])
+def test_gdn_qk_l2norm_matches_oracle(cuda_device, oracle_threads, b, t, dtype):
+    """qk_l2norm=True on unnormalised q, k equals the recurrence on q/|q|, k/|k| (t=1 runs the decode kernel)."""
+    inp = _raw_qk_inputs(b, t, seed=31 + t, dtype=dtype)
+    out, fs = gdn.kernel_fn(**inp, qk_l2norm=True)
+    o_ref, s_ref = _oracle(_normalised_for_oracle(inp), oracle_threads)
+    np.testing.assert_allclose(_np(out), o_ref, **OUT_TOL)
+    np.testing.assert_allclose(_np(fs), s_ref.reshape(fs.shape), **STATE_TOL)
+
+
+def test_gdn_qk_l2norm_is_idempotent_on_normalised_inputs(cuda_device):
+    inp = gcfg.random_inputs(1, 300, seed=8, state_std=0.02)
+    a = gdn.kernel_fn(**inp)
+    b = gdn.kernel_fn(**inp, qk_l2norm=True)
+    np.testing.assert_allclose(_np(b[0]), _np(a[0]), **OUT_TOL)
+    np.testing.assert_allclose(_np(b[1]), _np(a[1]), **STATE_TOL)
+
+
+def test_l2norm_rows_kernel(cuda_device):
+    gen = torch.Generator().manual_seed(2)
+    for dtype in (torch.bfloat16, torch.float32):
+        x = (torch.randn(5, 7, 16, 128, generator=gen) * 5.0).to(dtype).to(cuda_device)
+        y = gdn.l2norm_rows(x)
+        assert y.dtype == torch.bfloat16 and y.shape == x.shape
+        ref = oracle.l2norm_rows(_np(x))
+        np.testing.assert_allclose(_np(y), ref, atol=4e-3, rtol=8e-3)
+    assert gdn.l2norm_rows(torch.zeros(0, 128, device=cuda_device)).shape == (0, 128)
+

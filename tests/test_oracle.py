@@ -118,3 +118,11 @@ def test_gdn_strong_negative_gate_is_finite():
     assert np.isfinite(o).all() and np.isfinite(s).all()
     o2, s2 = oracle.gdn_chunked_numpy(q, k, v, g, beta, st)
     np.testing.assert_allclose(o, o2, atol=1e-5, rtol=1e-4)
+
+
+def test_l2norm_rows_oracle_unit_rows():
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((6, 128)).astype(np.float32) * 4
+    y = oracle.l2norm_rows(x)
+    np.testing.assert_allclose(np.linalg.norm(y, axis=-1), 1.0, rtol=1e-5)
+    np.testing.assert_allclose(oracle.l2norm_rows(np.zeros((2, 128), np.float32)), 0.0)
