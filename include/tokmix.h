@@ -119,12 +119,15 @@ int tokmix_gdn_prefill_noalloc(const void* q, const void* k, const void* v, cons
  *                     stages share ONE cooperative launch: chain CTAs consume each chunk's record
  *                     as soon as preparation CTAs on the other SMs have written it.  NULL (or a
  *                     device where the cooperative launch is refused) gives two ordinary launches.
+ *   checkpoints:      NULL, or device fp32 [total_chunks, heads_v, 128, 128]: the state after each
+ *                     chunk, checkpoints[chunk_base[n] + c] = the state of sequence n after its
+ *                     tokens [0, 64 (c + 1)) (its last entry equals that sequence's final state)
  *   workspace:        device memory of at least tokmix_gdn_split_workspace_bytes(total_chunks,
  *                     heads_v) bytes, 16-byte aligned (contents need no initialisation)
  * No counterpart in the reference (its prefill is one kernel chain per layer call). */
 int tokmix_gdn_prefill_split(const void* q, const void* k, const void* v, const float* g, const float* beta,
-                             const float* initial_state, void* out, float* final_state, const int32_t* cu_seqlens_dev,
-                             const int32_t* chunk_base_dev, const int32_t* record_order_dev, int num_seqs,
+                             const float* initial_state, void* out, float* final_state, float* checkpoints,
+                             const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev, const int32_t* record_order_dev, int num_seqs,
                              int total_tokens, int total_chunks, int heads_k, int heads_v, int head_dim_k,
                              int head_dim_v, float scale, int io_dtype, void* workspace, long long workspace_bytes,
                              uint32_t* status, void* stream);

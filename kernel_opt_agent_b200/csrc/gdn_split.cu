@@ -111,6 +111,7 @@ struct PrepParams {
 struct ChainParams {
   const float* state_in;
   float* state_out;
+  float* checkpoints;  // [total_chunks, hv, 128, 128] or null: the state after each chunk
   __nv_bfloat16* out;
   const int32_t* cu_seqlens;
   const int32_t* chunk_base;
@@ -578,6 +579,13 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
           const float gam = params_of(c).gamma_c;
           uint32_t sv[64];
           tmem_ld64(lb + kColS + 64 * hh, sv);
+          if (p.checkpoints != nullptr && c > 0) {  // S(c): the state after chunk c-1
+            float* dst = p.checkpoints + (static_cast<size_t>(gc0 + c - 1) * p.hv + h) * kD * kD + v * kD + 64 * hh;
+#pragma unroll
+            for (int j = 0; j < 64; j += 4)
+              __stcs(reinterpret_cast<float4*>(dst + j), make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
+                                                                     __uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3])));
+          }
 #pragma unroll
           for (int j = 0; j < 64; ++j) sv[j] = __float_as_uint(__uint_as_float(sv[j]) * gam);
           tmem_st32(lb + kColS + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
@@ -632,10 +640,16 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
         tmem_ld64(lb + kColS + 64 * hh, sv);
         if (last) {
           float* dst = p.state_out + state_off + v * kD + 64 * hh;
+          float* ck = p.checkpoints != nullptr
+                          ? p.checkpoints + (static_cast<size_t>(gc0 + c) * p.hv + h) * kD * kD + v * kD + 64 * hh
+                          : nullptr;
 #pragma unroll
-          for (int j = 0; j < 64; j += 4)
-            *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
-                                                              __uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3]));
+          for (int j = 0; j < 64; j += 4) {
+            const float4 val = make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
+                                           __uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3]));
+            *reinterpret_cast<float4*>(dst + j) = val;
+            if (ck != nullptr) __stcs(reinterpret_cast<float4*>(ck + j), val);
+          }
         } else {
           uint32_t hi[32], lo[32];
 #pragma unroll
@@ -797,7 +811,7 @@ extern "C" long long tokmix_gdn_split_workspace_bytes(int total_chunks, int head
 
 extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void* v, const float* g,
                                         const float* beta, const float* initial_state, void* out, float* final_state,
-                                        const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev,
+                                        float* checkpoints, const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev,
                                         const int32_t* record_order_dev, int num_seqs, int total_tokens,
                                         int total_chunks, int heads_k, int heads_v, int head_dim_k,
                                         int head_dim_v, float scale, int io_dtype, void* workspace,
@@ -824,7 +838,7 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: workspace of %lld bytes needed (got %lld)", need,
                 workspace_bytes);
   for (const void* ptr : {q, k, v, static_cast<const void*>(initial_state), static_cast<const void*>(final_state),
-                          static_cast<const void*>(workspace)})
+                          static_cast<const void*>(checkpoints), static_cast<const void*>(workspace)})
     if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
       return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: tensors must be 16-byte aligned");
   if (const int rc = check_device()) return rc;
@@ -863,6 +877,7 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   ChainParams cp{};
   cp.state_in = initial_state;
   cp.state_out = final_state;
+  cp.checkpoints = checkpoints;
   cp.out = static_cast<__nv_bfloat16*>(out);
   cp.cu_seqlens = cu_seqlens_dev;
   cp.chunk_base = chunk_base_dev;

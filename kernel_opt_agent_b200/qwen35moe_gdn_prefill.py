@@ -26,6 +26,11 @@ Extensions over the reference module:
   first, ``x / sqrt(sum x^2 + 1e-6)`` in fp32 (``l2norm_rows``), as the workloads' generators do
   before calling the reference; the result is the kernels' bf16 operand, so with fp32 inputs the
   normalisation replaces the conversion pass.
+* ``checkpoints`` (keyword, default False): also return the state after every 64-token chunk
+  as a third output -- [B, ceil(T/64), Hv, 128, 128] fp32 for a batch, [total_chunks, Hv, 128,
+  128] with cu_seqlens (sequence n's chunks from ``sum(ceil(len_m/64) for m < n)``) -- for prefix
+  caching or a backward pass; the last chunk's entry equals the final state.  Checkpoints come
+  from the split-family schedules ("split"/"overlap", chosen whatever the unit count).
 * ``mode`` (keyword): "auto" (default), "fused", "split" or "overlap" selects the schedule; the
   environment variable TOKMIX_GDN_MODE overrides "auto".  "auto" picks "fused" when the units
   fill the SMs, else "overlap" when at least 8 SMs are left for the preparation CTAs, else
@@ -131,6 +136,7 @@ def kernel_fn(
     cu_seqlens=None,
     mode: str = "auto",
     qk_l2norm: bool = False,
+    checkpoints: bool = False,
 ) -> list[torch.Tensor]:
     nseq, hk, hv = _validate(q, k, v, g, beta, state, cu_seqlens)
     if scale is None:
@@ -142,7 +148,8 @@ def kernel_fn(
     if cu_seqlens is None and T == 1 and B > 0 and _mode(mode) == "auto":
         from . import qwen35moe_gdn_decode
 
-        return qwen35moe_gdn_decode.kernel_fn(q, k, v, g, beta, state, scale, qk_l2norm=qk_l2norm)
+        res = qwen35moe_gdn_decode.kernel_fn(q, k, v, g, beta, state, scale, qk_l2norm=qk_l2norm)
+        return res + [res[1].unsqueeze(1).clone()] if checkpoints else res
     if cu_seqlens is None:
         lengths = (T,) * B
     else:
@@ -150,6 +157,9 @@ def kernel_fn(
     if total == 0:
         out = torch.empty(v.shape, dtype=io_dtype, device=dev)
         fs = state.to(torch.float32).clone() if state is not None else torch.zeros((nseq, hv, D, D), device=dev)
+        if checkpoints:
+            ck = torch.empty((0, hv, D, D), dtype=torch.float32, device=dev)
+            return [out, fs, ck if cu_seqlens is not None else ck.reshape(B, 0, hv, D, D)]
         return [out, fs]
     cu_t, order_t, cb_t, total_chunks, cb_host = _device_meta(lengths, dev)
     qb = l2norm_rows(q) if qk_l2norm else q.to(torch.bfloat16).contiguous()
@@ -162,7 +172,8 @@ def kernel_fn(
     final_state = torch.empty((nseq, hv, D, D), dtype=torch.float32, device=dev)
     lib = _lib.load()
     word = _lib.status_word(dev)
-    sched = _schedule(mode, nseq * hv, total_chunks, hv, dev)
+    sched = _schedule(mode, nseq * hv, total_chunks, hv, dev, checkpoints)
+    ck = torch.empty((total_chunks, hv, D, D), dtype=torch.float32, device=dev) if checkpoints else None
     with torch.cuda.device(dev):
         if sched != "fused":
             nbytes = int(lib.tokmix_gdn_split_workspace_bytes(total_chunks, hv))
@@ -171,7 +182,7 @@ def kernel_fn(
             rc = lib.tokmix_gdn_prefill_split(
                 qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
                 st.data_ptr() if st is not None else None, out.data_ptr(), final_state.data_ptr(),
-                cu_t.data_ptr(), cb_t.data_ptr(), rec_t.data_ptr() if rec_t is not None else None, nseq, total,
+                ck.data_ptr() if ck is not None else None, cu_t.data_ptr(), cb_t.data_ptr(), rec_t.data_ptr() if rec_t is not None else None, nseq, total,
                 total_chunks, hk, hv, D, D, float(scale), _lib.DTYPE_BF16, ws.data_ptr(), ws.numel(),
                 word.data_ptr(), _lib.stream_ptr(dev))
         else:
@@ -185,6 +196,8 @@ def kernel_fn(
         _lib.raise_on_device_status(word, "qwen35moe_gdn_prefill")
     if io_dtype != torch.bfloat16:
         out = out.to(io_dtype)
+    if ck is not None:
+        return [out, final_state, ck if cu_seqlens is not None else ck.reshape(B, total_chunks // B, hv, D, D)]
     return [out, final_state]
 
 
@@ -226,14 +239,19 @@ def _mode(mode: str) -> str:
     return mode
 
 
-def _schedule(mode: str, units: int, total_chunks: int, hv: int, dev: torch.device) -> str:
+def _schedule(mode: str, units: int, total_chunks: int, hv: int, dev: torch.device,
+              checkpoints: bool = False) -> str:
     """"fused" when one CTA per unit fills the SMs (or the workspace would be too large), else
-    "overlap" when the chains leave at least 8 SMs to the preparation CTAs, else "split"."""
+    "overlap" when the chains leave at least 8 SMs to the preparation CTAs, else "split".  With
+    checkpoints only "split" and "overlap" qualify."""
     mode = _mode(mode)
-    if mode != "auto":
-        return mode
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    if units >= sms or _lib.load().tokmix_gdn_split_workspace_bytes(total_chunks, hv) > _SPLIT_MAX_WORKSPACE:
+    if mode != "auto":
+        if checkpoints and mode == "fused":
+            raise ValueError("checkpoints need the split or overlap schedule (mode='fused' given)")
+        return mode
+    if not checkpoints and (units >= sms or
+                            _lib.load().tokmix_gdn_split_workspace_bytes(total_chunks, hv) > _SPLIT_MAX_WORKSPACE):
         return "fused"
     return "overlap" if units + 8 <= sms else "split"
 

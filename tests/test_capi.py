@@ -100,23 +100,23 @@ def test_gdn_split_rejects_bad_arguments():
     need = lib.tokmix_gdn_split_workspace_bytes(32, 32)
     assert need >= 32 * 32 * 4 * 1024 and need % 16 == 0  # records plus one flag word per record
     assert lib.tokmix_gdn_split_workspace_bytes(-1, 32) == -1
-    # q k v g beta state out final cu chunk_base order nseq tokens chunks hk hv dk dv scale io ws ws_bytes status
-    # stream
-    args = [p, p, p, p, p, None, p, p, p, p, None, 1, 2048, 32, 16, 32, 128, 128, 0.08, 0, p, need, p, None]
+    # q k v g beta state out final checkpoints cu chunk_base order nseq tokens chunks hk hv dk dv scale io ws ws_bytes
+    # status stream
+    args = [p, p, p, p, p, None, p, p, None, p, p, None, 1, 2048, 32, 16, 32, 128, 128, 0.08, 0, p, need, p, None]
     bad = list(args)
-    bad[9] = None  # chunk_base
+    bad[10] = None  # chunk_base
     assert lib.tokmix_gdn_prefill_split(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "null" in _lib.last_error()
     bad = list(args)
-    bad[21] = need - 16  # workspace too small
+    bad[22] = need - 16  # workspace too small
     assert lib.tokmix_gdn_prefill_split(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "workspace" in _lib.last_error()
     bad = list(args)
-    bad[16] = 64  # head dim
+    bad[17] = 64  # head dim
     assert lib.tokmix_gdn_prefill_split(*bad) == _lib.TOKMIX_ERR_UNSUPPORTED
     bad = list(args)
-    bad[19] = 1  # fp32 io
+    bad[20] = 1  # fp32 io
     assert lib.tokmix_gdn_prefill_split(*bad) == _lib.TOKMIX_ERR_UNSUPPORTED
     bad = list(args)
-    bad[11] = 0  # no sequences: no-op
+    bad[12] = 0  # no sequences: no-op
     assert lib.tokmix_gdn_prefill_split(*bad) == _lib.TOKMIX_OK
 
 

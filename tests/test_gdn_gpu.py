@@ -224,3 +224,50 @@ def test_l2norm_rows_kernel(cuda_device):
         np.testing.assert_allclose(_np(y), ref, atol=4e-3, rtol=8e-3)
     assert gdn.l2norm_rows(torch.zeros(0, 128, device=cuda_device)).shape == (0, 128)
 
+
+
+@pytest.mark.parametrize("mode", ["auto", "split", "overlap"])
+def test_gdn_checkpoints_match_prefix_oracle(cuda_device, oracle_threads, mode):
+    """checkpoints[:, c] = the state after tokens [0, 64 (c+1)): the recurrence on that prefix."""
+    inp = gcfg.random_inputs(2, 200, seed=21, state_std=0.02, hk=2, hv=4)
+    out, fs, ck = gdn.kernel_fn(**inp, checkpoints=True, mode=mode)
+    assert ck.shape == (2, 4, 4, 128, 128)
+    ref_out, ref_fs = gdn.kernel_fn(**inp, mode=mode)
+    assert torch.equal(out, ref_out) and torch.equal(fs, ref_fs)  # checkpoints change nothing else
+    assert torch.equal(ck[:, -1], fs)
+    for c in range(4):
+        t_end = min(64 * (c + 1), 200)
+        prefix = {n: (x[:, :t_end] if n in ("q", "k", "v", "g", "beta") else x) for n, x in inp.items()}
+        _, s_ref = _oracle(prefix, oracle_threads)
+        np.testing.assert_allclose(_np(ck[:, c]), s_ref, **STATE_TOL, err_msg=f"chunk {c}")
+
+
+def test_gdn_checkpoints_varlen(cuda_device, oracle_threads):
+    lengths = [1, 63, 64, 65, 200, 0, 129]
+    inp = gcfg.random_inputs(1, 0, lengths=lengths, seed=6, state_std=0.02, hk=2, hv=4)
+    out, fs, ck = gdn.kernel_fn(**inp, checkpoints=True)
+    nch = [(n + 63) // 64 for n in lengths]
+    assert ck.shape == (sum(nch), 4, 128, 128)
+    cu = [0]
+    for n in lengths:
+        cu.append(cu[-1] + n)
+    base = 0
+    for s, n in enumerate(lengths):
+        for c in range(nch[s]):
+            t_end = cu[s] + min(64 * (c + 1), n)
+            one = {"q": inp["q"][:, cu[s]:t_end], "k": inp["k"][:, cu[s]:t_end], "v": inp["v"][:, cu[s]:t_end],
+                   "g": inp["g"][:, cu[s]:t_end], "beta": inp["beta"][:, cu[s]:t_end],
+                   "state": inp["state"][s:s + 1], "scale": inp["scale"]}
+            _, s_ref = _oracle(one, oracle_threads)
+            np.testing.assert_allclose(_np(ck[base + c]), s_ref[0], **STATE_TOL, err_msg=f"seq {s} chunk {c}")
+        if nch[s]:
+            assert torch.equal(ck[base + nch[s] - 1], fs[s])
+        base += nch[s]
+
+
+def test_gdn_checkpoints_single_token_and_fused_refusal(cuda_device):
+    inp = gcfg.random_inputs(3, 1, seed=2, state_std=0.02)
+    out, fs, ck = gdn.kernel_fn(**inp, checkpoints=True)
+    assert ck.shape == (3, 1, 32, 128, 128) and torch.equal(ck[:, 0], fs)
+    with pytest.raises(ValueError):
+        gdn.kernel_fn(**gcfg.random_inputs(1, 100, seed=2), checkpoints=True, mode="fused")
