@@ -157,6 +157,14 @@ int tokmix_gdn_decode(const void* q, const void* k, const void* v, const float* 
  * (kernels/qwen35moe_gdn_prefill.py:107-136 takes normalised q and k). */
 int tokmix_l2norm_rows(const void* x, int x_dtype, void* y, long long rows, int dim, float eps, void* stream);
 
+/* The Qwen3.5 gated-delta-net gates from the raw projections (the GDN gates option):
+ *   g = -exp(a_log[h]) * softplus(a + dt_bias[h]),  beta = sigmoid(b)      (fp32 arithmetic)
+ * a, b: [tokens, heads_v] bf16 (ab_dtype TOKMIX_DTYPE_BF16) or fp32; a_log, dt_bias: [heads_v] fp32;
+ * g, beta: [tokens, heads_v] fp32 outputs.  The reference takes g and beta ready-made
+ * (kernels/qwen35moe_gdn_prefill.py:107-136). */
+int tokmix_gdn_gates(const void* a, const void* b, int ab_dtype, const float* a_log, const float* dt_bias, float* g,
+                     float* beta, long long tokens, int heads_v, void* stream);
+
 /* Text of the last error reported on the calling thread ("" if none). */
 const char* tokmix_last_error(void);
 

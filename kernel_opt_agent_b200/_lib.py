@@ -51,6 +51,7 @@ SIGNATURES = {
     "tokmix_gdn_split_workspace_bytes": (ctypes.c_longlong, [_I, _I]),
     "tokmix_gdn_decode": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _F, _I, _VP]),
     "tokmix_l2norm_rows": (_I, [_VP, _I, _VP, ctypes.c_longlong, _I, _F, _VP]),
+    "tokmix_gdn_gates": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, ctypes.c_longlong, _I, _VP]),
     "tokmix_last_error": (ctypes.c_char_p, []),
     "tokmix_version": (ctypes.c_char_p, []),
 }

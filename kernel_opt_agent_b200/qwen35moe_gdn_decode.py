@@ -16,7 +16,8 @@ step its optimised prefill special-cases for one-token chunks
 may be bf16 (native) or fp32 (rounded to bf16 on the device; out is then returned as fp32).
 ``inplace=True`` (keyword) updates ``state`` itself and returns it as final_state: a decode
 loop then moves each state through HBM once per token and allocates nothing for it.
-``qk_l2norm=True`` L2-normalises q and k first, as in ``qwen35moe_gdn_prefill``.
+``qk_l2norm=True`` L2-normalises q and k first and ``gates=(A_log, dt_bias)`` takes raw gate
+projections in place of g and beta, as in ``qwen35moe_gdn_prefill``.
 """
 
 from __future__ import annotations
@@ -24,7 +25,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .qwen35moe_gdn_prefill import D, H_K, H_V, l2norm_rows
+from .qwen35moe_gdn_prefill import D, H_K, H_V, gdn_gates, l2norm_rows
 
 KERNEL_TYPE = "qwen35moe_gdn_decode"
 
@@ -68,8 +69,11 @@ def kernel_fn(
     *,
     inplace: bool = False,
     qk_l2norm: bool = False,
+    gates=None,
 ) -> list[torch.Tensor]:
     batch, hk, hv = _validate(q, k, v, g, beta, state)
+    if gates is not None:
+        g, beta = gdn_gates(g, beta, *gates)
     if scale is None:
         scale = D ** -0.5
     dev = q.device

@@ -26,6 +26,10 @@ Extensions over the reference module:
   first, ``x / sqrt(sum x^2 + 1e-6)`` in fp32 (``l2norm_rows``), as the workloads' generators do
   before calling the reference; the result is the kernels' bf16 operand, so with fp32 inputs the
   normalisation replaces the conversion pass.
+* ``gates`` (keyword, default None): ``(A_log, dt_bias)`` ([Hv] each) to pass the raw gate
+  projections instead of g and beta: the ``g`` and ``beta`` arguments then hold the projections
+  a and b, and ``g = -exp(A_log) * softplus(a + dt_bias)``, ``beta = sigmoid(b)`` are computed on
+  the device first (``gdn_gates``), as Qwen3.5's GDN layer does before its kernel.
 * ``checkpoints`` (keyword, default False): also return the state after every 64-token chunk
   as a third output -- [B, ceil(T/64), Hv, 128, 128] fp32 for a batch, [total_chunks, Hv, 128,
   128] with cu_seqlens (sequence n's chunks from ``sum(ceil(len_m/64) for m < n)``) -- for prefix
@@ -137,8 +141,11 @@ def kernel_fn(
     mode: str = "auto",
     qk_l2norm: bool = False,
     checkpoints: bool = False,
+    gates=None,
 ) -> list[torch.Tensor]:
     nseq, hk, hv = _validate(q, k, v, g, beta, state, cu_seqlens)
+    if gates is not None:
+        g, beta = gdn_gates(g, beta, *gates)
     if scale is None:
         scale = D ** -0.5
     dev = q.device
@@ -199,6 +206,27 @@ def kernel_fn(
     if ck is not None:
         return [out, final_state, ck if cu_seqlens is not None else ck.reshape(B, total_chunks // B, hv, D, D)]
     return [out, final_state]
+
+
+def gdn_gates(a: torch.Tensor, b: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor):
+    """g = -exp(a_log) * softplus(a + dt_bias), beta = sigmoid(b) on the device in fp32
+    (``tokmix_gdn_gates``).  a, b: [..., Hv] bf16 or fp32 CUDA tensors; a_log, dt_bias: [Hv]."""
+    if a.shape != b.shape or a.dtype != b.dtype or a.dtype not in (torch.bfloat16, torch.float32) or not a.is_cuda:
+        raise ValueError("gates: a and b must be CUDA tensors of one shape and dtype (bf16 or fp32)")
+    hv = a.shape[-1]
+    if tuple(a_log.shape) != (hv,) or tuple(dt_bias.shape) != (hv,):
+        raise ValueError(f"gates: A_log and dt_bias must have shape [{hv}]")
+    a, b = a.contiguous(), b.contiguous()
+    al = a_log.to(device=a.device, dtype=torch.float32).contiguous()
+    db = dt_bias.to(device=a.device, dtype=torch.float32).contiguous()
+    g = torch.empty(a.shape, dtype=torch.float32, device=a.device)
+    beta = torch.empty(a.shape, dtype=torch.float32, device=a.device)
+    with torch.cuda.device(a.device):
+        rc = _lib.load().tokmix_gdn_gates(
+            a.data_ptr(), b.data_ptr(), _lib.DTYPE_BF16 if a.dtype == torch.bfloat16 else _lib.DTYPE_FP32, al.data_ptr(),
+            db.data_ptr(), g.data_ptr(), beta.data_ptr(), a.numel() // hv, hv, _lib.stream_ptr(a.device))
+    _lib.check(rc, "gdn_gates")
+    return g, beta
 
 
 def l2norm_rows(x: torch.Tensor, eps: float = QK_L2NORM_EPS) -> torch.Tensor:

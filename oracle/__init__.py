@@ -108,6 +108,18 @@ def l2norm_rows(x, eps: float = 1e-6) -> np.ndarray:
     return (x / np.sqrt((x * x).sum(axis=-1, keepdims=True, dtype=np.float32) + np.float32(eps))).astype(np.float32)
 
 
+def gdn_gates(a, b, a_log, dt_bias):
+    """The Qwen3.5 gated-delta-net gates from the raw projections, in fp32:
+    g = -exp(A_log) * softplus(a + dt_bias), beta = sigmoid(b) (A_log, dt_bias per value head, the
+    last axis); restated for the ``gates`` option (the reference takes g and beta ready-made)."""
+    a, b = _f32(a), _f32(b)
+    x = a + _f32(dt_bias)
+    sp = np.where(x > 20.0, x, np.log1p(np.exp(np.minimum(x, 20.0)))).astype(np.float32)
+    g = (-np.exp(_f32(a_log)) * sp).astype(np.float32)
+    beta = (1.0 / (1.0 + np.exp(-b))).astype(np.float32)
+    return g, beta
+
+
 def gdn_recurrent_numpy(q, k, v, g, beta, state=None, scale=None):
     """Row-vectorised numpy transcription of ``kernels/qwen35moe_gdn_prefill.cu:55-99`` (batched
     layout only; small cases).  fp32 throughout."""

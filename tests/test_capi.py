@@ -155,3 +155,12 @@ def test_l2norm_rows_rejects_bad_arguments():
     assert lib.tokmix_l2norm_rows(p, 0, p, 10, 128, -1.0, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
     assert lib.tokmix_l2norm_rows(p, 0, p, 0, 128, 1e-6, None) == _lib.TOKMIX_OK  # nothing to do
 
+
+def test_gdn_gates_rejects_bad_arguments():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    assert lib.tokmix_gdn_gates(p, p, 1, p, p, p, p, 10, 0, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT  # heads
+    assert lib.tokmix_gdn_gates(p, p, 5, p, p, p, p, 10, 32, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT  # dtype
+    assert lib.tokmix_gdn_gates(p, p, 1, None, p, p, p, 10, 32, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert lib.tokmix_gdn_gates(p, p, 1, p, p, p, p, 0, 32, None) == _lib.TOKMIX_OK  # nothing to do
+

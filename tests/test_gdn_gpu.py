@@ -271,3 +271,34 @@ def test_gdn_checkpoints_single_token_and_fused_refusal(cuda_device):
     assert ck.shape == (3, 1, 32, 128, 128) and torch.equal(ck[:, 0], fs)
     with pytest.raises(ValueError):
         gdn.kernel_fn(**gcfg.random_inputs(1, 100, seed=2), checkpoints=True, mode="fused")
+
+
+def _raw_gates(shape, hv, seed, dtype=torch.float32):
+    gen = torch.Generator().manual_seed(seed)
+    a = (torch.randn(shape, generator=gen) * 2.0).to(dtype).cuda()
+    b = (torch.randn(shape, generator=gen) * 2.0).to(dtype).cuda()
+    a_log = torch.randn(hv, generator=gen) * 0.5
+    dt_bias = torch.randn(hv, generator=gen) * 0.5
+    return a, b, a_log, dt_bias
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gdn_gates_kernel_matches_oracle(cuda_device, dtype):
+    a, b, a_log, dt_bias = _raw_gates((3, 70, 32), 32, seed=5, dtype=dtype)
+    a[0, 0, 0] = 60.0  # the large-argument branch of softplus
+    g, beta = gdn.gdn_gates(a, b, a_log, dt_bias)
+    g_ref, b_ref = oracle.gdn_gates(_np(a), _np(b), a_log.numpy(), dt_bias.numpy())
+    np.testing.assert_allclose(_np(g), g_ref, rtol=2e-6, atol=1e-7)
+    np.testing.assert_allclose(_np(beta), b_ref, rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("t", [150, 1])
+def test_gdn_with_raw_gates_matches_oracle(cuda_device, oracle_threads, t):
+    """gates=(A_log, dt_bias): g, beta arguments are the raw projections (t=1 runs the decode kernel)."""
+    inp = gcfg.random_inputs(2, t, seed=12 + t, state_std=0.02, hk=4, hv=8)
+    a, b, a_log, dt_bias = _raw_gates(inp["g"].shape, 8, seed=13)
+    out, fs = gdn.kernel_fn(**{**inp, "g": a, "beta": b}, gates=(a_log, dt_bias))
+    g_ref, b_ref = oracle.gdn_gates(_np(a), _np(b), a_log.numpy(), dt_bias.numpy())
+    o_ref, s_ref = _oracle({**inp, "g": torch.from_numpy(g_ref), "beta": torch.from_numpy(b_ref)}, oracle_threads)
+    np.testing.assert_allclose(_np(out), o_ref, **OUT_TOL)
+    np.testing.assert_allclose(_np(fs), s_ref.reshape(fs.shape), **STATE_TOL)

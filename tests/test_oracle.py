@@ -126,3 +126,11 @@ def test_l2norm_rows_oracle_unit_rows():
     y = oracle.l2norm_rows(x)
     np.testing.assert_allclose(np.linalg.norm(y, axis=-1), 1.0, rtol=1e-5)
     np.testing.assert_allclose(oracle.l2norm_rows(np.zeros((2, 128), np.float32)), 0.0)
+
+
+def test_gdn_gates_oracle_formula():
+    a = np.array([[0.0, 30.0, -30.0]], np.float32)
+    b = np.array([[0.0, 5.0, -5.0]], np.float32)
+    g, beta = oracle.gdn_gates(a, b, np.zeros(3, np.float32), np.zeros(3, np.float32))
+    np.testing.assert_allclose(g, [[-np.log(2.0), -30.0, -np.log1p(np.exp(-30.0))]], rtol=1e-6)
+    np.testing.assert_allclose(beta, [[0.5, 1 / (1 + np.exp(-5.0)), 1 / (1 + np.exp(5.0))]], rtol=1e-6)
