@@ -10,7 +10,11 @@ Workloads (synthetic data from fixed seeds, shapes of the B200 configs):
                  8 key/value heads (with their 4 query heads each) are split across ranks.
   gdn_varlen     GDN prefill, 8 sequences of U[1024, 32768] tokens packed with cu_seqlens,
                  per-sequence initial state N(0, 0.02).  Strong scaling over head groups.
-The headline line also carries the other two workloads under "also" (same run, same timing rules).
+  gdn_decode_b128  one GDN decode token for 128 sequences, states updated in place.
+The headline line also carries the other workloads under "also" (same run, same timing rules), and
+on one GPU the three row-wise plugin ops (rms_norm M=16384 N=5120 bf16; swiglu_input_quant
+M=4096 N=7168; qkv_part_rope B=50 S=2048 12 heads of 256, nope 192) in GB/s of the bytes their
+configs count.
 
 Timing: W untimed warm-up steps, then K timed steps bracketed by a barrier and
 torch.cuda.synchronize(); each step is timed with CUDA events on the launching stream and the
@@ -40,7 +44,11 @@ sys.path.insert(0, ROOT)
 from kernel_opt_agent_b200 import flash_attention_2 as fa2  # noqa: E402
 from kernel_opt_agent_b200 import qwen35moe_gdn_decode as gdn_dec  # noqa: E402
 from kernel_opt_agent_b200 import qwen35moe_gdn_prefill as gdn  # noqa: E402
+from kernel_opt_agent_b200 import qkv_part_rope as rope_op  # noqa: E402
+from kernel_opt_agent_b200 import rms_norm as rms_op  # noqa: E402
 from kernel_opt_agent_b200 import sharding  # noqa: E402
+from kernel_opt_agent_b200 import swiglu_input_quant as swiglu_op  # noqa: E402
+from kernel_opt_agent_b200.kernel_configs import KERNEL_CONFIGS  # noqa: E402
 
 L2_BYTES = 126 * 1024 * 1024
 D = 128
@@ -266,6 +274,33 @@ def run_gdn_decode(device, rank, world, steps, warmup, batch=128):
                        "l2": "flushed between timed steps (256 MB write)", "shard": f"sequences {local}/rank"}}
 
 
+# the row-wise plugin ops: (module, config name, size, dtype, kernel symbol)
+ROW_OPS = {
+    "rms_norm_m16384_n5120": (rms_op, "rms_norm", {"M": 16384, "N": 5120}, torch.bfloat16,
+                              "tokmix::ops::rms_norm_kernel<__nv_bfloat16>"),
+    "swiglu_quant_m4096_n7168": (swiglu_op, "swiglu_input_quant", {"M": 4096, "N": 7168}, torch.bfloat16,
+                                 "tokmix::ops::swiglu_quant_kernel"),
+    "qkv_rope_b50_s2048": (rope_op, "qkv_part_rope", {"batch": 50, "seq_len": 2048, "q_heads": 10, "kv_heads": 1,
+                                                      "head_dim": 256, "nope_dim": 192}, torch.bfloat16,
+                           "tokmix::ops::qkv_part_rope_kernel"),
+}
+
+
+def run_row_op(device, steps, warmup, name):
+    """One call of a row-wise plugin op on its config's inputs; value = the config's byte count
+    (bytes_fn) per second.  L2 is flushed between steps."""
+    mod, cname, size, dtype, kern = ROW_OPS[name]
+    cfg = KERNEL_CONFIGS[cname]
+    inp = cfg["input_generator"](size, dtype, str(device), seed=7)
+    total_s, per = time_steps(lambda: mod.kernel_fn(**inp), steps, warmup, device, flush=True)
+    algo = cfg["bytes_fn"](size, dtype)
+    ms = total_s / steps * 1e3
+    return {"ms": ms, "value": algo / (total_s / steps) / 1e9, "unit": "GB/s", "kernel_ms_local": statistics.mean(per),
+            "algo_bytes": algo, "schedule": "row_op", "kernel": kern,
+            "config": {"workload": name, **size, "dtype": str(dtype).replace("torch.", ""),
+                       "l2": "flushed between timed steps (256 MB write)"}}
+
+
 def run_fa2(device, rank, world, steps, warmup, batch=4, verify=False):
     B, HQ, HKV, S, DD = batch, 32, 8, 8192, 128
     ranges = sharding.even_ranges(HKV, world)
@@ -388,8 +423,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="gdn_b1_t2048",
                     choices=["gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_decode_b128", "gdn_b4_t2048",
-                             "fa2_b1_s8192"],
-                    help="gdn_b4_t2048 / fa2_b1_s8192 are profiling-size cases (inputs just above L2)")
+                             "fa2_b1_s8192"] + list(ROW_OPS),
+                    help="gdn_b4_t2048 / fa2_b1_s8192 are profiling-size cases (inputs just above L2); the "
+                         "row-wise op names time one op alone (one GPU)")
     ap.add_argument("--no-also", action="store_true", help="skip the secondary workloads")
     ap.add_argument("--no-verify", action="store_true",
                     help="with N > 1, skip gathering the sharded outputs to rank 0 for comparison with a one-GPU run")
@@ -416,6 +452,8 @@ def main():
     sampler = ClockSampler(list(range(world))) if rank == 0 else None
     results = {}
     head = args.workload
+    if head in ROW_OPS and world != 1:
+        raise SystemExit("the row-wise op workloads run on one GPU")
     order = [head] + ([w for w in ("gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_decode_b128") if w != head]
                       if not args.no_also else [])
     e2e = None
@@ -434,10 +472,16 @@ def main():
                         verify=not args.no_verify)
         elif w == "gdn_decode_b128":
             r = run_gdn_decode(device, rank, world, steps_w, args.warmup)
+        elif w in ROW_OPS:
+            r = run_row_op(device, steps_w, args.warmup, w)
         else:
             r = run_gdn_varlen(device, rank, world, steps_w, args.warmup, verify=not args.no_verify)
         results[w] = r
         torch.cuda.empty_cache()
+    if world == 1 and not args.no_also:
+        for w in (x for x in ROW_OPS if x != head):
+            results[w] = run_row_op(device, max(5, args.steps // 5), args.warmup, w)
+            torch.cuda.empty_cache()
     clocks = sampler.stop() if sampler else None
 
     cpu = None
@@ -446,7 +490,7 @@ def main():
         cpu = {"value": v, "unit": "Mtok/s", "cores": cores, "kind": "port",
                "sample": f"full decode step, 128 sequences Hk=16 Hv=32, median of 5 runs ({sec:.4f} s each), fp32 "
                          "recurrence (oracle/gdn_recurrent.c, OpenMP)"}
-    elif rank == 0 and world == 1:
+    elif rank == 0 and world == 1 and head not in ROW_OPS:
         v, cores, sec = cpu_gdn_b1()
         cpu = {"value": v, "unit": "Mtok/s", "cores": cores, "kind": "port",
                "sample": f"full B=1 T=2048 Hk=16 Hv=32 workload, median of 3 runs ({sec:.3f} s each), fp32 "
@@ -467,6 +511,8 @@ def main():
             kern = "tokmix::gdn::split::gdn_overlap_kernel"
         elif r.get("schedule") == "decode":
             kern = "tokmix::gdn_decode::gdn_decode_kernel"
+        elif r.get("schedule") == "row_op":
+            kern = r["kernel"]
         else:
             kern = "tokmix::gdn::gdn_prefill_kernel"
         return {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -477,12 +523,13 @@ def main():
     if rank == 0:
         hr = results[head]
         metric = ("FA2 fwd TFLOPS" if head.startswith("fa2") else
-                  "GDN decode Mtok/s" if head == "gdn_decode_b128" else HEADLINE_METRIC)
+                  "GDN decode Mtok/s" if head == "gdn_decode_b128" else
+                  f"{ROW_OPS[head][1]} GB/s" if head in ROW_OPS else HEADLINE_METRIC)
         cfg = hr["config"]
         line = {"metric": metric, "value": hr["value"], "unit": hr["unit"], "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": hr["ms"], "higher_is_better": True,
                 "scaling": "weak" if head in ("gdn_b1_t2048", "gdn_b4_t2048") else "strong", "vs_baseline": None,
-                "dtype": "bf16" if head.startswith("fa2") else "bf16 in / fp32 state",
+                "dtype": "bf16" if head.startswith("fa2") or head in ROW_OPS else "bf16 in / fp32 state",
                 "data": "synthetic (seeded, B200 config shapes)", "config": cfg,
                 "roofline": roofline(head, hr), "cpu_baseline": cpu,
                 "e2e": e2e if e2e is not None else None,

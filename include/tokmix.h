@@ -52,6 +52,7 @@ extern "C" {
 /* element types */
 #define TOKMIX_DTYPE_BF16 0
 #define TOKMIX_DTYPE_FP32 1
+#define TOKMIX_DTYPE_FP16 2
 
 /* Causal / non-causal attention forward, bf16 in and out, fp32 softmax and accumulation.
  *
@@ -164,6 +165,28 @@ int tokmix_l2norm_rows(const void* x, int x_dtype, void* y, long long rows, int 
  * (kernels/qwen35moe_gdn_prefill.py:107-136). */
 int tokmix_gdn_gates(const void* a, const void* b, int ab_dtype, const float* a_log, const float* dt_bias, float* g,
                      float* beta, long long tokens, int heads_v, void* stream);
+
+/* ---- the harness's other registered row-wise ops (HBM-bound; no counterpart kernels in the
+ * reference, whose configs check them against references/<op>.py) ---- */
+
+/* RMS norm (references/rms_norm.py:6-10): out = x / sqrt(mean(x^2) + eps) * weight, fp32 arithmetic.
+ * x, out: [rows, n]; weight: [n]; dtype TOKMIX_DTYPE_BF16 or TOKMIX_DTYPE_FP16; n a multiple of 8. */
+int tokmix_rms_norm(const void* x, const void* weight, void* out, int rows, int n, int dtype, float eps,
+                    void* stream);
+
+/* SwiGLU with FP8 input quantisation (references/swiglu_input_quant.py:6-30).  x: [m, 2n] bf16 = [x0 | x1];
+ * out: [m, n] bf16 = bf16(x0 * x1 * sigmoid(x1)) (fp32 arithmetic); x_fp8: [m, 2n] e4m3 =
+ * e4m3(bf16(x * bf16(1 / scale))) with scale = max(amax |block|, eps) / 448 per 128-column block;
+ * x_scale: [2n / 128, m] fp32.  n must be a multiple of 128. */
+int tokmix_swiglu_input_quant(const void* x, void* out, void* x_fp8, float* x_scale, int m, int n, float eps,
+                              void* stream);
+
+/* Partial rotary embedding of packed QKV (references/qkv_part_rope.py:6-45).  qkv, out: [batch, seq, heads,
+ * head_dim] bf16; cos, sin: [seq, (head_dim - nope_dim) / 2] fp32.  out = qkv with the last head_dim - nope_dim
+ * columns of the first q_heads + kv_heads heads rotated: (x0, x1) -> (x0 cos - x1 sin, x0 sin + x1 cos) over
+ * the column pairs (j, j + half); negative_sin != 0 negates sin.  head_dim, nope_dim multiples of 8. */
+int tokmix_qkv_part_rope(const void* qkv, const float* cos, const float* sin, void* out, int batch, int seq, int heads,
+                         int head_dim, int q_heads, int kv_heads, int nope_dim, int negative_sin, void* stream);
 
 /* Text of the last error reported on the calling thread ("" if none). */
 const char* tokmix_last_error(void);

@@ -28,6 +28,7 @@ LAYOUT_BHSD = 0
 LAYOUT_BSHD = 1
 DTYPE_BF16 = 0
 DTYPE_FP32 = 1
+DTYPE_FP16 = 2
 
 DEV_STATUS_BITS = {
     0x1: "a TMA load never completed",
@@ -52,6 +53,9 @@ SIGNATURES = {
     "tokmix_gdn_decode": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _F, _I, _VP]),
     "tokmix_l2norm_rows": (_I, [_VP, _I, _VP, ctypes.c_longlong, _I, _F, _VP]),
     "tokmix_gdn_gates": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, ctypes.c_longlong, _I, _VP]),
+    "tokmix_rms_norm": (_I, [_VP, _VP, _VP, _I, _I, _I, _F, _VP]),
+    "tokmix_swiglu_input_quant": (_I, [_VP, _VP, _VP, _VP, _I, _I, _F, _VP]),
+    "tokmix_qkv_part_rope": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _VP]),
     "tokmix_last_error": (ctypes.c_char_p, []),
     "tokmix_version": (ctypes.c_char_p, []),
 }

@@ -1,4 +1,4 @@
-"""Config registry for the two token-mixer plugins -- same mechanism and schema as the
+"""Config registry for the plugins -- same mechanism and schema as the
 reference's ``kernel_configs/__init__.py:60-111``: every ``<name>.toml`` in this directory is
 parsed and merged with the callables of its companion ``<name>.py`` (``input_generator``,
 ``reference_fn``, ``flops_fn``, ``bytes_fn`` and the optional ``numerical_stability_cases``,

@@ -164,3 +164,48 @@ def test_gdn_gates_rejects_bad_arguments():
     assert lib.tokmix_gdn_gates(p, p, 1, None, p, p, p, 10, 32, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
     assert lib.tokmix_gdn_gates(p, p, 1, p, p, p, p, 0, 32, None) == _lib.TOKMIX_OK  # nothing to do
 
+
+
+def test_rms_norm_rejects_bad_arguments():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    bf16, fp16 = _lib.DTYPE_BF16, _lib.DTYPE_FP16
+    assert lib.tokmix_rms_norm(p, p, p, 10, 100, bf16, 1e-6, None) == _lib.TOKMIX_ERR_UNSUPPORTED  # n % 8
+    assert lib.tokmix_rms_norm(p, p, p, 10, 128, 1, 1e-6, None) == _lib.TOKMIX_ERR_UNSUPPORTED  # fp32
+    assert lib.tokmix_rms_norm(p, p, p, -1, 128, bf16, 1e-6, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert lib.tokmix_rms_norm(p, p, p, 10, 128, fp16, -1.0, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert lib.tokmix_rms_norm(p, None, p, 10, 128, bf16, 1e-6, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert lib.tokmix_rms_norm(p, p, ctypes.c_void_p(24), 10, 128, bf16, 1e-6, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert lib.tokmix_rms_norm(p, p, p, 0, 128, bf16, 1e-6, None) == _lib.TOKMIX_OK  # nothing to do
+
+
+def test_swiglu_input_quant_rejects_bad_arguments():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    assert lib.tokmix_swiglu_input_quant(p, p, p, p, 4, 96, 1e-15, None) == _lib.TOKMIX_ERR_UNSUPPORTED  # n % 128
+    assert lib.tokmix_swiglu_input_quant(p, p, p, p, -1, 128, 1e-15, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert lib.tokmix_swiglu_input_quant(p, p, p, p, 4, 128, 0.0, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT  # eps
+    assert lib.tokmix_swiglu_input_quant(p, p, None, p, 4, 128, 1e-15, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert lib.tokmix_swiglu_input_quant(p, p, p, p, 0, 128, 1e-15, None) == _lib.TOKMIX_OK
+
+
+def test_qkv_part_rope_rejects_bad_arguments():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    ok = [p, p, p, p, 1, 16, 12, 256, 10, 1, 192, 0, None]
+
+    def call(**changes):
+        args = list(ok)
+        names = ["qkv", "cos", "sin", "out", "batch", "seq", "heads", "head_dim", "q_heads", "kv_heads", "nope_dim",
+                 "negative_sin", "stream"]
+        for key, val in changes.items():
+            args[names.index(key)] = val
+        return lib.tokmix_qkv_part_rope(*args)
+
+    assert call(q_heads=12) == _lib.TOKMIX_ERR_INVALID_ARGUMENT  # q_heads + kv_heads > heads
+    assert call(nope_dim=196) == _lib.TOKMIX_ERR_UNSUPPORTED
+    assert call(nope_dim=264) == _lib.TOKMIX_ERR_UNSUPPORTED  # nope_dim > head_dim
+    assert call(batch=-1) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert call(sin=None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert call(out=ctypes.c_void_p(24)) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    assert call(seq=0) == _lib.TOKMIX_OK
