@@ -83,7 +83,7 @@ def test_swiglu_quant_bytes_exact(cuda_device, m, n):
     x = torch.randn(m, 2 * n, generator=gen).to(torch.bfloat16).to(cuda_device)
     out, x_fp8, x_scale = swq.kernel_fn(x)
     r_out, r_fp8, r_scale = references.swiglu_input_quant_ref(x)
-    assert torch.equal(x_scale, r_scale)                                       # same fp32 division
+    assert torch.equal(x_scale, r_scale)                                       # same rounding of amax / 448
     assert torch.equal(x_fp8.view(torch.uint8), r_fp8.view(torch.uint8))       # same bf16 product, same rounding
     torch.testing.assert_close(out.float(), r_out.float(), **ULP[torch.bfloat16])
 
@@ -121,6 +121,8 @@ def test_swiglu_quant_rejects_bad_inputs(cuda_device):
     (3, 17, 4, 2, 128, 64, False),
     (1, 5, 8, 0, 64, 0, False),          # full rotation, no key heads
     (2, 9, 2, 2, 96, 96, False),         # nothing rotated: a copy
+    (2, 7, 3, 1, 320, 256, False),       # head_dim above 256: the per-row kernel
+    (1, 11, 5, 3, 64, 40, True),         # rope half of 12 columns: the per-row kernel
 ])
 def test_qkv_rope_matches_reference(cuda_device, b, s, qh, kvh, d, nope, neg):
     inp = rope.get_inputs(batch=b, seq_len=s, q_heads=qh, kv_heads=kvh, head_dim=d, nope_dim=nope,
@@ -131,7 +133,7 @@ def test_qkv_rope_matches_reference(cuda_device, b, s, qh, kvh, d, nope, neg):
     nrot = qh + kvh
     assert torch.equal(out[:, :, nrot:], inp["qkv"][:, :, nrot:])           # value heads pass through
     assert torch.equal(out[..., :nope], inp["qkv"][..., :nope])             # nope columns pass through
-    torch.testing.assert_close(out.float(), ref.float(), **ULP[torch.bfloat16])
+    assert torch.equal(out, ref)    # products and sums rounded one by one, as the checker's tensor ops
 
 
 def test_qkv_rope_three_dim_input(cuda_device):
@@ -140,7 +142,7 @@ def test_qkv_rope_three_dim_input(cuda_device):
     out = rope.kernel_fn(**inp)
     ref = references.qkv_part_rope_ref(**inp)
     assert out.shape == ref.shape == (1, 64, 12, 256)
-    torch.testing.assert_close(out.float(), ref.float(), **ULP[torch.bfloat16])
+    assert torch.equal(out, ref)
 
 
 def test_qkv_rope_rejects_bad_inputs(cuda_device):
