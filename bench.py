@@ -63,6 +63,9 @@ NCU_TRAFFIC_BYTES = {
     "gdn_b1_t2048/fused": 36_302_848 + 54_016,
     "fa2_b4_s8192/fused": 4 * (101_431_808 + 32_353_792),
     "gdn_decode_b128/decode": 270_583_808 + 210_555_648,
+    "rms_norm_m16384_n5120/row_op": 167_820_032 + 111_249_664,
+    "swiglu_quant_m4096_n7168/row_op": 117_455_360 + 68_852_992,
+    "qkv_rope_b50_s2048/row_op": 629_694_464 + 579_417_344,
 }
 
 
