@@ -120,7 +120,7 @@ struct ChainParams {
   uint32_t* status;
 };
 
-// bulk copy global -> shared, completing on an mbarrier (no multicast)
+// bulk copy global -> shared, completing on an mbarrier (one destination CTA)
 __device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    smem_u32(sdst)),

@@ -150,7 +150,7 @@ __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
 }
 
 // ------------------------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA (every load has one destination CTA)
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
