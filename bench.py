@@ -217,7 +217,7 @@ def run_gdn_batch(device, rank, world, steps, warmup, batch=1):
     ms = total_s / steps * 1e3
     return {"tokens_per_step": tokens, "ms": ms, "value": tokens * steps / total_s / 1e6, "unit": "Mtok/s",
             "kernel_ms_local": statistics.mean(per), "algo_bytes": algo, "inp": inp,
-            "schedule": gdn.schedule(inp["q"], inp["v"])}
+            "token_heads": 2048 * batch * HV, "schedule": gdn.schedule(inp["q"], inp["v"])}
 
 
 def headline_config(world: int) -> dict:
@@ -227,6 +227,11 @@ def headline_config(world: int) -> dict:
 
 
 HEADLINE_METRIC = "GDN prefill Mtok/s"
+SPEC_HBM_GBS = 8000.0       # nominal HBM3e bandwidth, for context beside the measured copy peak
+SPEC_BF16_TFLOPS = 2250.0   # nominal dense bf16 tensor throughput
+# tensor-core work of the chunked GDN form per token and value head (C = 64, D = 128):
+# 6 D^2 for the state products plus 8 C D for the in-chunk products
+GDN_CHUNKED_FLOP_PER_TOKEN_HEAD = 6 * 128 * 128 + 8 * 64 * 128
 
 
 def run_gdn_varlen(device, rank, world, steps, warmup, verify=False):
@@ -244,7 +249,7 @@ def run_gdn_varlen(device, rank, world, steps, warmup, verify=False):
     algo = gdn.algorithmic_bytes(tokens, len(lengths), hk=b - a, hv=2 * (b - a))
     res = {"tokens_per_step": tokens, "ms": total_s / steps * 1e3, "value": tokens * steps / total_s / 1e6,
            "unit": "Mtok/s", "kernel_ms_local": statistics.mean(per), "algo_bytes": algo,
-           "schedule": gdn.schedule(inp["q"], inp["v"], inp.get("cu_seqlens")),
+           "token_heads": tokens * 2 * (b - a), "schedule": gdn.schedule(inp["q"], inp["v"], inp.get("cu_seqlens")),
            "config": {"workload": "gdn_varlen", "n_seqs": 8, "lengths": lengths, "total_tokens": tokens,
                       "hk": HK, "hv": HV, "head_dim": D, "chunk": 64, "initial_state": "N(0,0.02)",
                       "shard": f"key heads {HK // world}/rank (+ the value heads reading them)"}}
@@ -505,6 +510,7 @@ def main():
             ach = r["local_flops"] / (kms / 1e3) / 1e12
             return {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                     "frac": ach / peaks["bf16_tflops"], "peak_source": peaks["source"] + " burst bf16",
+                    "frac_of_spec": ach / SPEC_BF16_TFLOPS,
                     "traffic": NCU_TRAFFIC_BYTES.get(w + "/fused"), "kernel": "tokmix::fa2::fa2_fwd_kernel<128>",
                     "kernel_ms": kms}
         ach = r["algo_bytes"] / (kms / 1e3) / 1e9
@@ -518,10 +524,18 @@ def main():
             kern = r["kernel"]
         else:
             kern = "tokmix::gdn::gdn_prefill_kernel"
-        return {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+        line = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": ach / peaks["hbm_gbs"], "peak_source": peaks["source"] + " copy bandwidth",
+                "frac_of_spec": ach / SPEC_HBM_GBS,
                 "traffic": NCU_TRAFFIC_BYTES.get(f"{w}/{r.get('schedule', 'fused')}"), "algorithmic_bytes": r["algo_bytes"],
                 "kernel": kern, "kernel_ms": kms, "schedule": r.get("schedule", "fused")}
+        if "token_heads" in r:  # GDN: the tensor-core view of the same launch
+            sec = kms / 1e3
+            chunked = r["token_heads"] * GDN_CHUNKED_FLOP_PER_TOKEN_HEAD / sec / 1e12
+            line["tensor"] = {"chunked_tflops": chunked, "chunked_frac": chunked / peaks["bf16_tflops"],
+                              "flop_per_token_head": GDN_CHUNKED_FLOP_PER_TOKEN_HEAD,
+                              "reference_formula_tflops": r["token_heads"] * 4 * D * D / sec / 1e12}
+        return line
 
     if rank == 0:
         hr = results[head]
