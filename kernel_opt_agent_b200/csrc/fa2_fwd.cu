@@ -286,9 +286,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cc = 0; cc < 128; ++cc)
           if (cc >= lim) s[cc] = -INFINITY;
       }
-      float mx = s[0];
+      float mx;
+      {  // four independent chains of three-input maxima over the 128 columns
+        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-      for (int cc = 1; cc < 128; ++cc) mx = fmaxf(mx, s[cc]);
+        for (int cc = 0; cc < 128; cc += 8) {
+          m0 = max3f(m0, s[cc], s[cc + 1]);
+          m1 = max3f(m1, s[cc + 2], s[cc + 3]);
+          m2 = max3f(m2, s[cc + 4], s[cc + 5]);
+          m3 = max3f(m3, s[cc + 6], s[cc + 7]);
+        }
+        mx = max3f(m0, m1, fmaxf(m2, m3));
+      }
       const float mx_scaled = mx * c;
       // Lazy rescale: a row moves its running max only when it grew by more than 2^8.  The
       // decision is per row, the O read-modify-write is done by the whole warp (alpha = 1 for
@@ -601,9 +610,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cc = 0; cc < 64; ++cc)
           if (cc >= lim) s[cc] = -INFINITY;
       }
-      float mx = s[0];
+      float mx;
+      {  // four independent chains of three-input maxima over the 64 columns
+        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-      for (int cc = 1; cc < 64; ++cc) mx = fmaxf(mx, s[cc]);
+        for (int cc = 0; cc < 64; cc += 8) {
+          m0 = max3f(m0, s[cc], s[cc + 1]);
+          m1 = max3f(m1, s[cc + 2], s[cc + 3]);
+          m2 = max3f(m2, s[cc + 4], s[cc + 5]);
+          m3 = max3f(m3, s[cc + 6], s[cc + 7]);
+        }
+        mx = max3f(m0, m1, fmaxf(m2, m3));
+      }
       const float mx_scaled = mx * c;
       const bool grow = mx_scaled > m + kRescaleThreshold;
       float alpha = 1.0f;

@@ -385,4 +385,11 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Blackwell's three-input maximum (one instruction for two comparisons)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 }  // namespace tokmix
