@@ -433,34 +433,38 @@ int launch(const void* q, const void* k, const void* v, void* o, int batch, int 
 // ---------------------------------------------------------------------------------------------
 // head_dim 256.  Two tiles' S and O (2 x (128 + 256) TMEM columns) do not fit in TMEM, so one CTA
 // takes one 128-row query tile and double-buffers S instead: the tensor core computes S(j+1)
-// while the softmax warps work on S(j).  Keys come in tiles of 64 (K and V 32 KB each, two-stage
-// rings; Q 64 KB: 192 KB of shared memory).  Order of the MMAs: S(0) S(1) | PV(0) S(2) | PV(1)
-// S(3) | ...; S(j+2) overwrites the buffer PV(j) read P(j) from, after PV(j) in issue order.
+// while the softmax warps work on S(j).  Keys come in tiles of 128 (S(j) is one N=128 product
+// per 16-column step of Q, PV(j) a K=128 product), with K(j) and V(j) single-buffered (64 KB
+// each; Q 64 KB: 192 KB of shared memory).  Order of the MMAs: S(0) | S(1) PV(0) | S(2) PV(1) |
+// ...; S(j+1) overwrites the buffer PV(j-1) read P(j-1) from, after PV(j-1) in issue order.  The
+// loads of K(j+1) start once S(j) has completed (while the softmax works on S(j)), those of V(j+1)
+// once PV(j) has completed; one producer lane each, so neither waits behind the other's release.
 // The lazy O rescale of step j needs PV(j-1) complete (it may still accumulate into O): the
 // softmax warps then wait for its commit, which a rescale makes rare.
-// Warps 0-3: softmax (thread = query row); warp 4: TMA; warp 5: TMEM owner and MMA issuer.
-// TMEM columns: S0 [0,64)  S1 [64,128)  O [128,384).
+// Warps 0-3: softmax (thread = query row); warp 4: TMA (lane 0 Q and K, lane 1 V); warp 5: TMEM
+// owner and MMA issuer.  TMEM columns: S0 [0,128)  S1 [128,256)  O [256,512).
 // ---------------------------------------------------------------------------------------------
 namespace d256 {
 
 constexpr int kD = 256;
-constexpr int kBN = 64;                            // keys per kv tile
+constexpr int kBN = 128;                           // keys per kv tile
 constexpr int kThreads = 192;
 constexpr int kWarpTma = 4, kWarpMma = 5;
 constexpr int kQBytes = kBM * kD * 2;              // 64 KB: four boxes of 128 rows x 64 columns
 constexpr int kQBox = kBM * 128;                   // 16 KB
-constexpr int kKVBytes = kBN * kD * 2;             // 32 KB: four boxes of 64 rows x 64 columns
-constexpr int kKVBox = kBN * 128;                  // 8 KB
-constexpr int kQ = 0, kK = kQBytes, kV = kQBytes + 2 * kKVBytes, kBytes = kQBytes + 4 * kKVBytes;
-__device__ __forceinline__ uint32_t col_s(int st) { return st ? 64u : 0u; }  // S buffer st
-constexpr uint32_t kColO = 128;
+constexpr int kKVBytes = kBN * kD * 2;             // 64 KB: four boxes of 128 rows x 64 columns
+constexpr int kKVBox = kBN * 128;                  // 16 KB
+constexpr int kQ = 0, kK = kQBytes, kV = kQBytes + kKVBytes, kBytes = kQBytes + 2 * kKVBytes;
+static_assert(kBytes + 1024 <= 227 * 1024, "d256 shared memory budget");
+__device__ __forceinline__ uint32_t col_s(int st) { return st ? 128u : 0u; }  // S buffer st
+constexpr uint32_t kColO = 256;
 
 __global__ void __launch_bounds__(kThreads, 1)
     fa2_fwd_d256_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar_q, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_s[2], bar_p[2], bar_pv[2];
+  __shared__ uint64_t bar_q, bar_kfull, bar_kempty, bar_vfull, bar_vempty, bar_s[2], bar_p[2], bar_pv[2];
   __shared__ uint64_t bar_o, bar_drain;
   __shared__ uint32_t tmem_base_shared;
 
@@ -482,11 +486,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bar_q, 1);
     mbar_init(&bar_o, 1);
     mbar_init(&bar_drain, 1);
+    mbar_init(&bar_kfull, 1);
+    mbar_init(&bar_kempty, 1);
+    mbar_init(&bar_vfull, 1);
+    mbar_init(&bar_vempty, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar_kfull[i], 1);
-      mbar_init(&bar_kempty[i], 1);
-      mbar_init(&bar_vfull[i], 1);
-      mbar_init(&bar_vempty[i], 1);
       mbar_init(&bar_s[i], 1);
       mbar_init(&bar_p[i], 128);
       mbar_init(&bar_pv[i], 1);
@@ -503,31 +507,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = tmem_base_shared;
 
   if (warp == kWarpTma) {
-    // ------------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------------ TMA producers
+    // K(j) waits for S(j-1) to release the K buffer, V(j) for PV(j-1) (kempty / vempty complete
+    // once per tile, so the release of tile j-1 is phase (j-1) & 1)
     if (lane == 0) {
       tma_prefetch_desc(&map_q);
       tma_prefetch_desc(&map_k);
-      tma_prefetch_desc(&map_v);
       mbar_arrive_expect_tx(&bar_q, kQBytes);
       for (int bx = 0; bx < kD / 64; ++bx) tma_load_4d(smem + kQ + bx * kQBox, &map_q, &bar_q, bx * 64, q0, head, b);
       int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&bar_kempty[st], ((j >> 1) - 1) & 1, p.status, kDevTimeoutPipe)) break;
-        mbar_arrive_expect_tx(&bar_kfull[st], kKVBytes);
+        if (j >= 1 && !mbar_wait(&bar_kempty, (j - 1) & 1, p.status, kDevTimeoutPipe)) break;
+        mbar_arrive_expect_tx(&bar_kfull, kKVBytes);
         for (int bx = 0; bx < kD / 64; ++bx)
-          tma_load_4d(smem + kK + st * kKVBytes + bx * kKVBox, &map_k, &bar_kfull[st], bx * 64, j * kBN, kvh, b);
-        if (j >= 2 && !mbar_wait(&bar_vempty[st], ((j >> 1) - 1) & 1, p.status, kDevTimeoutPipe)) break;
-        mbar_arrive_expect_tx(&bar_vfull[st], kKVBytes);
-        for (int bx = 0; bx < kD / 64; ++bx)
-          tma_load_4d(smem + kV + st * kKVBytes + bx * kKVBox, &map_v, &bar_vfull[st], bx * 64, j * kBN, kvh, b);
+          tma_load_4d(smem + kK + bx * kKVBox, &map_k, &bar_kfull, bx * 64, j * kBN, kvh, b);
         issued = j + 1;
       }
       mbar_drain(&bar_q, 0);
-      for (int j = max(0, issued - 2); j < issued; ++j) {
-        mbar_drain(&bar_kfull[j & 1], (j >> 1) & 1);
-        mbar_drain(&bar_vfull[j & 1], (j >> 1) & 1);
+      if (issued > 0) mbar_drain(&bar_kfull, (issued - 1) & 1);
+    } else if (lane == 1) {
+      tma_prefetch_desc(&map_v);
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        if (j >= 1 && !mbar_wait(&bar_vempty, (j - 1) & 1, p.status, kDevTimeoutPipe)) break;
+        mbar_arrive_expect_tx(&bar_vfull, kKVBytes);
+        for (int bx = 0; bx < kD / 64; ++bx)
+          tma_load_4d(smem + kV + bx * kKVBox, &map_v, &bar_vfull, bx * 64, j * kBN, kvh, b);
+        issued = j + 1;
       }
+      if (issued > 0) mbar_drain(&bar_vfull, (issued - 1) & 1);
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------------ MMA issuer
@@ -535,48 +543,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc_s = make_idesc(kBM, kBN, 1, 0, 0);
       const uint32_t idesc_o = make_idesc(kBM, kD, 1, 0, 1);
       const uint32_t qa = smem_u32(smem + kQ);
-      // S(j) = Q K(j)^T into S buffer j & 1 (K in stage j & 1)
-      auto issue_s = [&](int j) {
-        const uint32_t ka = smem_u32(smem + kK + (j & 1) * kKVBytes);
+      const uint32_t ka = smem_u32(smem + kK);
+      const uint32_t va = smem_u32(smem + kV);
+      // S(j) = Q K(j)^T into S buffer j & 1, once K(j) is in; releases the K buffer
+      auto issue_s = [&](int j) -> bool {
+        if (!mbar_wait(&bar_kfull, j & 1, p.status, kDevTimeoutTma)) return false;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
           umma_bf16_ss(tbase + col_s(j & 1), make_sdesc_sw128(qa + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024),
                        make_sdesc_sw128(ka + (kk >> 2) * kKVBox + (kk & 3) * 32, 16, 1024), idesc_s,
                        kk > 0 ? 1u : 0u);
         umma_commit(&bar_s[j & 1]);
+        umma_commit(&bar_kempty);
+        return true;
       };
-      bool ok = mbar_wait(&bar_q, 0, p.status, kDevTimeoutTma);
-      for (int j = 0; ok && j < min(2, n_kv); ++j) {
-        ok = mbar_wait(&bar_kfull[j], 0, p.status, kDevTimeoutTma);
-        if (ok) {
-          tc_fence_after();
-          issue_s(j);
-          umma_commit(&bar_kempty[j]);
-        }
-      }
+      bool ok = mbar_wait(&bar_q, 0, p.status, kDevTimeoutTma) && (n_kv == 0 || issue_s(0));
       for (int j = 0; ok && j < n_kv; ++j) {
         const int st = j & 1;
-        ok = mbar_wait(&bar_vfull[st], (j >> 1) & 1, p.status, kDevTimeoutTma) &&
+        // S(j+1) first: it runs while the softmax warps work on S(j)
+        if (j + 1 < n_kv && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        ok = mbar_wait(&bar_vfull, j & 1, p.status, kDevTimeoutTma) &&
              mbar_wait(&bar_p[st], (j >> 1) & 1, p.status, kDevTimeoutPipe);
         if (!ok) break;
         tc_fence_after();
         // O (+)= P(j) V(j): P read from TMEM (bf16 over S buffer j & 1), V MN-major in smem
-        const uint32_t va = smem_u32(smem + kV + st * kKVBytes);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
           umma_bf16_ts(tbase + kColO, tbase + col_s(st) + 8 * kk, make_sdesc_sw128(va + kk * 2048, kKVBox, 1024),
                        idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&bar_pv[st]);
-        umma_commit(&bar_vempty[st]);
+        umma_commit(&bar_vempty);
         if (j == n_kv - 1) umma_commit(&bar_o);
-        if (j + 2 < n_kv) {
-          ok = mbar_wait(&bar_kfull[st], ((j + 2) >> 1) & 1, p.status, kDevTimeoutTma);
-          if (ok) {
-            tc_fence_after();
-            issue_s(j + 2);
-            umma_commit(&bar_kempty[st]);
-          }
-        }
       }
       umma_commit(&bar_drain);
       mbar_drain(&bar_drain, 0);
@@ -598,23 +599,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t raw[64];
-      tmem_ld64(lane_base + col_s(st), raw);
-      float s[64];
+      uint32_t raw[128];
+      tmem_ld64(lane_base + col_s(st), *reinterpret_cast<uint32_t(*)[64]>(&raw[0]));
+      tmem_ld64(lane_base + col_s(st) + 64, *reinterpret_cast<uint32_t(*)[64]>(&raw[64]));
+      float s[128];
 #pragma unroll
-      for (int cc = 0; cc < 64; ++cc) s[cc] = __uint_as_float(raw[cc]);
+      for (int cc = 0; cc < 128; ++cc) s[cc] = __uint_as_float(raw[cc]);
       const int kv0 = j * kBN;
       if ((p.causal && kv0 + kBN - 1 > q0) || (kv0 + kBN > p.skv)) {
         const int lim = (p.causal ? min(qrow + 1, p.skv) : p.skv) - kv0;
 #pragma unroll
-        for (int cc = 0; cc < 64; ++cc)
+        for (int cc = 0; cc < 128; ++cc)
           if (cc >= lim) s[cc] = -INFINITY;
       }
       float mx;
-      {  // four independent chains of three-input maxima over the 64 columns
+      {  // four independent chains of three-input maxima over the 128 columns
         float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-        for (int cc = 0; cc < 64; cc += 8) {
+        for (int cc = 0; cc < 128; cc += 8) {
           m0 = max3f(m0, s[cc], s[cc + 1]);
           m1 = max3f(m1, s[cc + 2], s[cc + 3]);
           m2 = max3f(m2, s[cc + 4], s[cc + 5]);
@@ -648,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       l *= alpha;
       float rowsum = 0.0f;
 #pragma unroll
-      for (int chunk = 0; chunk < 2; ++chunk) {
+      for (int chunk = 0; chunk < 4; ++chunk) {
         uint32_t packed[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
