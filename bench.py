@@ -14,7 +14,7 @@ Workloads (synthetic data from fixed seeds, shapes of the B200 configs):
 The headline line also carries the other workloads under "also" (same run, same timing rules), and
 on one GPU the three row-wise plugin ops (rms_norm M=16384 N=5120 bf16; swiglu_input_quant
 M=4096 N=7168; qkv_part_rope B=50 S=2048 12 heads of 256, nope 192) in GB/s of the bytes their
-configs count.
+configs count, and FA2 head_dim 256 (fa2_d256_b16_s4096: causal GQA B=16 Hq=16 Hkv=2 S=4096).
 
 Timing: W untimed warm-up steps, then K timed steps bracketed by a barrier and
 torch.cuda.synchronize(); each step is timed with CUDA events on the launching stream and the
@@ -66,6 +66,9 @@ NCU_TRAFFIC_BYTES = {
     "rms_norm_m16384_n5120/row_op": 167_820_032 + 111_249_664,
     "swiglu_quant_m4096_n7168/row_op": 117_455_360 + 68_852_992,
     "qkv_rope_b50_s2048/row_op": 629_694_464 + 579_417_344,
+    # FA2 head_dim 256: captured at batch 4 (the batch-16 inputs exceed the capture size rule), x4
+    "fa2_d256_b16_s4096/fused": 4 * (169_233_152 + 92_687_872),
+    "fa2_d256_b4_s4096/fused": 169_233_152 + 92_687_872,
 }
 
 
@@ -334,6 +337,26 @@ def run_fa2(device, rank, world, steps, warmup, batch=4, verify=False):
     return res
 
 
+def run_fa2_d256(device, steps, warmup, batch=16):
+    """FA2 head_dim 256, the hybrid configuration's attention: causal GQA B16 Hq16 Hkv2 S4096
+    (batch 4: the profiling-size case, inputs above L2), one GPU (the fa2::d256 kernel)."""
+    B, HQ, HKV, S, DD = batch, 16, 2, 4096, 256
+    inp = fa2_inputs(device, B, HQ, HKV, S, DD, seed=4)
+    flops = fa2.get_flops(B, HQ, S, DD, causal=True)
+    total_s, per = time_steps(lambda: fa2.kernel_fn(**inp), steps, warmup, device,
+                              flush=input_bytes(inp) < L2_BYTES)
+    fa2.check_device_status(device)
+    return {"ms": total_s / steps * 1e3, "value": flops * steps / total_s / 1e12, "unit": "TFLOP/s",
+            "kernel_ms_local": statistics.mean(per), "local_flops": flops,
+            "kernel": "tokmix::fa2::d256::fa2_fwd_d256_kernel",
+            "config": {"workload": f"fa2_d256_b{B}_s4096", "batch": B, "heads_q": HQ, "heads_kv": HKV, "seq_len": S,
+                       "head_dim": DD, "causal": True, "layout": "bhsd"}}
+
+
+# workloads that run on one GPU only (in "also" when the bench runs on one GPU)
+ONE_GPU_WORKLOADS = list(ROW_OPS) + ["fa2_d256_b16_s4096"]
+
+
 def e2e_gdn_b1(device, rank, world, steps, warmup, inp):
     """Headline step through the public plugin call from pinned host memory."""
     host = {k: (v.cpu().pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
@@ -431,8 +454,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="gdn_b1_t2048",
                     choices=["gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_decode_b128", "gdn_b4_t2048",
-                             "fa2_b1_s8192"] + list(ROW_OPS),
-                    help="gdn_b4_t2048 / fa2_b1_s8192 are profiling-size cases (inputs just above L2); the "
+                             "fa2_b1_s8192", "fa2_d256_b4_s4096"] + ONE_GPU_WORKLOADS,
+                    help="gdn_b4_t2048 / fa2_b1_s8192 / fa2_d256_b4_s4096 are profiling-size cases (inputs just above L2); the "
                          "row-wise op names time one op alone (one GPU)")
     ap.add_argument("--no-also", action="store_true", help="skip the secondary workloads")
     ap.add_argument("--no-verify", action="store_true",
@@ -460,8 +483,8 @@ def main():
     sampler = ClockSampler(list(range(world))) if rank == 0 else None
     results = {}
     head = args.workload
-    if head in ROW_OPS and world != 1:
-        raise SystemExit("the row-wise op workloads run on one GPU")
+    if (head in ONE_GPU_WORKLOADS or head == "fa2_d256_b4_s4096") and world != 1:
+        raise SystemExit(f"workload {head} runs on one GPU")
     order = [head] + ([w for w in ("gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_decode_b128") if w != head]
                       if not args.no_also else [])
     e2e = None
@@ -482,13 +505,17 @@ def main():
             r = run_gdn_decode(device, rank, world, steps_w, args.warmup)
         elif w in ROW_OPS:
             r = run_row_op(device, steps_w, args.warmup, w)
+        elif w in ("fa2_d256_b16_s4096", "fa2_d256_b4_s4096"):
+            r = run_fa2_d256(device, steps_w, args.warmup, batch=16 if w == "fa2_d256_b16_s4096" else 4)
         else:
             r = run_gdn_varlen(device, rank, world, steps_w, args.warmup, verify=not args.no_verify)
         results[w] = r
         torch.cuda.empty_cache()
     if world == 1 and not args.no_also:
-        for w in (x for x in ROW_OPS if x != head):
-            results[w] = run_row_op(device, max(5, args.steps // 5), args.warmup, w)
+        for w in (x for x in ONE_GPU_WORKLOADS if x != head):
+            steps_w = max(5, args.steps // 5)
+            results[w] = (run_fa2_d256(device, steps_w, args.warmup) if w == "fa2_d256_b16_s4096"
+                          else run_row_op(device, steps_w, args.warmup, w))
             torch.cuda.empty_cache()
     clocks = sampler.stop() if sampler else None
 
@@ -498,7 +525,7 @@ def main():
         cpu = {"value": v, "unit": "Mtok/s", "cores": cores, "kind": "port",
                "sample": f"full decode step, 128 sequences Hk=16 Hv=32, median of 5 runs ({sec:.4f} s each), fp32 "
                          "recurrence (oracle/gdn_recurrent.c, OpenMP)"}
-    elif rank == 0 and world == 1 and head not in ROW_OPS:
+    elif rank == 0 and world == 1 and head not in ONE_GPU_WORKLOADS and not head.startswith("fa2_d256"):
         v, cores, sec = cpu_gdn_b1()
         cpu = {"value": v, "unit": "Mtok/s", "cores": cores, "kind": "port",
                "sample": f"full B=1 T=2048 Hk=16 Hv=32 workload, median of 3 runs ({sec:.3f} s each), fp32 "
@@ -511,7 +538,8 @@ def main():
             return {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                     "frac": ach / peaks["bf16_tflops"], "peak_source": peaks["source"] + " burst bf16",
                     "frac_of_spec": ach / SPEC_BF16_TFLOPS,
-                    "traffic": NCU_TRAFFIC_BYTES.get(w + "/fused"), "kernel": "tokmix::fa2::fa2_fwd_kernel<128>",
+                    "traffic": NCU_TRAFFIC_BYTES.get(w + "/fused"),
+                    "kernel": r.get("kernel", "tokmix::fa2::fa2_fwd_kernel<128>"),
                     "kernel_ms": kms}
         ach = r["algo_bytes"] / (kms / 1e3) / 1e9
         if r.get("schedule") == "split":  # one step = the preparation launch + the state-chain launch
