@@ -64,7 +64,7 @@ NCU_TRAFFIC_BYTES = {
     "fa2_b4_s8192/fused": 4 * (101_431_808 + 32_353_792),
     "gdn_decode_b128/decode": 270_583_808 + 210_555_648,
     "rms_norm_m16384_n5120/row_op": 167_820_032 + 111_249_664,
-    "swiglu_quant_m4096_n7168/row_op": 117_455_360 + 68_852_992,
+    "swiglu_quant_m4096_n7168/row_op": 117_454_848 + 69_972_480,
     "qkv_rope_b50_s2048/row_op": 629_694_464 + 579_417_344,
     # FA2 head_dim 256: captured at batch 4 (the batch-16 inputs exceed the capture size rule), x4
     "fa2_d256_b16_s4096/fused": 4 * (169_233_152 + 92_687_872),

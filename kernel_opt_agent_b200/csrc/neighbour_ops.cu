@@ -239,7 +239,10 @@ __global__ void __launch_bounds__(128) swiglu_quant_kernel(const __nv_bfloat16* 
 #pragma unroll
   for (int j = 0; j < 8; ++j) {  // x0 * (x1 * sigmoid(x1)), each product rounded to fp32 as the checker's
     const float x1 = __bfloat162float(e1[j]);
-    const float sig = __frcp_rn(1.0f + expf(-x1));  // correctly rounded 1 / (1 + e^-x1)
+    // 1 / (1 + e^-x1) by the fast approximate divide: the correctly rounded reciprocal made the
+    // outputs bit-identical to the checker's but cost 17 % of the kernel's time; with this one an
+    // output differs from the checker's by at most one bf16 ulp (208 of 29.4M at M4096 N7168)
+    const float sig = __fdividef(1.0f, 1.0f + expf(-x1));
     oe[j] = __float2bfloat16_rn(__fmul_rn(__bfloat162float(e0[j]), __fmul_rn(x1, sig)));
   }
   __stcs(reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * n + col), o);
