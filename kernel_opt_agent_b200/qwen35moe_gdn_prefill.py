@@ -57,7 +57,20 @@ D = 128
 H_K = 16
 H_V = 32
 _CHECK_STATUS = os.environ.get("TOKMIX_CHECK_STATUS", "0") == "1"
-_SPLIT_MAX_WORKSPACE = 1 << 30  # bytes; larger problems use the one-launch schedule
+_SPLIT_MAX_WORKSPACE = 8 << 30  # bytes; larger problems use the one-launch schedule
+# Costs measured on a B200 (microseconds), from which "auto" predicts each schedule's time when
+# every unit fits on the SMs at once: a chunk of the fused kernel's chain (preparation inside the
+# CTA; 277 us / 32 chunks at B1 T2048, 2.9 ms / 347 chunks on a varlen slice), a chunk of the chain
+# fed from prepared records (113 us / 32, 1.05 ms / 347, start-up included), one preparation
+# record with three preparation groups per SM (alone, and beside the chains of the overlapped
+# launch: 4096 records on 60 groups took 1.36 ms), the overlapped launch's start-up, and the gap
+# between the split schedule's two launches.
+_US_FUSED_CHUNK = 8.5
+_US_CHAIN_CHUNK = 3.0
+_US_PREP_RECORD = 15.0
+_US_PREP_RECORD_OVERLAP = 20.0
+_US_OVERLAP_START = 20.0
+_US_SPLIT_GAP = 10.0
 QK_L2NORM_EPS = 1e-6
 
 _meta_cache: dict = {}
@@ -179,7 +192,8 @@ def kernel_fn(
     final_state = torch.empty((nseq, hv, D, D), dtype=torch.float32, device=dev)
     lib = _lib.load()
     word = _lib.status_word(dev)
-    sched = _schedule(mode, nseq * hv, total_chunks, hv, dev, checkpoints)
+    sched = _schedule(mode, nseq * hv, total_chunks, hv, dev, checkpoints,
+                      max_chunks=max((n + 63) // 64 for n in lengths))
     ck = torch.empty((total_chunks, hv, D, D), dtype=torch.float32, device=dev) if checkpoints else None
     with torch.cuda.device(dev):
         if sched != "fused":
@@ -267,11 +281,23 @@ def _mode(mode: str) -> str:
     return mode
 
 
+def _predicted_us(sched: str, units: int, records: int, max_chunks: int, sms: int) -> float:
+    """Predicted time of one schedule for `units` chains (all on the SMs at once) whose longest
+    has `max_chunks` chunks, with `records` preparation records in all."""
+    if sched == "fused":
+        return max_chunks * _US_FUSED_CHUNK
+    if sched == "overlap":  # the chains and 3 preparation groups on each remaining SM
+        prep = records * _US_PREP_RECORD_OVERLAP / (3 * (sms - units))
+        return max(max_chunks * _US_CHAIN_CHUNK, prep) + _US_OVERLAP_START
+    return records * _US_PREP_RECORD / (3 * sms) + max_chunks * _US_CHAIN_CHUNK + _US_SPLIT_GAP
+
+
 def _schedule(mode: str, units: int, total_chunks: int, hv: int, dev: torch.device,
-              checkpoints: bool = False) -> str:
-    """"fused" when one CTA per unit fills the SMs (or the workspace would be too large), else
-    "overlap" when the chains leave at least 8 SMs to the preparation CTAs, else "split".  With
-    checkpoints only "split" and "overlap" qualify."""
+              checkpoints: bool = False, max_chunks: int | None = None) -> str:
+    """"fused" when one CTA per unit fills the SMs (or the workspace would be too large);
+    otherwise the schedule with the lowest predicted time (`_predicted_us`) among "fused",
+    "overlap" (possible when the chains leave at least 8 SMs to the preparation CTAs) and "split".
+    With checkpoints only "split" and "overlap" qualify."""
     mode = _mode(mode)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     if mode != "auto":
@@ -281,7 +307,14 @@ def _schedule(mode: str, units: int, total_chunks: int, hv: int, dev: torch.devi
     if not checkpoints and (units >= sms or
                             _lib.load().tokmix_gdn_split_workspace_bytes(total_chunks, hv) > _SPLIT_MAX_WORKSPACE):
         return "fused"
-    return "overlap" if units + 8 <= sms else "split"
+    if units >= sms:
+        return "split"
+    if max_chunks is None:
+        max_chunks = -(-total_chunks // max(1, units // hv))
+    records = total_chunks * hv
+    # ties go to the earlier entry: the single fused launch first
+    cands = ([] if checkpoints else ["fused"]) + (["overlap"] if units + 8 <= sms else []) + ["split"]
+    return min(cands, key=lambda c: _predicted_us(c, units, records, max_chunks, sms))
 
 
 def schedule(q: torch.Tensor, v: torch.Tensor, cu_seqlens=None, mode: str = "auto") -> str:
@@ -291,7 +324,8 @@ def schedule(q: torch.Tensor, v: torch.Tensor, cu_seqlens=None, mode: str = "aut
         return "decode"
     lengths = (T,) * B if cu_seqlens is None else _lengths(cu_seqlens, T)
     chunks = sum((n + 63) // 64 for n in lengths)
-    return _schedule(mode, len(lengths) * hv, chunks, hv, q.device)
+    return _schedule(mode, len(lengths) * hv, chunks, hv, q.device,
+                     max_chunks=max([(n + 63) // 64 for n in lengths] or [0]))
 
 
 def check_device_status(device: torch.device | None = None) -> None:
