@@ -99,13 +99,24 @@ int tokmix_gdn_prefill(const void* q, const void* k, const void* v, const float*
  * [batch, heads_v, 128, 128]; the per-sequence token offsets (and the device status word when
  * `status` is NULL) live in a library-owned device array of about 16 KB per device instead of
  * caller memory.  batch must be <= 4095.  The first call on a device looks up that array's
- * address on the current device; make it before capturing the stream into a CUDA graph.  All
- * calls on a device share the array: calls that may overlap on the GPU (different streams
- * without ordering) race on it.  No counterpart in the reference. */
+ * address on the current device; make it before capturing the stream into a CUDA graph.  The
+ * address is kept for the life of the process: after cudaDeviceReset (or anything else that
+ * replaces the device's primary context) reload the library before calling again.  All calls on
+ * a device share the array: calls that may overlap on the GPU (different streams without
+ * ordering) race on it.  With status == NULL each call clears the library's status word when it
+ * starts and the kernels' timeout bits go there; read it with tokmix_gdn_noalloc_status after
+ * synchronising.  Every argument check runs before anything is enqueued.  No counterpart in the
+ * reference. */
 int tokmix_gdn_prefill_noalloc(const void* q, const void* k, const void* v, const float* g, const float* beta,
                                const float* initial_state, void* out, float* final_state, int batch, int seqlen,
                                int heads_k, int heads_v, int head_dim_k, int head_dim_v, float scale, int io_dtype,
                                uint32_t* status, void* stream);
+
+/* The library-owned status word of the current device that tokmix_gdn_prefill_noalloc writes
+ * when it is called with status == NULL: copied to *host_status synchronously (call it after
+ * synchronising the stream of the prefill), then zeroed if clear != 0.  Allocates nothing.  No
+ * counterpart in the reference. */
+int tokmix_gdn_noalloc_status(uint32_t* host_status, int clear);
 
 /* Gated-delta-rule prefill in two launches, for problems with few (sequence, value head) units
  * (fewer than the GPU has SMs): a chunk-parallel preparation kernel (one CTA per chunk and value
@@ -187,6 +198,19 @@ int tokmix_swiglu_input_quant(const void* x, void* out, void* x_fp8, float* x_sc
  * the column pairs (j, j + half); negative_sin != 0 negates sin.  head_dim, nope_dim multiples of 8. */
 int tokmix_qkv_part_rope(const void* qkv, const float* cos, const float* sin, void* out, int batch, int seq, int heads,
                          int head_dim, int q_heads, int kv_heads, int nope_dim, int negative_sin, void* stream);
+
+/* Self-test of the bounded waits every pipelined kernel relies on: one small kernel waits on an
+ * event that never happens -- which = 0: a transaction barrier whose bytes never land (a TMA load
+ * that never completes; sets TOKMIX_DEV_TIMEOUT_TMA), 1: a hand-off barrier missing an arrival
+ * (TOKMIX_DEV_TIMEOUT_PIPE), 2: the ready flag *flag (device uint32; TOKMIX_DEV_TIMEOUT_PIPE while
+ * it stays 0, success if the caller set it) -- with a limit of limit_ns (1e3 .. 1e9 ns), while a
+ * second warp waits on the same event with the library's own 2 s limit and must stop as soon as
+ * the first gives up.  result (device int32[2] or NULL) receives what each warp's wait returned
+ * (1 satisfied, 0 gave up); *status (device uint32) the bits.  Nothing is in flight in this
+ * kernel, so the run ends cleanly.  The reference's counterpart is host-side only (its bench
+ * harness puts a timeout around each run, tools/bench.py:138-169). */
+int tokmix_selftest_wait_timeout(int which, long long limit_ns, const uint32_t* flag, int32_t* result,
+                                 uint32_t* status, void* stream);
 
 /* Text of the last error reported on the calling thread ("" if none). */
 const char* tokmix_last_error(void);

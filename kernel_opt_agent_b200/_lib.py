@@ -11,6 +11,7 @@ reference's plugin modules report them: bad shapes / dtypes / devices raise ``Va
 from __future__ import annotations
 
 import ctypes
+import os
 import pathlib
 import threading
 
@@ -49,6 +50,7 @@ SIGNATURES = {
                                         _VP]),
     "tokmix_gdn_prefill_split": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I,
                                       _I, _I, _F, _I, _VP, ctypes.c_longlong, _VP, _VP]),
+    "tokmix_gdn_noalloc_status": (_I, [_VP, _I]),
     "tokmix_gdn_split_workspace_bytes": (ctypes.c_longlong, [_I, _I]),
     "tokmix_gdn_decode": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _F, _I, _VP]),
     "tokmix_l2norm_rows": (_I, [_VP, _I, _VP, ctypes.c_longlong, _I, _F, _VP]),
@@ -56,6 +58,7 @@ SIGNATURES = {
     "tokmix_rms_norm": (_I, [_VP, _VP, _VP, _I, _I, _I, _F, _VP]),
     "tokmix_swiglu_input_quant": (_I, [_VP, _VP, _VP, _VP, _I, _I, _F, _VP]),
     "tokmix_qkv_part_rope": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _VP]),
+    "tokmix_selftest_wait_timeout": (_I, [_I, ctypes.c_longlong, _VP, _VP, _VP, _VP]),
     "tokmix_last_error": (ctypes.c_char_p, []),
     "tokmix_version": (ctypes.c_char_p, []),
 }
@@ -114,13 +117,91 @@ def status_word(device: torch.device) -> torch.Tensor:
     return w
 
 
+def _raise_for(val: int, what: str) -> None:
+    reasons = ", ".join(txt for bit, txt in DEV_STATUS_BITS.items() if val & bit) or f"0x{val:x}"
+    raise TokmixDeviceError(f"{what}: device status 0x{val:x} ({reasons})")
+
+
 def raise_on_device_status(word: torch.Tensor, what: str) -> None:
-    """Synchronise-free check helper: reads the status word (this synchronises the stream)."""
+    """Reads the status word (this synchronises the stream) and raises TokmixDeviceError if a
+    kernel set a bit; the word is cleared first."""
     val = int(word.item()) & 0xFFFFFFFF
     if val:
         word.zero_()
-        reasons = ", ".join(txt for bit, txt in DEV_STATUS_BITS.items() if val & bit) or f"0x{val:x}"
-        raise TokmixDeviceError(f"{what}: device status 0x{val:x} ({reasons})")
+        _raise_for(val, what)
+
+
+# How the plugin modules check the device status word after each launch:
+#   "async" (default) -- without a synchronisation: a copy of the word to pinned host memory is
+#                        queued on a side stream behind the launch, and the next call (or
+#                        check_device_status) raises TokmixDeviceError once that copy shows a bit;
+#   "sync"            -- synchronise and check after every call;
+#   "off"             -- only explicit check_device_status calls look at the word.
+# TOKMIX_CHECK_STATUS=1 selects "sync", =0 "off".
+_STATUS_MODE = {"1": "sync", "0": "off"}.get(os.environ.get("TOKMIX_CHECK_STATUS", ""), "async")
+
+
+class _StatusMonitor:
+    """Non-blocking watch of one device's status word (see _STATUS_MODE)."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.side = torch.cuda.Stream(device)
+        self.copied = None  # event recorded after the copy in flight, if any
+        self.what = ""
+
+    def poll(self) -> None:
+        """Raises if the last completed copy shows a bit (and clears the word)."""
+        if self.copied is not None and self.copied.query():
+            self.copied = None
+            val = int(self.host[0]) & 0xFFFFFFFF
+            if val:
+                self.host.zero_()
+                status_word(self.device).zero_()
+                _raise_for(val, self.what)
+
+    def after_launch(self, what: str) -> None:
+        self.poll()
+        if self.copied is not None:
+            return  # one copy in flight at a time; it covers every launch before it
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self.side.wait_event(ev)
+        with torch.cuda.stream(self.side):
+            self.host.copy_(status_word(self.device), non_blocking=True)
+        self.copied = torch.cuda.Event()
+        self.copied.record(self.side)
+        self.what = what
+
+
+_monitors: dict[int, _StatusMonitor] = {}
+
+
+def after_launch(device: torch.device, what: str) -> None:
+    """Status check after a launch that was given status_word(device), per _STATUS_MODE."""
+    if _STATUS_MODE == "off":
+        return
+    if _STATUS_MODE == "sync":
+        raise_on_device_status(status_word(device), what)
+        return
+    if torch.cuda.is_current_stream_capturing():
+        return  # no side-stream work inside a graph capture; check_device_status still works
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    m = _monitors.get(idx)
+    if m is None:
+        m = _monitors[idx] = _StatusMonitor(torch.device("cuda", idx))
+    m.after_launch(what)
+
+
+def check_status(device: torch.device, what: str) -> None:
+    """Synchronise and raise if any kernel given status_word(device) reported a device-side
+    timeout (also drops a pending asynchronous check, which this one covers)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    m = _monitors.get(idx)
+    if m is not None:
+        m.copied = None
+    raise_on_device_status(status_word(torch.device("cuda", idx)), what)
 
 
 def stream_ptr(device: torch.device) -> int:

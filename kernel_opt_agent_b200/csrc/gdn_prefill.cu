@@ -690,6 +690,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace gdn
 }  // namespace tokmix
 
+namespace tokmix {
+namespace gdn {
+
+// Host-side argument checks of tokmix_gdn_prefill that do not depend on the token offsets (shared
+// with the allocation-free entry point, which must reject a call before it touches its array).
+static int validate_prefill_args(const char* who, const void* q, const void* k, const void* v, const float* g,
+                                 const float* beta, const float* initial_state, const void* out,
+                                 const float* final_state, int num_seqs, int total_tokens, int heads_k, int heads_v,
+                                 int head_dim_k, int head_dim_v, float scale, int io_dtype) {
+  if (!q || !k || !v || !g || !beta || !out || !final_state)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: null pointer argument", who);
+  if (num_seqs < 0 || total_tokens < 0 || heads_k <= 0 || heads_v <= 0)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: negative or zero size", who);
+  if (heads_v % heads_k != 0)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: heads_v (%d) must be a multiple of heads_k (%d)", who, heads_v,
+                heads_k);
+  if (head_dim_k != kD || head_dim_v != kD)
+    return fail(TOKMIX_ERR_UNSUPPORTED, "%s: head dims must be 128 (got %d, %d)", who, head_dim_k, head_dim_v);
+  if (io_dtype != TOKMIX_DTYPE_BF16)
+    return fail(TOKMIX_ERR_UNSUPPORTED, "%s: only bf16 q/k/v/out are supported by the kernel", who);
+  if (!std::isfinite(scale)) return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: scale must be finite", who);
+  for (const void* ptr : {q, k, v, out, static_cast<const void*>(initial_state), static_cast<const void*>(final_state)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+      return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: tensors must be 16-byte aligned", who);
+  return TOKMIX_OK;
+}
+
+}  // namespace gdn
+}  // namespace tokmix
+
 extern "C" int tokmix_gdn_prefill(const void* q, const void* k, const void* v, const float* g, const float* beta,
                                   const float* initial_state, void* out, float* final_state,
                                   const int32_t* cu_seqlens_dev, const int32_t* seq_order_dev, int num_seqs,
@@ -697,24 +727,14 @@ extern "C" int tokmix_gdn_prefill(const void* q, const void* k, const void* v, c
                                   float scale, int io_dtype, uint32_t* status, void* stream) {
   using namespace tokmix;
   using namespace tokmix::gdn;
-  if (!q || !k || !v || !g || !beta || !out || !final_state || !cu_seqlens_dev)
+  if (const int rc = validate_prefill_args("tokmix_gdn_prefill", q, k, v, g, beta, initial_state, out, final_state,
+                                           num_seqs, total_tokens, heads_k, heads_v, head_dim_k, head_dim_v, scale,
+                                           io_dtype))
+    return rc;
+  if (cu_seqlens_dev == nullptr)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: null pointer argument");
-  if (num_seqs < 0 || total_tokens < 0 || heads_k <= 0 || heads_v <= 0)
-    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: negative or zero size");
-  if (heads_v % heads_k != 0)
-    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: heads_v (%d) must be a multiple of heads_k (%d)",
-                heads_v, heads_k);
-  if (head_dim_k != kD || head_dim_v != kD)
-    return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_gdn_prefill: head dims must be 128 (got %d, %d)", head_dim_k,
-                head_dim_v);
-  if (io_dtype != TOKMIX_DTYPE_BF16)
-    return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_gdn_prefill: only bf16 q/k/v/out are supported by the kernel");
-  if (!std::isfinite(scale)) return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: scale must be finite");
   if (status == nullptr)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: a device status word is required");
-  for (const void* ptr : {q, k, v, static_cast<const void*>(initial_state), static_cast<const void*>(final_state)})
-    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
-      return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: tensors must be 16-byte aligned");
   if (num_seqs == 0) return TOKMIX_OK;
   if (const int rc = check_device()) return rc;
   const long long units = static_cast<long long>(num_seqs) * heads_v;
@@ -790,6 +810,25 @@ __global__ void fill_offsets(int32_t* offsets, int batch, int seqlen, uint32_t* 
 std::mutex g_mu;
 int32_t* g_base[64] = {};  // device address of g_scratch, per device (set up once)
 
+// Device address of the current device's copy of g_scratch.  Set-up, once per device, with that
+// device current: in host code the symbol is only a stand-in, the kernels need this address.
+int scratch_base(int32_t** base) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(TOKMIX_ERR_DEVICE, "tokmix_gdn_prefill_noalloc: no usable current device");
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_base[dev] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_scratch);
+    if (e != cudaSuccess)
+      return fail(TOKMIX_ERR_DEVICE, "tokmix_gdn_prefill_noalloc: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(e));
+    g_base[dev] = static_cast<int32_t*>(ptr);
+  }
+  *base = g_base[dev];
+  return TOKMIX_OK;
+}
+
 }  // namespace noalloc
 }  // namespace gdn
 }  // namespace tokmix
@@ -807,25 +846,16 @@ extern "C" int tokmix_gdn_prefill_noalloc(const void* q, const void* k, const vo
                 batch, na::kMaxSeqs);
   if (static_cast<long long>(batch) * seqlen > 0x7FFFFFFFll)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_noalloc: batch * seqlen exceeds 2^31 - 1");
+  // every check of the regular entry point that can fail runs before anything is enqueued, so a
+  // rejected call leaves the shared array (and a call still running on it) untouched
+  if (const int rc = gdn::validate_prefill_args("tokmix_gdn_prefill_noalloc", q, k, v, g, beta, initial_state, out,
+                                                final_state, batch, batch * seqlen, heads_k, heads_v, head_dim_k,
+                                                head_dim_v, scale, io_dtype))
+    return rc;
   if (batch == 0) return TOKMIX_OK;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
-    return fail(TOKMIX_ERR_DEVICE, "tokmix_gdn_prefill_noalloc: no usable current device");
+  if (const int rc = check_device()) return rc;
   int32_t* base = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(na::g_mu);
-    if (na::g_base[dev] == nullptr) {
-      // set-up, once per device, with that device current: the host-side symbol is only a
-      // stand-in, the kernels need the device address of this device's copy of the array
-      void* ptr = nullptr;
-      const cudaError_t e = cudaGetSymbolAddress(&ptr, na::g_scratch);
-      if (e != cudaSuccess)
-        return fail(TOKMIX_ERR_DEVICE, "tokmix_gdn_prefill_noalloc: cudaGetSymbolAddress failed: %s",
-                    cudaGetErrorString(e));
-      na::g_base[dev] = static_cast<int32_t*>(ptr);
-    }
-    base = na::g_base[dev];
-  }
+  if (const int rc = na::scratch_base(&base)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint32_t* st = status != nullptr ? status : reinterpret_cast<uint32_t*>(base);
   int32_t* offsets = base + 64;
@@ -833,4 +863,25 @@ extern "C" int tokmix_gdn_prefill_noalloc(const void* q, const void* k, const vo
   if (const int rc = check_launch("tokmix_gdn_prefill_noalloc")) return rc;
   return tokmix_gdn_prefill(q, k, v, g, beta, initial_state, out, final_state, offsets, nullptr, batch, batch * seqlen,
                             heads_k, heads_v, head_dim_k, head_dim_v, scale, io_dtype, st, stream);
+}
+
+// Reads the library-owned status word of the current device that tokmix_gdn_prefill_noalloc
+// uses when it is called with status == NULL (each such call clears it when it starts), with a
+// synchronous copy; clear != 0 zeroes it afterwards.  Allocates nothing.
+extern "C" int tokmix_gdn_noalloc_status(uint32_t* host_status, int clear) {
+  using namespace tokmix;
+  namespace na = tokmix::gdn::noalloc;
+  if (host_status == nullptr) return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_noalloc_status: null pointer");
+  if (const int rc = check_device()) return rc;
+  int32_t* base = nullptr;
+  if (const int rc = na::scratch_base(&base)) return rc;
+  cudaError_t e = cudaMemcpyFromSymbol(host_status, na::g_scratch, sizeof(uint32_t), 0, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && clear != 0) {
+    const int32_t zero = 0;
+    e = cudaMemcpyToSymbol(na::g_scratch, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice);
+  }
+  if (e != cudaSuccess)
+    return fail(TOKMIX_ERR_LAUNCH, "tokmix_gdn_noalloc_status: reading the status word failed: %s",
+                cudaGetErrorString(e));
+  return TOKMIX_OK;
 }

@@ -328,26 +328,6 @@ __device__ __forceinline__ uint32_t chain_setup(ChainBarriers& bars, uint32_t* t
   return *tmem_base_shared;
 }
 
-// Bounded wait for a record's ready flag (written by a preparation CTA of the same launch with
-// release semantics); afterwards the record may be read through the async proxy.
-__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t* status) {
-  const unsigned long long t0 = global_timer_ns();
-  while (true) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-    if (v != 0u) break;
-    if (cta_abort_flag() != 0u) return false;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
-      record_status(status, kDevTimeoutPipe);
-      cta_abort_flag() = 1u;
-      return false;
-    }
-    __nanosleep(128);
-  }
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-  return true;
-}
-
 // The state chain of one (sequence, value head) unit on warps 0-9 (roles above), with `bars`
 // initialised and 512 TMEM columns at `tbase`.  With `flags` non-null the loader waits (bounded)
 // for flags[record] before it reads a record: the records are then being written by other CTAs
@@ -837,7 +817,8 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   if (workspace == nullptr || workspace_bytes < need)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: workspace of %lld bytes needed (got %lld)", need,
                 workspace_bytes);
-  for (const void* ptr : {q, k, v, static_cast<const void*>(initial_state), static_cast<const void*>(final_state),
+  for (const void* ptr : {q, k, v, static_cast<const void*>(out), static_cast<const void*>(initial_state),
+                          static_cast<const void*>(final_state),
                           static_cast<const void*>(checkpoints), static_cast<const void*>(workspace)})
     if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
       return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: tensors must be 16-byte aligned");

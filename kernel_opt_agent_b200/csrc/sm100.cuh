@@ -122,21 +122,45 @@ __device__ __forceinline__ volatile uint32_t& cta_abort_flag() {
   return *reinterpret_cast<volatile uint32_t*>(&flag);
 }
 
-// Wait until the phase with the given parity has completed.  Gives up after kWaitTimeoutNs,
-// records `code` in *status (device memory, may be null), raises the CTA abort flag and returns
-// false; returns false at once if another warp of the CTA has already given up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t code) {
+// Wait until the phase with the given parity has completed.  Gives up after `limit_ns` of wall
+// time (kWaitTimeoutNs in every kernel; a shorter limit only in the wait self-test), records
+// `code` in *status (device memory, may be null), raises the CTA abort flag and returns false;
+// returns false at once if another warp of the CTA has already given up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t code,
+                                          unsigned long long limit_ns = kWaitTimeoutNs) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   while (true) {
     if (mbar_try_sleep(bar, parity, 100000u)) return true;
     if (cta_abort_flag() != 0u) return false;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       record_status(status, code);
       cta_abort_flag() = 1u;
       return false;
     }
   }
+}
+
+// Bounded wait for a ready flag in global memory (written by another CTA of the same launch with
+// release semantics); afterwards what the flag guards may be read through the async proxy.  Gives
+// up like mbar_wait, recording kDevTimeoutPipe.
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t* status,
+                                          unsigned long long limit_ns = kWaitTimeoutNs) {
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v != 0u) break;
+    if (cta_abort_flag() != 0u) return false;
+    if (global_timer_ns() - t0 > limit_ns) {
+      record_status(status, kDevTimeoutPipe);
+      cta_abort_flag() = 1u;
+      return false;
+    }
+    __nanosleep(128);
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
 }
 
 // Bounded wait that ignores the abort flag: used before a CTA retires, to let its own TMA loads

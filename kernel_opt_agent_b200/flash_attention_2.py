@@ -13,7 +13,6 @@ keyword; with the reference's arguments it behaves the same: q, k, v bf16 CUDA t
 from __future__ import annotations
 
 import math
-import os
 
 import torch
 
@@ -23,7 +22,6 @@ KERNEL_TYPE = "flash_attention_2"
 _HEAD_DIM = 128
 _HEAD_DIMS = (64, 128, 256)
 _DTYPE = torch.bfloat16
-_CHECK_STATUS = os.environ.get("TOKMIX_CHECK_STATUS", "0") == "1"
 
 
 def _validate_inputs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layout: str):
@@ -77,15 +75,14 @@ def kernel_fn(
             _lib.LAYOUT_BHSD if layout == "bhsd" else _lib.LAYOUT_BSHD, 1 if causal else 0, float(sm_scale),
             word.data_ptr(), _lib.stream_ptr(dev))
     _lib.check(rc, "flash_attention_2")
-    if _CHECK_STATUS:
-        _lib.raise_on_device_status(word, "flash_attention_2")
+    _lib.after_launch(dev, "flash_attention_2")
     return out
 
 
 def check_device_status(device: torch.device | None = None) -> None:
     """Synchronise and raise if any kernel on `device` reported a device-side timeout."""
     dev = device or torch.device("cuda", torch.cuda.current_device())
-    _lib.raise_on_device_status(_lib.status_word(dev), "flash_attention_2")
+    _lib.check_status(dev, "flash_attention_2")
 
 
 def get_inputs(

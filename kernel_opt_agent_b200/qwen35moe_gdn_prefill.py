@@ -56,7 +56,6 @@ KERNEL_TYPE = "qwen35moe_gdn_prefill"
 D = 128
 H_K = 16
 H_V = 32
-_CHECK_STATUS = os.environ.get("TOKMIX_CHECK_STATUS", "0") == "1"
 _SPLIT_MAX_WORKSPACE = 8 << 30  # bytes; larger problems use the one-launch schedule
 # Costs measured on a B200 (microseconds), from which "auto" predicts each schedule's time when
 # every unit fits on the SMs at once: a chunk of the fused kernel's chain (preparation inside the
@@ -213,8 +212,7 @@ def kernel_fn(
                 cu_t.data_ptr(), order_t.data_ptr() if order_t is not None else None,
                 nseq, total, hk, hv, D, D, float(scale), _lib.DTYPE_BF16, word.data_ptr(), _lib.stream_ptr(dev))
     _lib.check(rc, "qwen35moe_gdn_prefill")
-    if _CHECK_STATUS:
-        _lib.raise_on_device_status(word, "qwen35moe_gdn_prefill")
+    _lib.after_launch(dev, "qwen35moe_gdn_prefill")
     if io_dtype != torch.bfloat16:
         out = out.to(io_dtype)
     if ck is not None:
@@ -331,7 +329,7 @@ def schedule(q: torch.Tensor, v: torch.Tensor, cu_seqlens=None, mode: str = "aut
 def check_device_status(device: torch.device | None = None) -> None:
     """Synchronise and raise if any kernel on `device` reported a device-side timeout."""
     dev = device or torch.device("cuda", torch.cuda.current_device())
-    _lib.raise_on_device_status(_lib.status_word(dev), "qwen35moe_gdn_prefill")
+    _lib.check_status(dev, "qwen35moe_gdn_prefill")
 
 
 def filled(shape, scale: float, bias: float, dtype=torch.float32, device="cuda") -> torch.Tensor:
