@@ -2,6 +2,8 @@
 
   python tests/golden/make_golden.py --fa2 [--out DIR]   # CPU: torch's own SDPA (the reference's FA2 oracle)
   python tests/golden/make_golden.py --gdn [--out DIR]   # B200: the reference's scalar GDN CUDA kernel
+  python tests/golden/make_golden.py --rowops [--reference DIR] [--out DIR]
+                                                         # CPU: the reference's row-op checkers
 
 FA2: the reference's oracle is ``torch.nn.functional.scaled_dot_product_attention``
 (``references/flash_attention_2.py:33-41``); it is run here on the CPU in fp32 from bf16-rounded
@@ -9,7 +11,10 @@ inputs.  GDN: the reference's oracle is its fp32 scalar CUDA kernel
 (``kernels/qwen35moe_gdn_prefill.cu:31-100``), built from the reference sources by
 ``oracle/build_ref.py`` and run on a B200.  Inputs are not stored: they are regenerated from
 the formulas/seeds in ``golden_inputs`` below, which the tests import.  To keep the files small
-only some heads of each output are stored.
+only some heads of each output are stored.  Row ops: the reference's own torch checkers
+(``references/{rms_norm,swiglu_input_quant,qkv_part_rope}.py``), loaded from the reference
+checkout and run here on the CPU; every output is stored bit for bit (bf16 / fp16 / e4m3 as raw
+integers), so that the repository's checkers can be pinned without the checkout.
 """
 
 from __future__ import annotations
@@ -124,10 +129,74 @@ def make_gdn(out_dir: pathlib.Path):
     (out_dir / "gdn_golden_meta.json").write_text(json.dumps(meta, indent=1))
 
 
+ROWOP_CASES = {
+    "rowop_rms_norm_bf16": dict(op="rms_norm", m=64, n=512, dtype="bfloat16", seed=31),
+    "rowop_rms_norm_fp16": dict(op="rms_norm", m=33, n=1040, dtype="float16", seed=32),
+    "rowop_swiglu_quant": dict(op="swiglu_input_quant", m=48, n=384, seed=33),
+    "rowop_rope": dict(op="qkv_part_rope", b=1, s=16, heads=12, d=256, q_heads=10, kv_heads=1, nope=192,
+                       negative_sin=False, seed=34),
+    "rowop_rope_negsin": dict(op="qkv_part_rope", b=1, s=17, heads=6, d=128, q_heads=3, kv_heads=2, nope=64,
+                              negative_sin=True, seed=35),
+}
+
+
+def rowop_inputs(case: dict) -> dict:
+    """Seeded CPU inputs of a row-op case (the keyword arguments of its checker)."""
+    gen = torch.Generator().manual_seed(case["seed"])
+    if case["op"] == "rms_norm":
+        dt = getattr(torch, case["dtype"])
+        x = (torch.randn(case["m"], case["n"], generator=gen) * 2.0).to(dt)
+        w = (torch.rand(case["n"], generator=gen) + 0.5).to(dt)
+        return {"x": x, "weight": w, "eps": 1e-6}
+    if case["op"] == "swiglu_input_quant":
+        x = (torch.randn(case["m"], 2 * case["n"], generator=gen) * 3.0).to(torch.bfloat16)
+        x[0, :128] = 0.0  # an all-zero block: the eps clamp
+        return {"x": x}
+    rope = case["d"] - case["nope"]
+    pos = torch.arange(case["s"], dtype=torch.float32)[:, None]
+    inv = 10000.0 ** (-torch.arange(0, rope, 2, dtype=torch.float32) / rope)
+    return {"qkv": torch.randn(case["b"], case["s"], case["heads"], case["d"], generator=gen).to(torch.bfloat16),
+            "cos": torch.cos(pos * inv), "sin": torch.sin(pos * inv), "q_heads": case["q_heads"],
+            "kv_heads": case["kv_heads"], "nope_dim": case["nope"], "negative_sin": case["negative_sin"]}
+
+
+def raw(t: torch.Tensor) -> np.ndarray:
+    """The tensor's bits as an integer array (2- or 1-byte types) or its fp32 values."""
+    if t.dtype in (torch.bfloat16, torch.float16):
+        return t.contiguous().view(torch.int16).numpy()
+    if t.dtype == torch.float8_e4m3fn:
+        return t.contiguous().view(torch.uint8).numpy()
+    return t.contiguous().numpy()
+
+
+def reference_rowop_checkers(reference: pathlib.Path) -> dict:
+    """The reference's three row-op checker functions, loaded file by file from its checkout."""
+    import importlib.util
+
+    fns = {}
+    for op in ("rms_norm", "swiglu_input_quant", "qkv_part_rope"):
+        spec = importlib.util.spec_from_file_location(f"_ref_{op}", reference / "references" / f"{op}.py")
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        fns[op] = getattr(mod, f"{op}_ref")
+    return fns
+
+
+def make_rowops(out_dir: pathlib.Path, reference: pathlib.Path):
+    fns = reference_rowop_checkers(reference)
+    for name, case in ROWOP_CASES.items():
+        res = fns[case["op"]](**rowop_inputs(case))
+        res = res if isinstance(res, tuple) else (res,)
+        np.savez_compressed(out_dir / f"{name}.npz", **{f"out{i}": raw(t) for i, t in enumerate(res)})
+        print("wrote", name)
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--fa2", action="store_true")
     ap.add_argument("--gdn", action="store_true")
+    ap.add_argument("--rowops", action="store_true")
+    ap.add_argument("--reference", type=pathlib.Path, default=pathlib.Path("/root/reference"))
     ap.add_argument("--out", type=pathlib.Path, default=HERE)
     a = ap.parse_args()
     a.out.mkdir(parents=True, exist_ok=True)
@@ -135,3 +204,5 @@ if __name__ == "__main__":
         make_fa2(a.out)
     if a.gdn:
         make_gdn(a.out)
+    if a.rowops:
+        make_rowops(a.out, a.reference)
