@@ -6,11 +6,18 @@
 Workloads (synthetic data from fixed seeds, shapes of the B200 configs):
   gdn_b1_t2048   (default, headline)  GDN prefill B=1 T=2048 Hk=16 Hv=32 d=128, chunk 64, bf16 q/k/v/o,
                  fp32 g/beta/state, zero initial state.  Weak scaling: every rank runs its own batch.
+  gdn_b1_t2048_heads  the same single batch strong-scaled: the 16 key heads (with the value heads
+                 reading them) split across the ranks (at N > 1 under "also").
   fa2_b4_s8192   FA2 causal GQA forward B=4 Hq=32 Hkv=8 S=8192 D=128 bf16.  Strong scaling: the
-                 8 key/value heads (with their 4 query heads each) are split across ranks.
+                 8 key/value heads (with their 4 query heads each) are split across ranks.  Carries
+                 its own end-to-end leg, the CPU oracle on a sample, and torch SDPA (the reference's
+                 FA2 oracle) timed on the same inputs as a same-box comparator.
   gdn_varlen     GDN prefill, 8 sequences of U[1024, 32768] tokens packed with cu_seqlens,
                  per-sequence initial state N(0, 0.02).  Strong scaling over head groups.
   gdn_decode_b128  one GDN decode token for 128 sequences, states updated in place.
+  hybrid_t4096 / hybrid_t16384 / hybrid_t65536  (opt-in with --workload; minutes at T=65536)
+                 the hybrid prefill sweep: FA2 causal GQA Hq=16 Hkv=2 D=256 plus GDN prefill Hk=16
+                 Hv=32 d=128, both at B=16 and sequence length T, the batch split across the ranks.
 The headline line also carries the other workloads under "also" (same run, same timing rules), and
 on one GPU the three row-wise plugin ops (rms_norm M=16384 N=5120 bf16; swiglu_input_quant
 M=4096 N=7168; qkv_part_rope B=50 S=2048 12 heads of 256, nope 192) in GB/s of the bytes their
@@ -54,11 +61,12 @@ L2_BYTES = 126 * 1024 * 1024
 D = 128
 HK, HV = 16, 32
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of each workload's
-# kernel(s) from one ncu capture, keyed "workload/schedule"; profiles/*.md give the commands and
-# the raw figures.  ncu replays each kernel with flushed caches, so for the split GDN schedule the
-# chain kernel's reads of the records (which stay in L2 in a real run) count as DRAM reads.
-# FA2: captured at batch 1 (the batch-4 inputs exceed the capture size rule) and scaled by 4.
+# kernel(s) from one ncu capture, keyed "workload/schedule".  ncu replays each kernel with flushed
+# caches, so for the split GDN schedule the chain kernel's reads of the records (which stay in L2
+# in a real run) count as DRAM reads.  FA2: captured at batch 1 (the batch-4 inputs exceed the
+# capture size rule) and scaled by 4.
 NCU_TRAFFIC_BYTES = {
+    "gdn_b1_t2048/overlap": 43_180_000 + 47_150_000,  # ncu prints MB with two decimals here
     "gdn_b1_t2048/split": 17_699_072 + 23_969_536 + 104_127_488 + 7_339_264,  # prep + chain
     "gdn_b1_t2048/fused": 36_302_848 + 54_016,
     "fa2_b4_s8192/fused": 4 * (101_431_808 + 32_353_792),
@@ -182,8 +190,9 @@ def barrier():
         dist.barrier()
 
 
-def time_steps(step_fn, steps, warmup, device, flush: bool):
-    """Runs warmup + steps; returns (max-over-ranks total seconds of the K timed steps, per-step ms list)."""
+def time_steps(step_fn, steps, warmup, device, flush: bool, collective: bool = True):
+    """Runs warmup + steps; returns (max-over-ranks total seconds of the K timed steps, per-step ms
+    list).  collective=False: this rank alone (no barrier, no max over ranks)."""
     flush_buf = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device) if flush else None
     stream = torch.cuda.current_stream(device)
     for _ in range(warmup):
@@ -191,7 +200,8 @@ def time_steps(step_fn, steps, warmup, device, flush: bool):
             flush_buf.fill_(1)
         step_fn()
     torch.cuda.synchronize(device)
-    barrier()
+    if collective:
+        barrier()
     torch.cuda.synchronize(device)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -202,11 +212,12 @@ def time_steps(step_fn, steps, warmup, device, flush: bool):
         step_fn()
         ends[i].record(stream)
     torch.cuda.synchronize(device)
-    barrier()
+    if collective:
+        barrier()
     torch.cuda.synchronize(device)
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_s = sum(per) / 1e3
-    return max_over_ranks(total_s, device), per
+    return (max_over_ranks(total_s, device) if collective else total_s), per
 
 
 # ----------------------------------------------------------------------------- workloads
@@ -312,7 +323,9 @@ def run_row_op(device, steps, warmup, name):
                        "l2": "flushed between timed steps (256 MB write)"}}
 
 
-def run_fa2(device, rank, world, steps, warmup, batch=4, verify=False):
+def run_fa2(device, rank, world, steps, warmup, batch=4, verify=False, extras=False):
+    """FA2 causal GQA B4 Hq32 Hkv8 S8192 D128, key/value heads split across the ranks.  With
+    `extras`: the end-to-end leg and (one GPU) the torch SDPA comparators."""
     B, HQ, HKV, S, DD = batch, 32, 8, 8192, 128
     ranges = sharding.even_ranges(HKV, world)
     a, b = ranges[rank]
@@ -334,6 +347,10 @@ def run_fa2(device, rank, world, steps, warmup, batch=4, verify=False):
         got = sharding.gather_to_rank0(fa2.kernel_fn(**inp), dim=1)
         if rank == 0:
             res["verified_vs_one_gpu"] = bool(torch.equal(got, fa2.kernel_fn(**full)))
+    if extras:
+        res["e2e"] = e2e_fa2(device, inp, max(3, steps // 2), warmup, flops_total)
+        if world == 1:
+            res["sdpa"] = sdpa_comparators(inp, flops_total, steps, warmup, device)
     return res
 
 
@@ -349,10 +366,157 @@ def run_fa2_d256(device, steps, warmup, batch=16):
     return {"ms": total_s / steps * 1e3, "value": flops * steps / total_s / 1e12, "unit": "TFLOP/s",
             "kernel_ms_local": statistics.mean(per), "local_flops": flops,
             "kernel": "tokmix::fa2::d256::fa2_fwd_d256_kernel",
+            "sdpa": sdpa_comparators(inp, flops, steps, warmup, device),
             "config": {"workload": f"fa2_d256_b{B}_s4096", "batch": B, "heads_q": HQ, "heads_kv": HKV, "seq_len": S,
                        "head_dim": DD, "causal": True, "layout": "bhsd"}}
 
 
+def sdpa_comparators(inp, flops, steps, warmup, device):
+    """torch.nn.functional.scaled_dot_product_attention -- the reference's FA2 oracle and comparator
+    (``references/flash_attention_2.py:33-41``, paired with ``kernel_fn`` in ``tools/bench.py``) --
+    on the same device inputs with the same timing, once per backend that accepts the shape
+    (NVIDIA's own attention kernels for this GPU are among them).  TFLOP/s of the same flop count."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    q, k, v = inp["q"], inp["k"], inp["v"]
+    gqa = q.shape[1] != k.shape[1]
+    res = {}
+    for name, backend in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION),
+                          ("efficient", SDPBackend.EFFICIENT_ATTENTION)):
+        def call():
+            with sdpa_kernel(backend):
+                return torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True,
+                                                                        scale=inp["sm_scale"], enable_gqa=gqa)
+        try:
+            call()
+            torch.cuda.synchronize(device)
+        except RuntimeError as e:  # backend does not take this shape / GPU
+            res[name] = {"unavailable": str(e).splitlines()[0][:160]}
+            continue
+        total_s, _ = time_steps(call, steps, warmup, device, flush=input_bytes(inp) < L2_BYTES, collective=False)
+        res[name] = {"value": flops * steps / total_s / 1e12, "unit": "TFLOP/s", "ms": total_s / steps * 1e3}
+    return res
+
+
+def e2e_fa2(device, inp, steps, warmup, flops_total):
+    """FA2 step through the public plugin call from pinned host memory: q, k, v host->device,
+    kernel_fn, the output device->host, all inside the timed region."""
+    host = {n: inp[n].cpu().pin_memory() for n in ("q", "k", "v")}
+    dev_bufs = {n: torch.empty_like(t, device=device) for n, t in host.items()}
+    out_host = torch.empty(host["q"].shape, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * 2
+
+    def step():
+        for n, t in dev_bufs.items():
+            t.copy_(host[n], non_blocking=True)
+        out = fa2.kernel_fn(dev_bufs["q"], dev_bufs["k"], dev_bufs["v"], causal=True, sm_scale=inp["sm_scale"])
+        out_host.copy_(out, non_blocking=True)
+
+    total_s, _ = time_steps(step, steps, warmup, device, flush=False)
+    return {"value": flops_total * steps / total_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": total_s / steps * 1e3}
+
+
+def cpu_fa2_sample(s=8192, d=128, group=4, repeats=1):
+    """The oracle (fp32 softmax(q k^T scale + causal mask) v, numpy) on the host cores over a sample
+    of the FA2 workload: one (batch, key/value head) unit -- its `group` query heads over the full
+    sequence; returns (TFLOP/s of the causal flop count, cores, seconds, sample text)."""
+    sys.path.insert(0, ROOT)
+    import oracle  # the CPU restatement; only this leg of the benchmark uses it
+
+    gen = torch.Generator().manual_seed(3)
+    q = torch.randn(1, group, s, d, generator=gen).to(torch.bfloat16).float().numpy()
+    k = torch.randn(1, 1, s, d, generator=gen).to(torch.bfloat16).float().numpy()
+    v = torch.randn(1, 1, s, d, generator=gen).to(torch.bfloat16).float().numpy()
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        oracle.fa2_attention(q, k, v, causal=True, sm_scale=1.0 / math.sqrt(d))
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    flops = fa2.get_flops(1, group, s, d, causal=True)
+    return (flops / med / 1e12, os.cpu_count() or 1, med,
+            f"one (batch, kv head) unit of the workload: {group} query heads x S={s} x D={d}, causal, fp32 "
+            f"numpy oracle (oracle.fa2_attention) on the host cores, median of {repeats} ({med:.2f} s)")
+
+
+def run_gdn_heads(device, rank, world, steps, warmup, verify=False):
+    """GDN B1 T2048 strong-scaled: the 16 key heads (each with the value heads reading it) split
+    across the ranks; every rank runs the whole 2048-token sequence for its heads."""
+    full = gdn_inputs(device, 2048, seed=1000)
+    ranges = sharding.even_ranges(HK, world)
+    a, b = ranges[rank]
+    inp = sharding.slice_gdn_inputs(full, a, b)
+    if not verify:
+        del full
+    total_s, per = time_steps(lambda: gdn.kernel_fn(**inp), steps, warmup, device, flush=input_bytes(inp) < L2_BYTES)
+    gdn.check_device_status(device)
+    res = {"tokens_per_step": 2048, "ms": total_s / steps * 1e3, "value": 2048 * steps / total_s / 1e6,
+           "unit": "Mtok/s", "kernel_ms_local": statistics.mean(per),
+           "algo_bytes": gdn.algorithmic_bytes(2048, 1, hk=b - a, hv=2 * (b - a)), "token_heads": 2048 * 2 * (b - a),
+           "schedule": gdn.schedule(inp["q"], inp["v"]),
+           "config": {"workload": "gdn_b1_t2048_heads", "batch": 1, "seq_len": 2048, "hk": HK, "hv": HV,
+                      "head_dim": D, "shard": f"key heads {HK // world}/rank (+ the value heads reading them)",
+                      "scaling": "strong"}}
+    if verify and world > 1:
+        out, fs = gdn.kernel_fn(**inp)
+        go = sharding.gather_to_rank0(out, dim=2)
+        gs = sharding.gather_to_rank0(fs, dim=1)
+        if rank == 0:
+            ref_o, ref_s = gdn.kernel_fn(**full)
+            sizes = [2 * (y - x) for x, y in ranges]
+            offs = [sum(sizes[:i]) for i in range(world)]
+            o = sharding.unscatter_gdn_heads([go.narrow(2, o0, n) for o0, n in zip(offs, sizes)], ranges, HK, HV, 2)
+            st = sharding.unscatter_gdn_heads([gs.narrow(1, o0, n) for o0, n in zip(offs, sizes)], ranges, HK, HV, 1)
+            res["verified_vs_one_gpu"] = bool(torch.equal(o, ref_o) and torch.equal(st, ref_s))
+    return res
+
+
+HYBRID_B, HYBRID_HQ, HYBRID_HKV, HYBRID_D = 16, 16, 2, 256
+
+
+def run_hybrid(device, rank, world, steps, warmup, seq_len):
+    """The hybrid prefill sweep at one sequence length: FA2 causal GQA Hq=16 Hkv=2 D=256 and GDN
+    prefill Hk=16 Hv=32 d=128, both over a batch of 16 sequences of `seq_len` tokens, the batch
+    split evenly across the ranks (16 / N sequences per rank).  A step is one FA2 forward and one
+    GDN prefill over the rank's sequences; each is also timed alone for its roofline."""
+    local = HYBRID_B // world
+    fi = fa2_inputs(device, local, HYBRID_HQ, HYBRID_HKV, seq_len, HYBRID_D, seed=40 + rank)
+    gi = gdn_inputs(device, seq_len, seed=50 + rank, lengths=[seq_len] * local)
+    flush = input_bytes(fi) + input_bytes(gi) < L2_BYTES
+    fa_s, fa_per = time_steps(lambda: fa2.kernel_fn(**fi), steps, warmup, device, flush=flush)
+    fa2.check_device_status(device)
+    gd_s, gd_per = time_steps(lambda: gdn.kernel_fn(**gi), steps, warmup, device, flush=flush)
+    gdn.check_device_status(device)
+
+    def step():
+        fa2.kernel_fn(**fi)
+        gdn.kernel_fn(**gi)
+
+    tot_s, per = time_steps(step, steps, warmup, device, flush=flush)
+    tokens = HYBRID_B * seq_len
+    fa_flops = fa2.get_flops(HYBRID_B, HYBRID_HQ, seq_len, HYBRID_D, causal=True)
+    fa_local = fa2.get_flops(local, HYBRID_HQ, seq_len, HYBRID_D, causal=True)
+    return {"tokens_per_step": tokens, "ms": tot_s / steps * 1e3, "value": tokens * steps / tot_s / 1e6,
+            "unit": "Mtok/s", "kernel_ms_local": statistics.mean(per),
+            "parts": {
+                "fa2": {"ms": fa_s / steps * 1e3, "value": fa_flops * steps / fa_s / 1e12, "unit": "TFLOP/s",
+                        "kernel_ms_local": statistics.mean(fa_per), "local_flops": fa_local,
+                        "kernel": "tokmix::fa2::d256::fa2_fwd_d256_kernel"},
+                "gdn": {"ms": gd_s / steps * 1e3, "value": tokens * steps / gd_s / 1e6, "unit": "Mtok/s",
+                        "kernel_ms_local": statistics.mean(gd_per),
+                        "algo_bytes": gdn.algorithmic_bytes(local * seq_len, local),
+                        "token_heads": local * seq_len * HV,
+                        "schedule": gdn.schedule(gi["q"], gi["v"], gi["cu_seqlens"])}},
+            "config": {"workload": f"hybrid_t{seq_len}", "batch": HYBRID_B, "seq_len": seq_len,
+                       "fa2": {"heads_q": HYBRID_HQ, "heads_kv": HYBRID_HKV, "head_dim": HYBRID_D, "causal": True},
+                       "gdn": {"hk": HK, "hv": HV, "head_dim": D, "chunk": 64, "initial_state": "zero"},
+                       "shard": f"batch {local}/rank", "l2": "flushed between timed steps" if flush
+                       else "inputs larger than L2 (no flush)"}}
+
+
+HYBRID_WORKLOADS = ["hybrid_t4096", "hybrid_t16384", "hybrid_t65536"]
 # workloads that run on one GPU only (in "also" when the bench runs on one GPU)
 ONE_GPU_WORKLOADS = list(ROW_OPS) + ["fa2_d256_b16_s4096"]
 
@@ -453,10 +617,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="gdn_b1_t2048",
-                    choices=["gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_decode_b128", "gdn_b4_t2048",
-                             "fa2_b1_s8192", "fa2_d256_b4_s4096"] + ONE_GPU_WORKLOADS,
+                    choices=["gdn_b1_t2048", "gdn_b1_t2048_heads", "fa2_b4_s8192", "gdn_varlen", "gdn_decode_b128",
+                             "gdn_b4_t2048", "fa2_b1_s8192", "fa2_d256_b4_s4096"] + HYBRID_WORKLOADS
+                            + ONE_GPU_WORKLOADS,
                     help="gdn_b4_t2048 / fa2_b1_s8192 / fa2_d256_b4_s4096 are profiling-size cases (inputs just above L2); the "
-                         "row-wise op names time one op alone (one GPU)")
+                         "row-wise op names time one op alone (one GPU); hybrid_t* run the hybrid prefill sweep")
     ap.add_argument("--no-also", action="store_true", help="skip the secondary workloads")
     ap.add_argument("--no-verify", action="store_true",
                     help="with N > 1, skip gathering the sharded outputs to rank 0 for comparison with a one-GPU run")
@@ -485,8 +650,8 @@ def main():
     head = args.workload
     if (head in ONE_GPU_WORKLOADS or head == "fa2_d256_b4_s4096") and world != 1:
         raise SystemExit(f"workload {head} runs on one GPU")
-    order = [head] + ([w for w in ("gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_decode_b128") if w != head]
-                      if not args.no_also else [])
+    also = ["gdn_b1_t2048", "fa2_b4_s8192", "gdn_varlen", "gdn_decode_b128"] + (["gdn_b1_t2048_heads"] if world > 1 else [])
+    order = [head] + ([w for w in also if w != head] if not args.no_also and head not in HYBRID_WORKLOADS else [])
     e2e = None
     for w in order:
         steps_w = args.steps if w == head else max(5, args.steps // 5)
@@ -500,7 +665,11 @@ def main():
             del inp
         elif w in ("fa2_b4_s8192", "fa2_b1_s8192"):
             r = run_fa2(device, rank, world, steps_w, args.warmup, batch=4 if w == "fa2_b4_s8192" else 1,
-                        verify=not args.no_verify)
+                        verify=not args.no_verify, extras=(w == "fa2_b4_s8192"))
+        elif w == "gdn_b1_t2048_heads":
+            r = run_gdn_heads(device, rank, world, steps_w, args.warmup, verify=not args.no_verify)
+        elif w in HYBRID_WORKLOADS:
+            r = run_hybrid(device, rank, world, steps_w, args.warmup, seq_len=int(w[len("hybrid_t"):]))
         elif w == "gdn_decode_b128":
             r = run_gdn_decode(device, rank, world, steps_w, args.warmup)
         elif w in ROW_OPS:
@@ -511,7 +680,7 @@ def main():
             r = run_gdn_varlen(device, rank, world, steps_w, args.warmup, verify=not args.no_verify)
         results[w] = r
         torch.cuda.empty_cache()
-    if world == 1 and not args.no_also:
+    if world == 1 and not args.no_also and head not in HYBRID_WORKLOADS:
         for w in (x for x in ONE_GPU_WORKLOADS if x != head):
             steps_w = max(5, args.steps // 5)
             results[w] = (run_fa2_d256(device, steps_w, args.warmup) if w == "fa2_d256_b16_s4096"
@@ -525,13 +694,21 @@ def main():
         cpu = {"value": v, "unit": "Mtok/s", "cores": cores, "kind": "port",
                "sample": f"full decode step, 128 sequences Hk=16 Hv=32, median of 5 runs ({sec:.4f} s each), fp32 "
                          "recurrence (oracle/gdn_recurrent.c, OpenMP)"}
-    elif rank == 0 and world == 1 and head not in ONE_GPU_WORKLOADS and not head.startswith("fa2_d256"):
+    elif rank == 0 and world == 1 and head in ("gdn_b1_t2048", "gdn_b1_t2048_heads", "gdn_b4_t2048", "gdn_varlen"):
         v, cores, sec = cpu_gdn_b1()
         cpu = {"value": v, "unit": "Mtok/s", "cores": cores, "kind": "port",
                "sample": f"full B=1 T=2048 Hk=16 Hv=32 workload, median of 3 runs ({sec:.3f} s each), fp32 "
                          "recurrence (oracle/gdn_recurrent.c, OpenMP)"}
+    if rank == 0 and world == 1 and "fa2_b4_s8192" in results:
+        v, cores, sec, sample = cpu_fa2_sample()
+        fa2_cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
+        results["fa2_b4_s8192"]["cpu_baseline"] = fa2_cpu
+        if head == "fa2_b4_s8192":
+            cpu = fa2_cpu
 
     def roofline(w, r):
+        if "parts" in r:  # hybrid sweep: one roofline per kernel
+            return {"fa2": roofline("fa2_hybrid", r["parts"]["fa2"]), "gdn": roofline("gdn_hybrid", r["parts"]["gdn"])}
         kms = r["kernel_ms_local"]
         if w.startswith("fa2"):
             ach = r["local_flops"] / (kms / 1e3) / 1e12
@@ -571,6 +748,15 @@ def main():
                   "GDN decode Mtok/s" if head == "gdn_decode_b128" else
                   f"{ROW_OPS[head][1]} GB/s" if head in ROW_OPS else HEADLINE_METRIC)
         cfg = hr["config"]
+        if head in HYBRID_WORKLOADS:
+            metric = "hybrid prefill (FA2 D256 + GDN) Mtok/s"
+            sched = hr["parts"]["gdn"]["schedule"]
+            launches = args.steps * (1 + (2 if sched == "split" else 1))
+        else:
+            launches = args.steps * (2 if hr.get("schedule") == "split" else 1)
+        if e2e is None and "e2e" in hr:
+            e2e = hr["e2e"]
+        extra_keys = ("verified_vs_one_gpu", "e2e", "sdpa", "cpu_baseline", "parts")
         line = {"metric": metric, "value": hr["value"], "unit": hr["unit"], "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": hr["ms"], "higher_is_better": True,
                 "scaling": "weak" if head in ("gdn_b1_t2048", "gdn_b4_t2048") else "strong", "vs_baseline": None,
@@ -578,11 +764,12 @@ def main():
                 "data": "synthetic (seeded, B200 config shapes)", "config": cfg,
                 "roofline": roofline(head, hr), "cpu_baseline": cpu,
                 "e2e": e2e if e2e is not None else None,
-                "gpu_launches": args.steps * (2 if hr.get("schedule") == "split" else 1), "clocks": clocks,
+                "gpu_launches": launches, "clocks": clocks,
+                **({"sdpa": hr["sdpa"]} if "sdpa" in hr else {}),
+                **({"parts": hr["parts"]} if "parts" in hr else {}),
                 "also": {w: {"value": r["value"], "unit": r["unit"], "ms_per_step": r["ms"],
                              "roofline": roofline(w, r), **({"config": r["config"]} if "config" in r else {}),
-                             **({"verified_vs_one_gpu": r["verified_vs_one_gpu"]}
-                                if "verified_vs_one_gpu" in r else {})}
+                             **{x: r[x] for x in extra_keys if x in r}}
                          for w, r in results.items() if w != head}}
         print(json.dumps(line), flush=True)
     if world > 1:
