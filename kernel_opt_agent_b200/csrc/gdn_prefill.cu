@@ -84,6 +84,7 @@ struct Params {
   const int32_t* cu_seqlens;
   const int32_t* seq_order;
   int hk, hv;
+  int num_seqs, total_tokens;
   float scale;
   uint32_t* status;
 };
@@ -233,10 +234,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int unit = blockIdx.x;
   const int order = unit / p.hv;
   const int h = unit - order * p.hv;
-  const int seq = p.seq_order ? p.seq_order[order] : order;
+  // The scheduling order and the token offsets are device data the host does not read: a unit
+  // whose entries are out of range sets TOKMIX_DEV_BAD_ARGS and touches no memory.
+  const int seq_raw = p.seq_order ? p.seq_order[order] : order;
+  const bool seq_ok = seq_raw >= 0 && seq_raw < p.num_seqs;
+  const int seq = seq_ok ? seq_raw : 0;
   const int kh = h % p.hk;
-  const int tok0 = p.cu_seqlens[seq];
-  const int len = p.cu_seqlens[seq + 1] - tok0;
+  const long long t_begin = p.cu_seqlens[seq], t_end = p.cu_seqlens[seq + 1];
+  const bool bad = !seq_ok || t_begin < 0 || t_end < t_begin || t_end > p.total_tokens;
+  const int tok0 = bad ? 0 : static_cast<int>(t_begin);
+  const int len = bad ? 0 : static_cast<int>(t_end - t_begin);
   const int N = len > 0 ? (len + kC - 1) / kC : 0;
   ChunkParams* params = reinterpret_cast<ChunkParams*>(smem + kOffParams);
   const size_t state_off = (static_cast<size_t>(seq) * p.hv + h) * kD * kD;
@@ -265,9 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = tmem_base_shared;
   if (threadIdx.x == 0) GDN_TRACE(19, 0);
 
+  if (bad && threadIdx.x == 0) record_status(p.status, kDevBadArgs);
   if (N == 0) {
     // empty sequence: final state = initial state
-    if (warp < 4) {
+    if (warp < 4 && !bad) {
       const int v = threadIdx.x;
       for (int kk = 0; kk < kD; kk += 4) {
         float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -767,6 +775,8 @@ extern "C" int tokmix_gdn_prefill(const void* q, const void* k, const void* v, c
   p.seq_order = seq_order_dev;
   p.hk = heads_k;
   p.hv = heads_v;
+  p.num_seqs = num_seqs;
+  p.total_tokens = total_tokens;
   p.scale = scale;
   p.status = status;
   const int smem_bytes = kSmemBytes + 1024;

@@ -104,6 +104,7 @@ struct PrepParams {
   const int32_t* chunk_base;  // [num_seqs + 1]: first global chunk of each sequence
   uint8_t* ws;
   int num_seqs, hk, hv;
+  int total_tokens;
   float scale;
   uint32_t* status;
 };
@@ -117,6 +118,7 @@ struct ChainParams {
   const int32_t* chunk_base;
   const uint8_t* ws;
   int hk, hv;
+  int total_tokens, total_chunks;
   uint32_t* status;
 };
 
@@ -143,10 +145,17 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
     const int mid = (lo + hi) >> 1;
     if (p.chunk_base[mid] <= gc) lo = mid; else hi = mid;
   }
-  const int seq = lo, c = gc - p.chunk_base[seq];
-  const int tok0 = p.cu_seqlens[seq];
-  const int n_valid = min(kC, p.cu_seqlens[seq + 1] - tok0 - c * kC);
-  const int row0 = tok0 + c * kC;
+  // token offsets and chunk bases are device data the host does not read: a chunk that falls
+  // outside [0, total_tokens) sets TOKMIX_DEV_BAD_ARGS and reads no g / beta (its TMA loads stay
+  // in bounds on their own: rows outside the tensor read as zero)
+  const int seq = lo;
+  const long long c_ll = static_cast<long long>(gc) - p.chunk_base[seq];
+  const long long row_ll = p.cu_seqlens[seq] + c_ll * kC;
+  const long long valid_ll = min(static_cast<long long>(kC), static_cast<long long>(p.cu_seqlens[seq + 1]) - row_ll);
+  const bool bad = c_ll < 0 || row_ll < 0 || row_ll + max(valid_ll, 0ll) > p.total_tokens;
+  if (bad && tid == 0) record_status(p.status, kDevBadArgs);
+  const int n_valid = bad ? 0 : static_cast<int>(valid_ll);
+  const int row0 = bad ? 0 : static_cast<int>(row_ll);
   const int kh = h % p.hk;
   ChunkParams& pc = *reinterpret_cast<ChunkParams*>(smem + kPParams);
   float* Ls = reinterpret_cast<float*>(smem + kPL);
@@ -345,10 +354,18 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
   const int warp = warp_id(), lane = lane_id();
   const int seq = unit / p.hv, h = unit - seq * p.hv;
   const int kh = h % p.hk;
-  const int tok0 = p.cu_seqlens[seq];
-  const int len = p.cu_seqlens[seq + 1] - tok0;
+  // The token offsets and chunk bases are device data the host does not read: a unit whose
+  // entries are out of range or inconsistent sets TOKMIX_DEV_BAD_ARGS and touches no memory.
+  const long long t_begin = p.cu_seqlens[seq], t_end = p.cu_seqlens[seq + 1];
+  const long long gc_begin = p.chunk_base[seq];
+  const long long n_chunks = t_end > t_begin ? (t_end - t_begin + kC - 1) / kC : 0;
+  const bool bad = t_begin < 0 || t_end < t_begin || t_end > p.total_tokens || gc_begin < 0 ||
+                   gc_begin + n_chunks > p.total_chunks;
+  const int tok0 = bad ? 0 : static_cast<int>(t_begin);
+  const int len = bad ? 0 : static_cast<int>(t_end - t_begin);
   const int N = len > 0 ? (len + kC - 1) / kC : 0;
-  const int gc0 = p.chunk_base[seq];
+  const int gc0 = bad ? 0 : static_cast<int>(gc_begin);
+  if (bad && threadIdx.x == 0) record_status(p.status, kDevBadArgs);
   const size_t state_off = (static_cast<size_t>(seq) * p.hv + h) * kD * kD;
   auto stage = [&](int c) { return smem + (c & 1) * kStageBytes; };
   auto params_of = [&](int c) -> const ChunkParams& {
@@ -356,7 +373,7 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
   };
 
   if (N == 0) {
-    if (warp < 4) {
+    if (warp < 4 && !bad) {
       const int v = threadIdx.x;
       for (int kk = 0; kk < kD; kk += 4) {
         float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -738,6 +755,10 @@ __global__ void __launch_bounds__(kOverlapThreads, 1)
   uint32_t k = 0;
   for (int r = first; ok && r < op.records; r += stride, ++k) {
     const int rid = op.record_order[r];
+    if (rid < 0 || rid >= op.records) {  // device data the host does not read
+      if (tid == 0) record_status(pp.status, kDevBadArgs);
+      continue;
+    }
     const int gc = rid / pp.hv, h = rid - gc * pp.hv;
     ok = prep_record(&map_q, &map_k, pp, gc, h, smem + grp * kPSmemA, &pbar[grp][0], k & 1, &pbar[grp][1], tbase, tid,
                      1 + grp);
@@ -851,6 +872,7 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   pp.chunk_base = chunk_base_dev;
   pp.ws = static_cast<uint8_t*>(workspace);
   pp.num_seqs = num_seqs;
+  pp.total_tokens = total_tokens;
   pp.hk = heads_k;
   pp.hv = heads_v;
   pp.scale = scale;
@@ -865,6 +887,8 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   cp.ws = static_cast<const uint8_t*>(workspace);
   cp.hk = heads_k;
   cp.hv = heads_v;
+  cp.total_tokens = total_tokens;
+  cp.total_chunks = total_chunks;
   cp.status = status;
   const long long records = static_cast<long long>(total_chunks) * heads_v;
   // --- one cooperative launch when the chains leave SMs free for the preparation CTAs

@@ -94,3 +94,49 @@ def test_selftest_rejects_bad_arguments():
     assert lib.tokmix_selftest_wait_timeout(0, 10, None, None, 16, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
     assert lib.tokmix_selftest_wait_timeout(0, 2_000_000_000, None, None, 16, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
     assert lib.tokmix_selftest_wait_timeout(2, LIMIT_NS, None, None, 16, None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+
+
+def _prefill_args(inp):
+    q, k, v, g, beta, st = (inp[x] for x in ("q", "k", "v", "g", "beta", "state"))
+    out = torch.empty_like(v)
+    final = torch.empty(st.shape, dtype=torch.float32, device=q.device)
+    return q, k, v, g, beta, st, out, final
+
+
+def test_inconsistent_device_offsets_set_bad_args_bit(cuda_device):
+    """Token offsets and chunk bases live on the device, where the host does not check them: a
+    sequence whose offsets run backwards (one-CTA-per-unit kernel) or whose chunk base points
+    past the workspace (record-fed chain) sets TOKMIX_DEV_BAD_ARGS and is skipped, while the
+    consistent sequence of the same call is still computed."""
+    lib = _lib.load()
+    inp = gcfg.random_inputs(1, 128, seed=4, state_std=0.02, hk=2, hv=4)
+    inp["state"] = torch.cat([inp["state"], inp["state"]])  # two sequences
+    q, k, v, g, beta, st, out, final = _prefill_args(inp)
+    ref_o, ref_s = gdn.kernel_fn(q[:, :64], k[:, :64], v[:, :64], g[:, :64], beta[:, :64], inp["state"][:1],
+                                 inp["scale"], mode="fused")
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    # fused kernel: sequence 1 = tokens [64, 32): backwards
+    word = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    cu = torch.tensor([0, 64, 32], dtype=torch.int32, device=cuda_device)
+    rc = lib.tokmix_gdn_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), st.data_ptr(),
+                                out.data_ptr(), final.data_ptr(), cu.data_ptr(), None, 2, 128, 2, 4, 128, 128,
+                                float(inp["scale"]), _lib.DTYPE_BF16, word.data_ptr(), stream)
+    _lib.check(rc, "tokmix_gdn_prefill")
+    torch.cuda.synchronize()
+    assert int(word.item()) == 0x8
+    assert torch.equal(out[:, :64], ref_o) and torch.equal(final[:1], ref_s)
+    # record-fed chain: sequence 1's chunk base lies past the two records of the workspace
+    word.zero_()
+    cu = torch.tensor([0, 64, 128], dtype=torch.int32, device=cuda_device)
+    cb = torch.tensor([0, 5, 6], dtype=torch.int32, device=cuda_device)
+    nbytes = int(lib.tokmix_gdn_split_workspace_bytes(2, 4))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda_device)
+    out.zero_()
+    rc = lib.tokmix_gdn_prefill_split(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(),
+                                      st.data_ptr(), out.data_ptr(), final.data_ptr(), None, cu.data_ptr(), cb.data_ptr(),
+                                      None, 2, 128, 2, 2, 4, 128, 128, float(inp["scale"]), _lib.DTYPE_BF16,
+                                      ws.data_ptr(), nbytes, word.data_ptr(), stream)
+    _lib.check(rc, "tokmix_gdn_prefill_split")
+    torch.cuda.synchronize()
+    assert int(word.item()) == 0x8
+    assert torch.equal(out[:, :64], ref_o) and torch.equal(final[:1], ref_s)
