@@ -147,6 +147,52 @@ int tokmix_gdn_prefill_split(const void* q, const void* k, const void* v, const 
 /* Workspace size of tokmix_gdn_prefill_split in bytes (-1 for negative arguments). */
 long long tokmix_gdn_split_workspace_bytes(int total_chunks, int heads_v);
 
+/* Gated-delta-rule prefill with long sequences cut into segments that run side by side, for
+ * problems whose longest sequence would otherwise set the time (a few long sequences, or a
+ * head slice of them on one GPU of several).  Same maths, arguments and results as
+ * tokmix_gdn_prefill (up to fp32 summation order and one extra bf16 rounding of the outputs of
+ * later segments), plus:
+ *   cu_seqlens_host:    host int32 [num_seqs + 1], the same offsets as cu_seqlens_dev (the
+ *                       segment plan is made on the host)
+ *   chunk_base_dev:     as for tokmix_gdn_prefill_split
+ *   max_segment_chunks: a sequence of more than this many 64-token chunks is cut into the
+ *                       fewest near-equal segments of at most this many chunks
+ *   plan_dev:           NULL, or a device copy (16-byte aligned) of the tables that
+ *                       tokmix_gdn_segmented_plan writes for the same offsets, heads_v and
+ *                       max_segment_chunks (kept by a caller that repeats a shape); with NULL the
+ *                       call uploads them into the workspace itself, from pageable host memory,
+ *                       which makes the host wait for the stream
+ *   workspace:          device memory of tokmix_gdn_segmented_workspace_bytes(...) bytes,
+ *                       16-byte aligned (preparation records, the segments' transition
+ *                       outputs and states, room for the plan's tables)
+ * Four launches on `stream`: chunk-parallel preparation; one state chain per segment and value
+ * head -- the first segment from the sequence's initial state, every later segment twice, from a
+ * zero state (its own contribution) and from the identity with zero values (its transition,
+ * whose end state and outputs are linear in the segment's true entry state); a combine kernel
+ * that chains the entry states E(j+1) = E(j) M(j) + N(j) in fp32 and writes the final states;
+ * and a tensor-core GEMM that adds each later segment's entry-state share R E^T to its outputs.
+ * No counterpart in the reference (its chunk scan runs each sequence's chunks in order,
+ * kernels_optimized/qwen35moe_gdn_prefill.cu:1131-1153). */
+int tokmix_gdn_prefill_segmented(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                                 const float* initial_state, void* out, float* final_state,
+                                 const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev,
+                                 const int32_t* cu_seqlens_host, int num_seqs, int total_tokens, int total_chunks,
+                                 int heads_k, int heads_v, int head_dim_k, int head_dim_v, float scale, int io_dtype,
+                                 int max_segment_chunks, const void* plan_dev, void* workspace,
+                                 long long workspace_bytes, uint32_t* status, void* stream);
+
+/* Workspace size of tokmix_gdn_prefill_segmented in bytes (-1 for inconsistent arguments). */
+long long tokmix_gdn_segmented_workspace_bytes(const int32_t* cu_seqlens_host, int num_seqs, int heads_v,
+                                               int max_segment_chunks);
+
+/* Size in bytes of the segment plan's tables (-1 for inconsistent arguments), and the tables
+ * written to plan_host (host memory of at least that size), for a device copy passed as
+ * tokmix_gdn_prefill_segmented's plan_dev. */
+long long tokmix_gdn_segmented_plan_bytes(const int32_t* cu_seqlens_host, int num_seqs, int heads_v,
+                                          int max_segment_chunks);
+int tokmix_gdn_segmented_plan(const int32_t* cu_seqlens_host, int num_seqs, int heads_v, int max_segment_chunks,
+                              void* plan_host, long long plan_bytes);
+
 /* One decode step of the gated delta rule: one new token per sequence, bf16 in and out, fp32 state.
  *
  *   for every sequence b, value head h (key head h % heads_k) and value row c:

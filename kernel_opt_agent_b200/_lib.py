@@ -51,6 +51,11 @@ SIGNATURES = {
     "tokmix_gdn_prefill_split": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I,
                                       _I, _I, _F, _I, _VP, ctypes.c_longlong, _VP, _VP]),
     "tokmix_gdn_noalloc_status": (_I, [_VP, _I]),
+    "tokmix_gdn_prefill_segmented": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I,
+                                          _I, _I, _F, _I, _I, _VP, _VP, ctypes.c_longlong, _VP, _VP]),
+    "tokmix_gdn_segmented_workspace_bytes": (ctypes.c_longlong, [_VP, _I, _I, _I]),
+    "tokmix_gdn_segmented_plan_bytes": (ctypes.c_longlong, [_VP, _I, _I, _I]),
+    "tokmix_gdn_segmented_plan": (_I, [_VP, _I, _I, _I, _VP, ctypes.c_longlong]),
     "tokmix_gdn_split_workspace_bytes": (ctypes.c_longlong, [_I, _I]),
     "tokmix_gdn_decode": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _F, _I, _VP]),
     "tokmix_l2norm_rows": (_I, [_VP, _I, _VP, ctypes.c_longlong, _I, _F, _VP]),

@@ -14,9 +14,13 @@
 // Results equal gdn_prefill.cu's up to fp32 summation order (same operands, same splits).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
+#include <cstring>
+#include <vector>
 
 #include "gdn_common.cuh"
+#include "gdn_segment.cuh"
 #include "host_common.h"
 
 namespace tokmix {
@@ -109,6 +113,20 @@ struct PrepParams {
   uint32_t* status;
 };
 
+// A chain unit of the segmented schedule: `nchunks` chunks of sequence `seq` from its chunk
+// `chunk0` on, for every value head.  kind:
+//   kSegWhole  the whole sequence: initial state -> state_out[seq]; outputs to out
+//   kSegFirst  its first segment: initial state -> seg_states[slot]; outputs to out
+//   kSegLocal  a later segment from a zero state: real V; end state -> seg_states[slot]; outputs
+//              (the segment's part that does not depend on its entry state) to out
+//   kSegTrans  the same segment from the identity with V = 0: its end state (the segment's
+//              transition matrix) -> seg_states[slot]; its outputs R (the entry state's share of
+//              the outputs is R times the entry state transposed) to r_out
+struct SegUnit {
+  int32_t seq, chunk0, nchunks, kind_slot;  // kind in the low 2 bits, slot above
+};
+constexpr int kSegWhole = 0, kSegFirst = 1, kSegLocal = 2, kSegTrans = 3;
+
 struct ChainParams {
   const float* state_in;
   float* state_out;
@@ -120,6 +138,11 @@ struct ChainParams {
   int hk, hv;
   int total_tokens, total_chunks;
   uint32_t* status;
+  // segmented schedule (units == null: unit u is (sequence u / hv, head u % hv), kind kSegWhole)
+  const SegUnit* units;
+  int num_units, num_slots, num_seqs;
+  float* seg_states;      // [num_slots, hv, 128, 128]
+  __nv_bfloat16* r_out;   // [total_tokens, hv, 128]
 };
 
 // bulk copy global -> shared, completing on an mbarrier (one destination CTA)
@@ -352,21 +375,49 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
                                            uint8_t* smem, ChainBarriers& bars, uint32_t tbase, int unit,
                                            const uint32_t* flags) {
   const int warp = warp_id(), lane = lane_id();
-  const int seq = unit / p.hv, h = unit - seq * p.hv;
+  const int entry = unit / p.hv, h = unit - entry * p.hv;
   const int kh = h % p.hk;
-  // The token offsets and chunk bases are device data the host does not read: a unit whose
-  // entries are out of range or inconsistent sets TOKMIX_DEV_BAD_ARGS and touches no memory.
-  const long long t_begin = p.cu_seqlens[seq], t_end = p.cu_seqlens[seq + 1];
-  const long long gc_begin = p.chunk_base[seq];
+  // Which tokens, start state and destinations this unit has.  The token offsets, chunk bases and
+  // segment table are device data the host does not read: a unit whose entries are out of range
+  // or inconsistent sets TOKMIX_DEV_BAD_ARGS and touches no memory.
+  int seq = entry, chunk0 = 0, kind = kSegWhole, slot = 0;
+  long long seg_chunks = -1;  // -1: the whole sequence
+  if (p.units != nullptr) {
+    const SegUnit su = p.units[entry];
+    seq = su.seq;
+    chunk0 = su.chunk0;
+    seg_chunks = su.nchunks;
+    kind = su.kind_slot & 3;
+    slot = su.kind_slot >> 2;
+  }
+  bool bad = seq < 0 || seq >= p.num_seqs || chunk0 < 0 ||
+             (kind != kSegWhole && (slot < 0 || slot >= p.num_slots || seg_chunks < 1));
+  long long t_begin = 0, t_end = 0, gc_begin = 0;
+  if (!bad) {
+    const long long s_begin = p.cu_seqlens[seq], s_end = p.cu_seqlens[seq + 1];
+    t_begin = s_begin + static_cast<long long>(chunk0) * kC;
+    t_end = seg_chunks < 0 ? s_end : min(s_end, t_begin + seg_chunks * kC);
+    gc_begin = static_cast<long long>(p.chunk_base[seq]) + chunk0;
+    bad = s_begin < 0 || s_end < s_begin || s_end > p.total_tokens || t_begin > s_end ||
+          (seg_chunks > 0 && t_end <= t_begin);
+  }
   const long long n_chunks = t_end > t_begin ? (t_end - t_begin + kC - 1) / kC : 0;
-  const bool bad = t_begin < 0 || t_end < t_begin || t_end > p.total_tokens || gc_begin < 0 ||
-                   gc_begin + n_chunks > p.total_chunks;
+  bad = bad || gc_begin < 0 || gc_begin + n_chunks > p.total_chunks;
   const int tok0 = bad ? 0 : static_cast<int>(t_begin);
   const int len = bad ? 0 : static_cast<int>(t_end - t_begin);
   const int N = len > 0 ? (len + kC - 1) / kC : 0;
   const int gc0 = bad ? 0 : static_cast<int>(gc_begin);
   if (bad && threadIdx.x == 0) record_status(p.status, kDevBadArgs);
-  const size_t state_off = (static_cast<size_t>(seq) * p.hv + h) * kD * kD;
+  const bool zero_v = (kind == kSegTrans);
+  // start state: the sequence's initial state (null: zero), zero, or the identity
+  const float* s_in = (kind == kSegWhole || kind == kSegFirst) && p.state_in != nullptr
+                          ? p.state_in + (static_cast<size_t>(seq) * p.hv + h) * kD * kD
+                          : nullptr;
+  const bool s_identity = (kind == kSegTrans);
+  float* s_out = kind == kSegWhole ? p.state_out + (static_cast<size_t>(seq) * p.hv + h) * kD * kD
+                                   : p.seg_states + (static_cast<size_t>(slot) * p.hv + h) * kD * kD;
+  __nv_bfloat16* o_dst = zero_v ? p.r_out : p.out;
+  float* const ckpt = kind == kSegWhole ? p.checkpoints : nullptr;
   auto stage = [&](int c) { return smem + (c & 1) * kStageBytes; };
   auto params_of = [&](int c) -> const ChunkParams& {
     return *reinterpret_cast<const ChunkParams*>(stage(c) + kRecParams);
@@ -377,8 +428,8 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
       const int v = threadIdx.x;
       for (int kk = 0; kk < kD; kk += 4) {
         float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (p.state_in) val = *reinterpret_cast<const float4*>(p.state_in + state_off + v * kD + kk);
-        *reinterpret_cast<float4*>(p.state_out + state_off + v * kD + kk) = val;
+        if (s_in) val = *reinterpret_cast<const float4*>(s_in + v * kD + kk);
+        *reinterpret_cast<float4*>(s_out + v * kD + kk) = val;
       }
     }
   } else if (warp == 8) {
@@ -399,12 +450,12 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
         const size_t ridx = static_cast<size_t>(gc0 + c) * p.hv + h;
         const uint8_t* rec = p.ws + ridx * kRecBytes;
         if (flags != nullptr && !wait_flag(flags + ridx, p.status)) break;
-        mbar_arrive_expect_tx(bar, kRecBytes + 32768);
+        mbar_arrive_expect_tx(bar, kRecBytes + (zero_v ? 16384 : 32768));
         bulk_g2s(st, rec, kRecP, bar);  // T, W, e^G Q
         bulk_g2s(st + kRecP, rec + kRecP, kRecBytes - kRecP, bar);  // P, params
         for (int bx = 0; bx < 2; ++bx) {
           tma_load_3d(st + kSK + bx * 8192, map_k, bar, bx * 64, kh, tok0 + c * kC);
-          tma_load_3d(st + kSV + bx * 8192, map_v, bar, bx * 64, h, tok0 + c * kC);
+          if (!zero_v) tma_load_3d(st + kSV + bx * 8192, map_v, bar, bx * 64, h, tok0 + c * kC);
         }
         issued = c + 1;
       }
@@ -417,10 +468,12 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
     auto issue_tv = [&](int c) {
       const uint32_t st = smem_u32(stage(c));
       const uint32_t id_v = make_idesc(128, 128, 1, 1, 1);
+      if (!zero_v) {  // with V = 0, T V is zero: the state terms start X instead
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        umma_bf16_ss(tbase + kColX, make_sdesc_sw128(st + kSV + kk * 2048, 8192, 1024),
-                     make_sdesc_sw128(st + kRecT + kk * 2048, 8192, 1024), id_v, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16_ss(tbase + kColX, make_sdesc_sw128(st + kSV + kk * 2048, 8192, 1024),
+                       make_sdesc_sw128(st + kRecT + kk * 2048, 8192, 1024), id_v, kk > 0 ? 1u : 0u);
+      }
       umma_commit(&bars.tv_done[c & 1]);
       SPLIT_TRACE(12, c);
     };
@@ -446,7 +499,7 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             umma_bf16_ts(tbase + kColX, tbase + kColShi + 8 * kk, make_sdesc_sw128(st + kRecW + kk * 2048, 16384, 1024),
-                         id128, 1u);
+                         id128, (zero_v && kk == 0) ? 0u : 1u);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             umma_bf16_ts(tbase + kColX, tbase + kColSlo + 8 * kk, make_sdesc_sw128(st + kRecW + kk * 2048, 16384, 1024),
@@ -524,11 +577,15 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
 #pragma unroll
       for (int j = 0; j < 64; j += 4) {
         float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (p.state_in) val = *reinterpret_cast<const float4*>(p.state_in + state_off + v * kD + 64 * hh + j);
+        if (s_in) val = *reinterpret_cast<const float4*>(s_in + v * kD + 64 * hh + j);
         sv[j] = __float_as_uint(val.x);
         sv[j + 1] = __float_as_uint(val.y);
         sv[j + 2] = __float_as_uint(val.z);
         sv[j + 3] = __float_as_uint(val.w);
+      }
+      if (s_identity) {  // the identity: row v has its 1 in key column v
+#pragma unroll
+        for (int j = 0; j < 64; ++j) sv[j] = (64 * hh + j == v) ? __float_as_uint(1.0f) : 0u;
       }
       store_split32<0>(lb + kColShi + 32 * hh, lb + kColSlo + 32 * hh, sv);
       store_split32<32>(lb + kColShi + 32 * hh + 16, lb + kColSlo + 32 * hh + 16, sv);
@@ -554,7 +611,7 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
       const int nv = min(kC, len - co * kC) - 32 * hh;
       const bool odd = (lane & 1) != 0;
       const size_t tstride = static_cast<size_t>(p.hv) * kD;
-      uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (static_cast<size_t>(tok0 + co * kC + 32 * hh) * p.hv + h) * kD +
+      uint32_t* dst = reinterpret_cast<uint32_t*>(o_dst + (static_cast<size_t>(tok0 + co * kC + 32 * hh) * p.hv + h) * kD +
                                                   (v & ~1)) + (odd ? tstride / 2 : 0);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -576,8 +633,8 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
           const float gam = params_of(c).gamma_c;
           uint32_t sv[64];
           tmem_ld64(lb + kColS + 64 * hh, sv);
-          if (p.checkpoints != nullptr && c > 0) {  // S(c): the state after chunk c-1
-            float* dst = p.checkpoints + (static_cast<size_t>(gc0 + c - 1) * p.hv + h) * kD * kD + v * kD + 64 * hh;
+          if (ckpt != nullptr && c > 0) {  // S(c): the state after chunk c-1
+            float* dst = ckpt + (static_cast<size_t>(gc0 + c - 1) * p.hv + h) * kD * kD + v * kD + 64 * hh;
 #pragma unroll
             for (int j = 0; j < 64; j += 4)
               __stcs(reinterpret_cast<float4*>(dst + j), make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
@@ -636,10 +693,9 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
         uint32_t sv[64];
         tmem_ld64(lb + kColS + 64 * hh, sv);
         if (last) {
-          float* dst = p.state_out + state_off + v * kD + 64 * hh;
-          float* ck = p.checkpoints != nullptr
-                          ? p.checkpoints + (static_cast<size_t>(gc0 + c) * p.hv + h) * kD * kD + v * kD + 64 * hh
-                          : nullptr;
+          float* dst = s_out + v * kD + 64 * hh;
+          float* ck = ckpt != nullptr ? ckpt + (static_cast<size_t>(gc0 + c) * p.hv + h) * kD * kD + v * kD + 64 * hh
+                                      : nullptr;
 #pragma unroll
           for (int j = 0; j < 64; j += 4) {
             const float4 val = make_float4(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1]),
@@ -803,6 +859,29 @@ extern "C" int tokmix_gdn_split_trace_read(unsigned long long* host, int n) {
 }
 #endif
 
+namespace tokmix {
+namespace gdn {
+namespace split {
+
+// TMA maps over q, k [tokens, heads_k, 128] and v [tokens, heads_v, 128] (bf16); boxes of 64
+// columns x 1 head x 64 tokens, 128-byte swizzle.
+static bool encode_qkv_maps(const void* q, const void* k, const void* v, int total_tokens, int heads_k, int heads_v,
+                            CUtensorMap* mq, CUtensorMap* mk, CUtensorMap* mv) {
+  const uint64_t rows = static_cast<uint64_t>(total_tokens > 0 ? total_tokens : 1);
+  uint64_t dims_k[3] = {kD, static_cast<uint64_t>(heads_k), rows};
+  uint64_t strides_k[2] = {kD * 2, static_cast<uint64_t>(heads_k) * kD * 2};
+  uint64_t dims_v[3] = {kD, static_cast<uint64_t>(heads_v), rows};
+  uint64_t strides_v[2] = {kD * 2, static_cast<uint64_t>(heads_v) * kD * 2};
+  uint32_t box[3] = {64, 1, 64};
+  return encode_tiled(mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, dims_k, strides_k, box, CU_TENSOR_MAP_SWIZZLE_128B) &&
+         encode_tiled(mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, k, dims_k, strides_k, box, CU_TENSOR_MAP_SWIZZLE_128B) &&
+         encode_tiled(mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, v, dims_v, strides_v, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace split
+}  // namespace gdn
+}  // namespace tokmix
+
 // records of kRecBytes, then one uint32 ready flag per record (used by the overlapped launch)
 extern "C" long long tokmix_gdn_split_workspace_bytes(int total_chunks, int heads_v) {
   if (total_chunks < 0 || heads_v < 0) return -1;
@@ -848,22 +927,8 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   if (units > 0x7FFFFFFFll)
     return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_gdn_prefill_split: problem too large");
 
-  const uint64_t rows = static_cast<uint64_t>(total_tokens > 0 ? total_tokens : 1);
   CUtensorMap mq, mk, mv;
-  {
-    uint64_t dims_k[3] = {kD, static_cast<uint64_t>(heads_k), rows};
-    uint64_t strides_k[2] = {kD * 2, static_cast<uint64_t>(heads_k) * kD * 2};
-    uint64_t dims_v[3] = {kD, static_cast<uint64_t>(heads_v), rows};
-    uint64_t strides_v[2] = {kD * 2, static_cast<uint64_t>(heads_v) * kD * 2};
-    uint32_t box[3] = {64, 1, 64};
-    if (!encode_tiled(&mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, dims_k, strides_k, box,
-                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_tiled(&mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, k, dims_k, strides_k, box,
-                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_tiled(&mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, v, dims_v, strides_v, box,
-                      CU_TENSOR_MAP_SWIZZLE_128B))
-      return TOKMIX_ERR_INVALID_ARGUMENT;
-  }
+  if (!encode_qkv_maps(q, k, v, total_tokens, heads_k, heads_v, &mq, &mk, &mv)) return TOKMIX_ERR_INVALID_ARGUMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   PrepParams pp{};
   pp.g = g;
@@ -889,6 +954,7 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   cp.hv = heads_v;
   cp.total_tokens = total_tokens;
   cp.total_chunks = total_chunks;
+  cp.num_seqs = num_seqs;  // units == null: one whole-sequence unit per (sequence, head)
   cp.status = status;
   const long long records = static_cast<long long>(total_chunks) * heads_v;
   // --- one cooperative launch when the chains leave SMs free for the preparation CTAs
@@ -937,4 +1003,295 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
     return check_launch("tokmix_gdn_prefill_split: cudaFuncSetAttribute (chain)");
   gdn_chain_kernel<<<static_cast<unsigned>(units), kChainThreads, smem, s>>>(mk, mv, cp);
   return check_launch("tokmix_gdn_prefill_split (chain)");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Segmented schedule: a long sequence's chunks are cut into segments that run side by side (see
+// gdn_segment.cuh for the maths).  Host side: the plan (chain units, combine items, correction
+// tiles), the workspace layout, and the entry point that launches preparation, chains, combine
+// and correction in order on one stream.
+namespace tokmix {
+namespace gdn {
+namespace segment {
+
+struct Plan {
+  std::vector<split::SegUnit> units;
+  std::vector<CombineItem> combine;
+  std::vector<CorrItem> corr;
+  int num_slots = 0, num_eslots = 0;
+  long long off_r = 0, off_states = 0, off_e = 0, off_units = 0, off_combine = 0, off_corr = 0, total = 0;
+};
+
+static long long round256(long long x) { return (x + 255) / 256 * 256; }
+
+// Builds the plan from the host copy of the token offsets; returns false (error set) on
+// inconsistent arguments.  Sequences of more than max_seg chunks are cut into the fewest
+// near-equal segments of at most max_seg chunks.
+static bool make_plan(const int32_t* cu, int num_seqs, int total_tokens, int total_chunks, int hv, int max_seg,
+                      Plan& plan) {
+  if (cu == nullptr || num_seqs < 0 || max_seg < 1) {
+    fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_segmented: bad host offsets or max_segment_chunks");
+    return false;
+  }
+  long long chunks = 0;
+  for (int n = 0; n < num_seqs; ++n) {
+    if (cu[n] < 0 || cu[n + 1] < cu[n]) {
+      fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_segmented: host offsets must be non-decreasing from 0");
+      return false;
+    }
+    chunks += (cu[n + 1] - cu[n] + kC - 1) / kC;
+  }
+  if (cu[0] != 0 || cu[num_seqs] != total_tokens || chunks != total_chunks) {
+    fail(TOKMIX_ERR_INVALID_ARGUMENT,
+         "tokmix_gdn_prefill_segmented: host offsets disagree with total_tokens / total_chunks");
+    return false;
+  }
+  for (int n = 0; n < num_seqs; ++n) {
+    const int len = cu[n + 1] - cu[n];
+    const int nch = (len + kC - 1) / kC;
+    if (nch <= max_seg) {
+      plan.units.push_back({n, 0, -1, split::kSegWhole});
+      continue;
+    }
+    const int nseg = (nch + max_seg - 1) / max_seg;
+    const int base = nch / nseg, extra = nch % nseg;
+    const int slot_base = plan.num_slots, e_base = plan.num_eslots;
+    plan.num_slots += 2 * nseg - 1;
+    plan.num_eslots += nseg - 1;
+    int c0 = 0;
+    for (int j = 0; j < nseg; ++j) {
+      const int sz = base + (j < extra ? 1 : 0);
+      if (j == 0) {
+        plan.units.push_back({n, 0, sz, split::kSegFirst | (slot_base << 2)});
+      } else {
+        plan.units.push_back({n, c0, sz, split::kSegLocal | ((slot_base + 2 * j - 1) << 2)});
+        plan.units.push_back({n, c0, sz, split::kSegTrans | ((slot_base + 2 * j) << 2)});
+        const int t_begin = cu[n] + c0 * kC, t_end = std::min(cu[n + 1], cu[n] + (c0 + sz) * kC);
+        for (int t = t_begin; t < t_end; t += 128)
+          plan.corr.push_back({t, std::min(128, t_end - t), e_base + j - 1, 0});
+      }
+      c0 += sz;
+    }
+    plan.combine.push_back({n, nseg, slot_base, e_base});
+  }
+  // longest chains first
+  std::stable_sort(plan.units.begin(), plan.units.end(), [&](const split::SegUnit& a, const split::SegUnit& b) {
+    auto len = [&](const split::SegUnit& u) { return u.nchunks >= 0 ? u.nchunks : (cu[u.seq + 1] - cu[u.seq] + kC - 1) / kC; };
+    return len(a) > len(b);
+  });
+  const long long records = static_cast<long long>(total_chunks) * hv;
+  plan.off_r = round256(records * split::kRecBytes);
+  plan.off_states = plan.off_r + round256(static_cast<long long>(total_tokens) * hv * kD * 2);
+  plan.off_e = plan.off_states + round256(static_cast<long long>(plan.num_slots) * hv * kD * kD * 4);
+  plan.off_units = plan.off_e + round256(static_cast<long long>(plan.num_eslots) * hv * kD * kD * 2);
+  plan.off_combine = plan.off_units + round256(static_cast<long long>(plan.units.size()) * sizeof(split::SegUnit));
+  plan.off_corr = plan.off_combine + round256(static_cast<long long>(plan.combine.size()) * sizeof(CombineItem));
+  plan.total = plan.off_corr + round256(static_cast<long long>(plan.corr.size()) * sizeof(CorrItem));
+  return true;
+}
+
+// The plan's tables as they lie in device memory: units, combine items, correction tiles, each
+// section starting on a 256-byte boundary (the last plan.total - plan.off_units bytes of the
+// workspace, or a separate device copy).
+static void write_tables(const Plan& plan, uint8_t* dst) {
+  std::memset(dst, 0, static_cast<size_t>(plan.total - plan.off_units));
+  std::memcpy(dst, plan.units.data(), plan.units.size() * sizeof(split::SegUnit));
+  std::memcpy(dst + (plan.off_combine - plan.off_units), plan.combine.data(), plan.combine.size() * sizeof(CombineItem));
+  std::memcpy(dst + (plan.off_corr - plan.off_units), plan.corr.data(), plan.corr.size() * sizeof(CorrItem));
+}
+
+}  // namespace segment
+}  // namespace gdn
+}  // namespace tokmix
+
+extern "C" long long tokmix_gdn_segmented_workspace_bytes(const int32_t* cu_seqlens_host, int num_seqs, int heads_v,
+                                                          int max_segment_chunks) {
+  using namespace tokmix::gdn;
+  if (cu_seqlens_host == nullptr || num_seqs < 0 || heads_v <= 0 || max_segment_chunks < 1) return -1;
+  long long chunks = 0;
+  for (int n = 0; n < num_seqs; ++n) {
+    if (cu_seqlens_host[n + 1] < cu_seqlens_host[n]) return -1;
+    chunks += (cu_seqlens_host[n + 1] - cu_seqlens_host[n] + kC - 1) / kC;
+  }
+  if (chunks > 0x7FFFFFFFll) return -1;
+  segment::Plan plan;
+  if (!segment::make_plan(cu_seqlens_host, num_seqs, cu_seqlens_host[num_seqs], static_cast<int>(chunks), heads_v,
+                          max_segment_chunks, plan))
+    return -1;
+  return plan.total;
+}
+
+// Size of the plan tables, and the tables themselves written to host memory (for a caller that
+// keeps a device copy and passes it as plan_dev).
+extern "C" long long tokmix_gdn_segmented_plan_bytes(const int32_t* cu_seqlens_host, int num_seqs, int heads_v,
+                                                     int max_segment_chunks) {
+  using namespace tokmix::gdn;
+  const long long ws = tokmix_gdn_segmented_workspace_bytes(cu_seqlens_host, num_seqs, heads_v, max_segment_chunks);
+  if (ws < 0) return -1;
+  long long chunks = 0;
+  for (int n = 0; n < num_seqs; ++n) chunks += (cu_seqlens_host[n + 1] - cu_seqlens_host[n] + kC - 1) / kC;
+  segment::Plan plan;
+  segment::make_plan(cu_seqlens_host, num_seqs, cu_seqlens_host[num_seqs], static_cast<int>(chunks), heads_v,
+                     max_segment_chunks, plan);
+  return plan.total - plan.off_units;
+}
+
+extern "C" int tokmix_gdn_segmented_plan(const int32_t* cu_seqlens_host, int num_seqs, int heads_v,
+                                         int max_segment_chunks, void* plan_host, long long plan_bytes) {
+  using namespace tokmix;
+  using namespace tokmix::gdn;
+  const long long need = tokmix_gdn_segmented_plan_bytes(cu_seqlens_host, num_seqs, heads_v, max_segment_chunks);
+  if (need < 0) return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_segmented_plan: inconsistent arguments");
+  if (plan_host == nullptr || plan_bytes < need)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_segmented_plan: %lld bytes needed (got %lld)", need, plan_bytes);
+  long long chunks = 0;
+  for (int n = 0; n < num_seqs; ++n) chunks += (cu_seqlens_host[n + 1] - cu_seqlens_host[n] + kC - 1) / kC;
+  segment::Plan plan;
+  segment::make_plan(cu_seqlens_host, num_seqs, cu_seqlens_host[num_seqs], static_cast<int>(chunks), heads_v,
+                     max_segment_chunks, plan);
+  segment::write_tables(plan, static_cast<uint8_t*>(plan_host));
+  return TOKMIX_OK;
+}
+
+extern "C" int tokmix_gdn_prefill_segmented(const void* q, const void* k, const void* v, const float* g,
+                                            const float* beta, const float* initial_state, void* out,
+                                            float* final_state, const int32_t* cu_seqlens_dev,
+                                            const int32_t* chunk_base_dev, const int32_t* cu_seqlens_host,
+                                            int num_seqs, int total_tokens, int total_chunks, int heads_k, int heads_v,
+                                            int head_dim_k, int head_dim_v, float scale, int io_dtype,
+                                            int max_segment_chunks, const void* plan_dev, void* workspace,
+                                            long long workspace_bytes, uint32_t* status, void* stream) {
+  using namespace tokmix;
+  using namespace tokmix::gdn;
+  using namespace tokmix::gdn::split;
+  const char* who = "tokmix_gdn_prefill_segmented";
+  if (num_seqs < 0 || total_tokens < 0 || total_chunks < 0 || heads_k <= 0 || heads_v <= 0)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: negative or zero size", who);
+  if (num_seqs == 0) return TOKMIX_OK;
+  if (!q || !k || !v || !g || !beta || !out || !final_state || !cu_seqlens_dev || !chunk_base_dev || !status)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: null pointer argument", who);
+  if (heads_v % heads_k != 0)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: heads_v (%d) must be a multiple of heads_k (%d)", who, heads_v, heads_k);
+  if (head_dim_k != kD || head_dim_v != kD)
+    return fail(TOKMIX_ERR_UNSUPPORTED, "%s: head dims must be 128 (got %d, %d)", who, head_dim_k, head_dim_v);
+  if (io_dtype != TOKMIX_DTYPE_BF16)
+    return fail(TOKMIX_ERR_UNSUPPORTED, "%s: only bf16 q/k/v/out are supported by the kernel", who);
+  if (!std::isfinite(scale)) return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: scale must be finite", who);
+  for (const void* ptr : {q, k, v, static_cast<const void*>(out), static_cast<const void*>(initial_state),
+                          static_cast<const void*>(final_state), static_cast<const void*>(workspace), plan_dev})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+      return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: tensors must be 16-byte aligned", who);
+  segment::Plan plan;
+  if (!segment::make_plan(cu_seqlens_host, num_seqs, total_tokens, total_chunks, heads_v, max_segment_chunks, plan))
+    return TOKMIX_ERR_INVALID_ARGUMENT;
+  if (workspace == nullptr || workspace_bytes < plan.total)
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: workspace of %lld bytes needed (got %lld)", who, plan.total,
+                workspace_bytes);
+  if (static_cast<long long>(plan.units.size()) * heads_v > 0x7FFFFFFFll ||
+      static_cast<long long>(plan.corr.size()) > 0x7FFFFFFFll || plan.num_slots > (1 << 28))
+    return fail(TOKMIX_ERR_UNSUPPORTED, "%s: problem too large", who);
+  if (const int rc = check_device()) return rc;
+
+  CUtensorMap mq, mk, mv;
+  if (!encode_qkv_maps(q, k, v, total_tokens, heads_k, heads_v, &mq, &mk, &mv)) return TOKMIX_ERR_INVALID_ARGUMENT;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  auto* r_out = reinterpret_cast<__nv_bfloat16*>(ws + plan.off_r);
+  auto* seg_states = reinterpret_cast<float*>(ws + plan.off_states);
+  auto* e_bf16 = reinterpret_cast<__nv_bfloat16*>(ws + plan.off_e);
+  // the plan's tables: the caller's device copy, or the workspace's last bytes (uploaded below)
+  const uint8_t* tables = plan_dev != nullptr ? static_cast<const uint8_t*>(plan_dev) : ws + plan.off_units;
+  auto* units_dev = reinterpret_cast<const SegUnit*>(tables);
+  auto* combine_dev = reinterpret_cast<const segment::CombineItem*>(tables + (plan.off_combine - plan.off_units));
+  auto* corr_dev = reinterpret_cast<const segment::CorrItem*>(tables + (plan.off_corr - plan.off_units));
+  CUtensorMap map_r{}, map_e{};
+  if (!plan.corr.empty()) {  // R [tokens, hv, 128] and E [eslots * hv * 128 rows, 128] bf16, 128-row boxes
+    uint64_t dims_r[3] = {kD, static_cast<uint64_t>(heads_v), static_cast<uint64_t>(total_tokens)};
+    uint64_t strides_r[2] = {kD * 2, static_cast<uint64_t>(heads_v) * kD * 2};
+    uint32_t box_r[3] = {64, 1, 128};
+    uint64_t dims_e[2] = {kD, static_cast<uint64_t>(plan.num_eslots) * heads_v * kD};
+    uint64_t strides_e[1] = {kD * 2};
+    uint32_t box_e[2] = {64, 128};
+    if (!encode_tiled(&map_r, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, r_out, dims_r, strides_r, box_r,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tiled(&map_e, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, e_bf16, dims_e, strides_e, box_e,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+      return TOKMIX_ERR_INVALID_ARGUMENT;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (plan_dev == nullptr) {  // from host memory into the workspace (pageable: staged by the driver)
+    std::vector<uint8_t> host(static_cast<size_t>(plan.total - plan.off_units));
+    segment::write_tables(plan, host.data());
+    if (cudaMemcpyAsync(ws + plan.off_units, host.data(), host.size(), cudaMemcpyHostToDevice, s) != cudaSuccess)
+      return check_launch("tokmix_gdn_prefill_segmented: uploading the plan");
+  }
+
+  PrepParams pp{};
+  pp.g = g;
+  pp.beta = beta;
+  pp.cu_seqlens = cu_seqlens_dev;
+  pp.chunk_base = chunk_base_dev;
+  pp.ws = ws;
+  pp.num_seqs = num_seqs;
+  pp.total_tokens = total_tokens;
+  pp.hk = heads_k;
+  pp.hv = heads_v;
+  pp.scale = scale;
+  pp.status = status;
+  if (total_chunks > 0) {
+    const int smem = kPSmem + 1024;
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_prep_kernel), smem))
+      return check_launch("tokmix_gdn_prefill_segmented: cudaFuncSetAttribute (prep)");
+    gdn_prep_kernel<<<dim3(static_cast<unsigned>(total_chunks), static_cast<unsigned>(heads_v)), kPrepThreads, smem, s>>>(
+        mq, mk, pp);
+    if (const int rc = check_launch("tokmix_gdn_prefill_segmented (prep)")) return rc;
+  }
+  ChainParams cp{};
+  cp.state_in = initial_state;
+  cp.state_out = final_state;
+  cp.checkpoints = nullptr;
+  cp.out = static_cast<__nv_bfloat16*>(out);
+  cp.cu_seqlens = cu_seqlens_dev;
+  cp.chunk_base = chunk_base_dev;
+  cp.ws = ws;
+  cp.hk = heads_k;
+  cp.hv = heads_v;
+  cp.total_tokens = total_tokens;
+  cp.total_chunks = total_chunks;
+  cp.status = status;
+  cp.units = units_dev;
+  cp.num_units = static_cast<int>(plan.units.size());
+  cp.num_slots = plan.num_slots;
+  cp.num_seqs = num_seqs;
+  cp.seg_states = seg_states;
+  cp.r_out = r_out;
+  {
+    const int smem = kCSmem + 1024;
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_chain_kernel), smem))
+      return check_launch("tokmix_gdn_prefill_segmented: cudaFuncSetAttribute (chain)");
+    gdn_chain_kernel<<<static_cast<unsigned>(plan.units.size() * heads_v), kChainThreads, smem, s>>>(mk, mv, cp);
+    if (const int rc = check_launch("tokmix_gdn_prefill_segmented (chain)")) return rc;
+  }
+  if (!plan.combine.empty()) {
+    const int smem = segment::kCombineSmem;
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(&segment::combine_kernel), smem))
+      return check_launch("tokmix_gdn_prefill_segmented: cudaFuncSetAttribute (combine)");
+    segment::combine_kernel<<<dim3(static_cast<unsigned>(plan.combine.size()), static_cast<unsigned>(heads_v),
+                                   kD / segment::kCombineRows),
+                              segment::kCombineThreads, smem, s>>>(combine_dev, static_cast<int>(plan.combine.size()),
+                                                                  seg_states, e_bf16, final_state, heads_v,
+                                                                  plan.num_slots, plan.num_eslots, num_seqs, status);
+    if (const int rc = check_launch("tokmix_gdn_prefill_segmented (combine)")) return rc;
+  }
+  if (!plan.corr.empty()) {
+    const int smem = segment::kCorrSmem + 1024;
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(&segment::correction_kernel), smem))
+      return check_launch("tokmix_gdn_prefill_segmented: cudaFuncSetAttribute (correction)");
+    segment::correction_kernel<<<dim3(static_cast<unsigned>(plan.corr.size()), static_cast<unsigned>(heads_v)),
+                                 segment::kCorrThreads, smem, s>>>(map_r, map_e, corr_dev,
+                                                                   static_cast<int>(plan.corr.size()),
+                                                                   static_cast<__nv_bfloat16*>(out), heads_v,
+                                                                   total_tokens, plan.num_eslots, status);
+    if (const int rc = check_launch("tokmix_gdn_prefill_segmented (correction)")) return rc;
+  }
+  return TOKMIX_OK;
 }

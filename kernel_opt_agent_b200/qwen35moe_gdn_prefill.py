@@ -35,17 +35,21 @@ Extensions over the reference module:
   128] with cu_seqlens (sequence n's chunks from ``sum(ceil(len_m/64) for m < n)``) -- for prefix
   caching or a backward pass; the last chunk's entry equals the final state.  Checkpoints come
   from the split-family schedules ("split"/"overlap", chosen whatever the unit count).
-* ``mode`` (keyword): "auto" (default), "fused", "split" or "overlap" selects the schedule; the
-  environment variable TOKMIX_GDN_MODE overrides "auto".  "auto" picks "fused" when the units
-  fill the SMs, else "overlap" when at least 8 SMs are left for the preparation CTAs, else
-  "split" (and the library itself falls back from "overlap" to two launches when the device
-  cannot hold the cooperative grid).  A batched call with one token per sequence (T = 1, the
+* ``mode`` (keyword): "auto" (default), "fused", "split", "overlap" or "segmented" selects the
+  schedule; the environment variable TOKMIX_GDN_MODE overrides "auto".  "auto" picks "fused" when
+  the units fill the SMs, else the schedule with the lowest predicted time (and the library
+  itself falls back from "overlap" to two launches when the device cannot hold the cooperative
+  grid).  "segmented" (``tokmix_gdn_prefill_segmented``) cuts sequences longer than a segment
+  length into segments whose chains run side by side and joins them afterwards (the entry state
+  of each segment enters its outputs and end state linearly); the length is the shortest whose
+  chains still fit on the SMs at once, or ``segment_chunks`` (keyword, in 64-token chunks).  A batched call with one token per sequence (T = 1, the
   decode step of a serving loop) runs ``qwen35moe_gdn_decode``'s one-pass kernel instead under
   "auto" ("decode").
 """
 
 from __future__ import annotations
 
+import ctypes
 import os
 
 import torch
@@ -60,16 +64,30 @@ _SPLIT_MAX_WORKSPACE = 8 << 30  # bytes; larger problems use the one-launch sche
 # Costs measured on a B200 (microseconds), from which "auto" predicts each schedule's time when
 # every unit fits on the SMs at once: a chunk of the fused kernel's chain (preparation inside the
 # CTA; 277 us / 32 chunks at B1 T2048, 2.9 ms / 347 chunks on a varlen slice), a chunk of the chain
-# fed from prepared records (113 us / 32, 1.05 ms / 347, start-up included), one preparation
-# record with three preparation groups per SM (alone, and beside the chains of the overlapped
-# launch: 4096 records on 60 groups took 1.36 ms), the overlapped launch's start-up, and the gap
-# between the split schedule's two launches.
+# fed from prepared records (split B1 T2048: 140 us = 44 preparation + 32 chunks + gap), one
+# preparation record with three preparation groups per SM (alone: 49 us for 1024 records, 308 us
+# for 7364; beside the chains of the overlapped launch: 1.51 ms for the 14,728 records of a 4-GPU
+# varlen slice), the overlapped launch's start-up, and the gap between launches.
 _US_FUSED_CHUNK = 8.5
-_US_CHAIN_CHUNK = 3.0
-_US_PREP_RECORD = 15.0
-_US_PREP_RECORD_OVERLAP = 20.0
+_US_CHAIN_CHUNK = 2.7
+_US_PREP_RECORD = 19.0
+_US_PREP_RECORD_OVERLAP = 24.0
 _US_OVERLAP_START = 20.0
 _US_SPLIT_GAP = 10.0
+# The segmented schedule (measured launch list: B1 T2048 cut in 2, a varlen slice of 4 value
+# heads cut into segments of 106 chunks): chains of a segment (start-up + per chunk), the combine
+# (start-up + per extra segment of the most-cut sequence), the correction GEMM (start-up + its
+# traffic: R read, out read and written, 768 B per later-segment token and head, at an effective
+# 3.5 TB/s), and the gaps between its four launches.  Segments shorter than _SEG_MIN_CHUNKS are
+# not made.
+_US_SEG_CHAIN_START = 10.0
+_US_SEG_CHAIN_CHUNK = 2.65
+_US_SEG_COMBINE_START = 5.0
+_US_SEG_COMBINE_STEP = 8.0
+_US_SEG_CORR_START = 5.0
+_SEG_CORR_BYTES_PER_US = 3.5e6
+_US_SEG_GAPS = 15.0
+_SEG_MIN_CHUNKS = 8
 QK_L2NORM_EPS = 1e-6
 
 _meta_cache: dict = {}
@@ -154,6 +172,7 @@ def kernel_fn(
     qk_l2norm: bool = False,
     checkpoints: bool = False,
     gates=None,
+    segment_chunks: int | None = None,
 ) -> list[torch.Tensor]:
     nseq, hk, hv = _validate(q, k, v, g, beta, state, cu_seqlens)
     if gates is not None:
@@ -191,11 +210,27 @@ def kernel_fn(
     final_state = torch.empty((nseq, hv, D, D), dtype=torch.float32, device=dev)
     lib = _lib.load()
     word = _lib.status_word(dev)
-    sched = _schedule(mode, nseq * hv, total_chunks, hv, dev, checkpoints,
-                      max_chunks=max((n + 63) // 64 for n in lengths))
+    sched, seg_len = _plan(mode, lengths, hv, dev, checkpoints)
+    if sched == "segmented" and segment_chunks is not None:
+        if int(segment_chunks) < 1:
+            raise ValueError("segment_chunks must be positive")
+        seg_len = int(segment_chunks)
     ck = torch.empty((total_chunks, hv, D, D), dtype=torch.float32, device=dev) if checkpoints else None
     with torch.cuda.device(dev):
-        if sched != "fused":
+        if sched == "segmented":
+            cu_host = _host_offsets(lengths)
+            nbytes = int(lib.tokmix_gdn_segmented_workspace_bytes(cu_host, nseq, hv, seg_len))
+            if nbytes < 0:
+                raise ValueError("qwen35moe_gdn_prefill: no segmented plan for these lengths")
+            ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+            plan_t = _segment_plan(lengths, cu_host, hv, seg_len, dev)
+            rc = lib.tokmix_gdn_prefill_segmented(
+                qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
+                st.data_ptr() if st is not None else None, out.data_ptr(), final_state.data_ptr(),
+                cu_t.data_ptr(), cb_t.data_ptr(), cu_host, nseq, total, total_chunks, hk, hv, D, D, float(scale),
+                _lib.DTYPE_BF16, seg_len, plan_t.data_ptr(), ws.data_ptr(), ws.numel(), word.data_ptr(),
+                _lib.stream_ptr(dev))
+        elif sched != "fused":
             nbytes = int(lib.tokmix_gdn_split_workspace_bytes(total_chunks, hv))
             ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
             rec_t = _record_order(lengths, cb_host, hv, dev) if sched == "overlap" else None
@@ -274,56 +309,154 @@ def _record_order(lengths: tuple[int, ...], chunk_base: list[int], hv: int, devi
 def _mode(mode: str) -> str:
     if mode == "auto":
         mode = os.environ.get("TOKMIX_GDN_MODE", "auto")
-    if mode not in ("auto", "fused", "split", "overlap"):
-        raise ValueError(f"mode must be 'auto', 'fused', 'split' or 'overlap' (got {mode!r})")
+    if mode not in ("auto", "fused", "split", "overlap", "segmented"):
+        raise ValueError(f"mode must be 'auto', 'fused', 'split', 'overlap' or 'segmented' (got {mode!r})")
     return mode
 
 
-def _predicted_us(sched: str, units: int, records: int, max_chunks: int, sms: int) -> float:
+def _host_offsets(lengths: tuple[int, ...]):
+    """cu_seqlens as a host int32 array for the C ABI (the segment plan is made on the host)."""
+    key = ("cu_host", lengths)
+    hit = _meta_cache.get(key)
+    if hit is None:
+        cu = [0]
+        for n in lengths:
+            cu.append(cu[-1] + n)
+        hit = (ctypes.c_int32 * len(cu))(*cu)
+        _meta_cache[key] = hit
+    return hit
+
+
+def _segment_plan(lengths: tuple[int, ...], cu_host, hv: int, seg_len: int, device: torch.device) -> torch.Tensor:
+    """The segmented schedule's tables (``tokmix_gdn_segmented_plan``) on the device, made and
+    uploaded once per shape, so that a call enqueues no host-to-device copy."""
+    key = ("segplan", lengths, hv, seg_len, device)
+    hit = _meta_cache.get(key)
+    if hit is None:
+        lib = _lib.load()
+        nbytes = int(lib.tokmix_gdn_segmented_plan_bytes(cu_host, len(lengths), hv, seg_len))
+        if nbytes < 0:
+            raise ValueError("qwen35moe_gdn_prefill: no segmented plan for these lengths")
+        host = torch.zeros(max(nbytes, 16), dtype=torch.uint8)
+        _lib.check(lib.tokmix_gdn_segmented_plan(cu_host, len(lengths), hv, seg_len, host.data_ptr(), host.numel()),
+                   "tokmix_gdn_segmented_plan")
+        hit = host.to(device)
+        _meta_cache[key] = hit
+    return hit
+
+
+def _segment_units(nchunks: list[int], seg_len: int) -> tuple[int, int, int]:
+    """(chain units per head, most segments of one sequence, chunks in later segments) when
+    sequences longer than seg_len chunks are cut into the fewest near-equal segments of at most
+    seg_len chunks: a whole sequence is one chain, a cut one 2 s - 1 (its first segment, then
+    each later segment twice)."""
+    units, most, later = 0, 1, 0
+    for n in nchunks:
+        s = -(-n // seg_len) if n > seg_len else 1
+        units += 2 * s - 1
+        most = max(most, s)
+        if s > 1:
+            later += n - (n // s + (1 if n % s else 0))
+    return units, most, later
+
+
+def segment_length(lengths, hv: int, sms: int) -> int | None:
+    """The segment length (chunks) of the segmented schedule: the shortest whose chains
+    (units x hv) still fit on the SMs at once, no shorter than _SEG_MIN_CHUNKS; None when cutting
+    gains nothing (no sequence longer than that length)."""
+    nch = [(n + 63) // 64 for n in lengths]
+    longest = max(nch, default=0)
+    best = None
+    for seg in range(longest - 1, _SEG_MIN_CHUNKS - 1, -1):
+        units = _segment_units(nch, seg)[0]
+        if units * hv > sms:
+            break
+        best = seg
+    return best
+
+
+def _predicted_us(sched: str, units: int, records: int, max_chunks: int, sms: int, segs: int = 1,
+                  later_chunks: int = 0, hv: int = 0) -> float:
     """Predicted time of one schedule for `units` chains (all on the SMs at once) whose longest
-    has `max_chunks` chunks, with `records` preparation records in all."""
+    has `max_chunks` chunks, with `records` preparation records in all (for "segmented": the
+    longest segment, `segs` segments in the most-cut sequence and `later_chunks` chunks in later
+    segments, per value head of the hv)."""
     if sched == "fused":
         return max_chunks * _US_FUSED_CHUNK
     if sched == "overlap":  # the chains and 3 preparation groups on each remaining SM
         prep = records * _US_PREP_RECORD_OVERLAP / (3 * (sms - units))
         return max(max_chunks * _US_CHAIN_CHUNK, prep) + _US_OVERLAP_START
-    return records * _US_PREP_RECORD / (3 * sms) + max_chunks * _US_CHAIN_CHUNK + _US_SPLIT_GAP
+    prep = records * _US_PREP_RECORD / (3 * sms)
+    if sched == "segmented":
+        corr = later_chunks * 64 * hv * 768 / _SEG_CORR_BYTES_PER_US
+        return (prep + _US_SEG_CHAIN_START + max_chunks * _US_SEG_CHAIN_CHUNK + _US_SEG_COMBINE_START
+                + (segs - 1) * _US_SEG_COMBINE_STEP + _US_SEG_CORR_START + corr + _US_SEG_GAPS)
+    return prep + max_chunks * _US_CHAIN_CHUNK + _US_SPLIT_GAP
+
+
+def _plan(mode: str, lengths: tuple[int, ...], hv: int, dev: torch.device,
+          checkpoints: bool = False) -> tuple[str, int]:
+    """_plan_uncached, memoised per shape (the search over segment lengths is host work that a
+    repeated call should not pay again)."""
+    key = ("plan", _mode(mode), lengths, hv, dev, checkpoints)
+    hit = _meta_cache.get(key)
+    if hit is None:
+        hit = _plan_uncached(mode, lengths, hv, dev, checkpoints)
+        _meta_cache[key] = hit
+    return hit
+
+
+def _plan_uncached(mode: str, lengths: tuple[int, ...], hv: int, dev: torch.device,
+                   checkpoints: bool = False) -> tuple[str, int]:
+    """(schedule, segment length in chunks -- 0 unless "segmented").  "auto": "fused" when one
+    CTA per unit fills the SMs (or the workspace would be too large); otherwise the schedule with
+    the lowest predicted time (`_predicted_us`) among "fused", "overlap" (possible when the
+    chains leave at least 8 SMs to the preparation CTAs), "split" and "segmented" (possible when
+    some sequence is long enough to cut).  With checkpoints only "split" and "overlap" qualify."""
+    mode = _mode(mode)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    units = len(lengths) * hv
+    nch = [(n + 63) // 64 for n in lengths]
+    total_chunks, max_chunks = sum(nch), max(nch, default=0)
+    seg = segment_length(lengths, hv, sms) if not checkpoints else None
+    if mode != "auto":
+        if checkpoints and mode in ("fused", "segmented"):
+            raise ValueError(f"checkpoints need the split or overlap schedule (mode={mode!r} given)")
+        if mode == "segmented":
+            return mode, seg if seg is not None else max(max_chunks, 1)
+        return mode, 0
+    if not checkpoints and (units >= sms or
+                            _lib.load().tokmix_gdn_split_workspace_bytes(total_chunks, hv) > _SPLIT_MAX_WORKSPACE):
+        return "fused", 0
+    if units >= sms:
+        return "split", 0
+    records = total_chunks * hv
+    # ties go to the earlier entry: the single fused launch first
+    cands = ([] if checkpoints else ["fused"]) + (["overlap"] if units + 8 <= sms else []) + ["split"]
+    pred = {c: _predicted_us(c, units, records, max_chunks, sms) for c in cands}
+    if seg is not None:
+        seg_units, most, later = _segment_units(nch, seg)
+        pred["segmented"] = _predicted_us("segmented", seg_units * hv, records, seg, sms, most, later, hv)
+    best = min(pred, key=pred.get)
+    return best, seg if best == "segmented" else 0
 
 
 def _schedule(mode: str, units: int, total_chunks: int, hv: int, dev: torch.device,
               checkpoints: bool = False, max_chunks: int | None = None) -> str:
-    """"fused" when one CTA per unit fills the SMs (or the workspace would be too large);
-    otherwise the schedule with the lowest predicted time (`_predicted_us`) among "fused",
-    "overlap" (possible when the chains leave at least 8 SMs to the preparation CTAs) and "split".
-    With checkpoints only "split" and "overlap" qualify."""
-    mode = _mode(mode)
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    if mode != "auto":
-        if checkpoints and mode == "fused":
-            raise ValueError("checkpoints need the split or overlap schedule (mode='fused' given)")
-        return mode
-    if not checkpoints and (units >= sms or
-                            _lib.load().tokmix_gdn_split_workspace_bytes(total_chunks, hv) > _SPLIT_MAX_WORKSPACE):
-        return "fused"
-    if units >= sms:
-        return "split"
-    if max_chunks is None:
-        max_chunks = -(-total_chunks // max(1, units // hv))
-    records = total_chunks * hv
-    # ties go to the earlier entry: the single fused launch first
-    cands = ([] if checkpoints else ["fused"]) + (["overlap"] if units + 8 <= sms else []) + ["split"]
-    return min(cands, key=lambda c: _predicted_us(c, units, records, max_chunks, sms))
+    """The schedule for `units` / hv sequences of equal chunk counts (see _plan)."""
+    n = max(1, units // hv)
+    per = max_chunks if max_chunks is not None else -(-total_chunks // n)
+    return _plan(mode, (per * 64,) * n, hv, dev, checkpoints)[0]
 
 
 def schedule(q: torch.Tensor, v: torch.Tensor, cu_seqlens=None, mode: str = "auto") -> str:
-    """The schedule kernel_fn picks for these inputs: "fused", "split", "overlap" or "decode"."""
+    """The schedule kernel_fn picks for these inputs: "fused", "split", "overlap", "segmented"
+    or "decode"."""
     B, T, hv = q.shape[0], q.shape[1], v.shape[2]
     if cu_seqlens is None and T == 1 and B > 0 and _mode(mode) == "auto":
         return "decode"
     lengths = (T,) * B if cu_seqlens is None else _lengths(cu_seqlens, T)
-    chunks = sum((n + 63) // 64 for n in lengths)
-    return _schedule(mode, len(lengths) * hv, chunks, hv, q.device,
-                     max_chunks=max([(n + 63) // 64 for n in lengths] or [0]))
+    return _plan(mode, lengths, hv, q.device)[0]
 
 
 def check_device_status(device: torch.device | None = None) -> None:

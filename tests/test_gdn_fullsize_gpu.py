@@ -102,7 +102,7 @@ def long16k():
     return inp, _oracle(inp, os.cpu_count() or 1)
 
 
-@pytest.mark.parametrize("mode", ["auto", "fused", "split", "overlap"])
+@pytest.mark.parametrize("mode", ["auto", "fused", "split", "overlap", "segmented"])
 def test_gdn_long_sequence_16k(cuda_device, long16k, mode):
     """One sequence of 16384 tokens (256 chunks), every head, under each schedule."""
     inp, (ref_o, ref_s) = long16k
@@ -118,7 +118,7 @@ def long64k():
     return inp, _oracle(inp, os.cpu_count() or 1)
 
 
-@pytest.mark.parametrize("mode", ["auto", "fused", "split", "overlap"])
+@pytest.mark.parametrize("mode", ["auto", "fused", "split", "overlap", "segmented"])
 def test_gdn_long_sequence_64k(cuda_device, long64k, mode):
     """One sequence of 65536 tokens (1024 chunks), every head: the hybrid sweep's longest length."""
     inp, (ref_o, ref_s) = long64k

@@ -140,12 +140,12 @@ def test_gdn_config1_full(cuda_device, oracle_threads, mode):
 def test_gdn_state_continuation_is_exact(cuda_device):
     """Chunk-aligned split with the state handed over equals the one-shot run bit for bit."""
     inp = gcfg.random_inputs(1, 640, seed=8, state_std=0.02)
-    out, fs = gdn.kernel_fn(**inp)
+    out, fs = gdn.kernel_fn(**inp, mode="split")
     a = {k: (v[:, :256] if k in ("q", "k", "v", "g", "beta") else v) for k, v in inp.items()}
-    oa, sa = gdn.kernel_fn(**a)
+    oa, sa = gdn.kernel_fn(**a, mode="split")
     b = {k: (v[:, 256:] if k in ("q", "k", "v", "g", "beta") else v) for k, v in inp.items()}
     b["state"] = sa
-    ob, sb = gdn.kernel_fn(**b)
+    ob, sb = gdn.kernel_fn(**b, mode="split")
     assert torch.equal(torch.cat([oa, ob], dim=1), out)
     assert torch.equal(sb, fs)
 
@@ -159,10 +159,11 @@ def test_gdn_deterministic(cuda_device):
 
 def test_gdn_varlen_full_size(cuda_device, oracle_threads):
     """8 sequences, lengths ~U[1024, 32768], per-sequence initial state N(0, 0.02): the two
-    shortest sequences against the oracle, every sequence against its own one-sequence run."""
+    shortest sequences against the oracle, every sequence against its own one-sequence run (all
+    sequences against the oracle: tests/test_gdn_fullsize_gpu.py)."""
     lengths = gcfg.varlen_lengths(8, seed=0)
     inp = gcfg.random_inputs(1, 0, lengths=lengths, seed=0, state_std=0.02)
-    out, fs = gdn.kernel_fn(**inp)
+    out, fs = gdn.kernel_fn(**inp, mode="fused")
     gdn.check_device_status(cuda_device)
     cu = np.cumsum([0] + lengths)
     order = np.argsort(lengths)
@@ -170,7 +171,7 @@ def test_gdn_varlen_full_size(cuda_device, oracle_threads):
         a, b = int(cu[n]), int(cu[n + 1])
         one = {k: (v[:, a:b] if k in ("q", "k", "v", "g", "beta") else v) for k, v in inp.items() if k != "cu_seqlens"}
         one["state"] = inp["state"][n:n + 1]
-        o1, s1 = gdn.kernel_fn(**one)
+        o1, s1 = gdn.kernel_fn(**one, mode="fused")  # the same kernel on one sequence: bit for bit
         assert torch.equal(o1, out[:, a:b]) and torch.equal(s1[0], fs[n]), n
         if n in order[:2]:
             o_ref, s_ref = _oracle({**one}, oracle_threads)
