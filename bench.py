@@ -266,7 +266,9 @@ def run_gdn_varlen(device, rank, world, steps, warmup, verify=False):
            "token_heads": tokens * 2 * (b - a), "schedule": gdn.schedule(inp["q"], inp["v"], inp.get("cu_seqlens")),
            "config": {"workload": "gdn_varlen", "n_seqs": 8, "lengths": lengths, "total_tokens": tokens,
                       "hk": HK, "hv": HV, "head_dim": D, "chunk": 64, "initial_state": "N(0,0.02)",
-                      "shard": f"key heads {HK // world}/rank (+ the value heads reading them)"}}
+                      "shard": f"key heads {HK // world}/rank (+ the value heads reading them); the rank's "
+                               "schedule cuts long sequences into segments chained side by side when that is "
+                               "predicted faster"}}
     if verify and world > 1:
         out, fs = gdn.kernel_fn(**inp)
         go = sharding.gather_to_rank0(out, dim=2)
@@ -277,8 +279,20 @@ def run_gdn_varlen(device, rank, world, steps, warmup, verify=False):
             offs = [sum(sizes[:i]) for i in range(world)]
             o = sharding.unscatter_gdn_heads([go.narrow(2, o0, n) for o0, n in zip(offs, sizes)], ranges, HK, HV, 2)
             st = sharding.unscatter_gdn_heads([gs.narrow(1, o0, n) for o0, n in zip(offs, sizes)], ranges, HK, HV, 1)
-            res["verified_vs_one_gpu"] = bool(torch.equal(o, ref_o) and torch.equal(st, ref_s))
+            res.update(compare_gdn(o, st, ref_o, ref_s))
     return res
+
+
+def compare_gdn(o, st, ref_o, ref_s) -> dict:
+    """Gathered GDN outputs against a one-GPU run: bit for bit when both ran schedules that issue
+    the same operations (fused / split / overlap), else within the parity tests' tolerances (the
+    segmented schedule rounds its later segments' outputs once more)."""
+    bitwise = bool(torch.equal(o, ref_o) and torch.equal(st, ref_s))
+    close = bool(torch.allclose(o.float(), ref_o.float(), atol=2e-2, rtol=2e-2) and
+                 torch.allclose(st, ref_s, atol=1e-4, rtol=1e-3))
+    return {"verified_vs_one_gpu": bitwise or close, "bitwise_vs_one_gpu": bitwise,
+            "max_abs_diff_vs_one_gpu": {"out": float((o.float() - ref_o.float()).abs().max()),
+                                        "state": float((st - ref_s).abs().max())}}
 
 
 def run_gdn_decode(device, rank, world, steps, warmup, batch=128):
@@ -469,7 +483,7 @@ def run_gdn_heads(device, rank, world, steps, warmup, verify=False):
             offs = [sum(sizes[:i]) for i in range(world)]
             o = sharding.unscatter_gdn_heads([go.narrow(2, o0, n) for o0, n in zip(offs, sizes)], ranges, HK, HV, 2)
             st = sharding.unscatter_gdn_heads([gs.narrow(1, o0, n) for o0, n in zip(offs, sizes)], ranges, HK, HV, 1)
-            res["verified_vs_one_gpu"] = bool(torch.equal(o, ref_o) and torch.equal(st, ref_s))
+            res.update(compare_gdn(o, st, ref_o, ref_s))
     return res
 
 
@@ -756,7 +770,8 @@ def main():
             launches = args.steps * (2 if hr.get("schedule") == "split" else 1)
         if e2e is None and "e2e" in hr:
             e2e = hr["e2e"]
-        extra_keys = ("verified_vs_one_gpu", "e2e", "sdpa", "cpu_baseline", "parts")
+        extra_keys = ("verified_vs_one_gpu", "bitwise_vs_one_gpu", "max_abs_diff_vs_one_gpu", "e2e", "sdpa",
+                      "cpu_baseline", "parts")
         line = {"metric": metric, "value": hr["value"], "unit": hr["unit"], "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": hr["ms"], "higher_is_better": True,
                 "scaling": "weak" if head in ("gdn_b1_t2048", "gdn_b4_t2048") else "strong", "vs_baseline": None,

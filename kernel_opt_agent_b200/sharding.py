@@ -10,8 +10,6 @@ outputs (and final states) to rank 0 for verification, outside any timed region.
 
 from __future__ import annotations
 
-import heapq
-
 import torch
 import torch.distributed as dist
 
@@ -62,17 +60,6 @@ def slice_fa2_inputs(inp: dict, a: int, b: int) -> dict:
     out["k"] = inp["k"].narrow(hd, a, b - a).contiguous()
     out["v"] = inp["v"].narrow(hd, a, b - a).contiguous()
     return out
-
-
-def lpt_assign(costs: list[float], world: int) -> list[list[int]]:
-    """Longest-processing-time-first assignment of units (by cost) to `world` ranks."""
-    heap = [(0.0, r) for r in range(world)]
-    bins: list[list[int]] = [[] for _ in range(world)]
-    for u in sorted(range(len(costs)), key=lambda i: -costs[i]):
-        load, r = heapq.heappop(heap)
-        bins[r].append(u)
-        heapq.heappush(heap, (load + costs[u], r))
-    return bins
 
 
 def gather_to_rank0(local: torch.Tensor, dim: int):

@@ -50,15 +50,6 @@ def test_gdn_slice_equals_heads_of_full_run():
     np.testing.assert_array_equal(s.numpy(), s_full)
 
 
-def test_lpt_balances_varlen_units():
-    lengths = gcfg.varlen_lengths(8, seed=0)
-    costs = [float(n) for n in lengths for _ in range(32)]  # (sequence, value head) units
-    bins = sharding.lpt_assign(costs, 8)
-    loads = [sum(costs[u] for u in b) for b in bins]
-    assert sorted(u for b in bins for u in b) == list(range(len(costs)))
-    assert max(loads) / (sum(loads) / 8) < 1.02
-
-
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
