@@ -69,6 +69,22 @@ int tokmix_fa2_fwd(const void* q, const void* k, const void* v, void* o, int bat
                    int seqlen_q, int seqlen_kv, int head_dim, int layout, int causal, float sm_scale,
                    uint32_t* status, void* stream);
 
+/* The Qwen3.5 gated-delta-net gates from the raw projections, for the GDN prefill entry points'
+ * `gates` argument: when given, the kernels compute g and beta themselves while preparing each
+ * chunk (and their g, beta arguments are ignored):
+ *   g = -exp(a_log[h]) * softplus(a + dt_bias[h]),  beta = sigmoid(b)      (fp32 arithmetic)
+ * a, b: device [total_tokens, heads_v] in `dtype` (TOKMIX_DTYPE_BF16 or TOKMIX_DTYPE_FP32);
+ * a_log, dt_bias: device fp32 [heads_v].  The arithmetic is tokmix_gdn_gates' own, so the results
+ * equal those of running tokmix_gdn_gates first, bit for bit.  The reference takes g and beta
+ * ready-made (kernels/qwen35moe_gdn_prefill.py:107-136). */
+typedef struct tokmix_gdn_gate_inputs {
+  const void* a;
+  const void* b;
+  int dtype;
+  const float* a_log;
+  const float* dt_bias;
+} tokmix_gdn_gate_inputs;
+
 /* Gated-delta-rule (GDN) prefill, chunked on the tensor cores.
  *
  * Token layout: q, k [total_tokens, heads_k, 128]; v, out [total_tokens, heads_v, 128];
@@ -79,6 +95,7 @@ int tokmix_fa2_fwd(const void* q, const void* k, const void* v, void* o, int bat
  * (initial_state may be NULL for a zero initial state; final_state may alias initial_state).
  * Value head h reads key head h % heads_k (as kernels/qwen35moe_gdn_prefill.cu:48).
  * io_dtype is the type of q, k, v and out: TOKMIX_DTYPE_BF16 (the only one this build runs).
+ * gates: NULL (g and beta as given), or the raw projections to compute them from (above).
  *
  * cu_seqlens_dev:   device int32 [num_seqs + 1]
  * seq_order_dev:    device int32 [num_seqs], the order in which sequences are scheduled
@@ -88,7 +105,8 @@ int tokmix_fa2_fwd(const void* q, const void* k, const void* v, void* o, int bat
 int tokmix_gdn_prefill(const void* q, const void* k, const void* v, const float* g, const float* beta,
                        const float* initial_state, void* out, float* final_state, const int32_t* cu_seqlens_dev,
                        const int32_t* seq_order_dev, int num_seqs, int total_tokens, int heads_k, int heads_v,
-                       int head_dim_k, int head_dim_v, float scale, int io_dtype, uint32_t* status, void* stream);
+                       int head_dim_k, int head_dim_v, float scale, int io_dtype, const tokmix_gdn_gate_inputs* gates,
+                       uint32_t* status, void* stream);
 
 /* Gated-delta-rule prefill for a batch of equal-length sequences that allocates nothing.
  *
@@ -141,8 +159,8 @@ int tokmix_gdn_prefill_split(const void* q, const void* k, const void* v, const 
                              const float* initial_state, void* out, float* final_state, float* checkpoints,
                              const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev, const int32_t* record_order_dev, int num_seqs,
                              int total_tokens, int total_chunks, int heads_k, int heads_v, int head_dim_k,
-                             int head_dim_v, float scale, int io_dtype, void* workspace, long long workspace_bytes,
-                             uint32_t* status, void* stream);
+                             int head_dim_v, float scale, int io_dtype, const tokmix_gdn_gate_inputs* gates,
+                             void* workspace, long long workspace_bytes, uint32_t* status, void* stream);
 
 /* Workspace size of tokmix_gdn_prefill_split in bytes (-1 for negative arguments). */
 long long tokmix_gdn_split_workspace_bytes(int total_chunks, int heads_v);
@@ -178,8 +196,8 @@ int tokmix_gdn_prefill_segmented(const void* q, const void* k, const void* v, co
                                  const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev,
                                  const int32_t* cu_seqlens_host, int num_seqs, int total_tokens, int total_chunks,
                                  int heads_k, int heads_v, int head_dim_k, int head_dim_v, float scale, int io_dtype,
-                                 int max_segment_chunks, const void* plan_dev, void* workspace,
-                                 long long workspace_bytes, uint32_t* status, void* stream);
+                                 const tokmix_gdn_gate_inputs* gates, int max_segment_chunks, const void* plan_dev,
+                                 void* workspace, long long workspace_bytes, uint32_t* status, void* stream);
 
 /* Workspace size of tokmix_gdn_prefill_segmented in bytes (-1 for inconsistent arguments). */
 long long tokmix_gdn_segmented_workspace_bytes(const int32_t* cu_seqlens_host, int num_seqs, int heads_v,

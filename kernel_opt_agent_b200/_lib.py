@@ -45,14 +45,14 @@ _F = ctypes.c_float
 SIGNATURES = {
     "tokmix_fa2_fwd": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _F, _VP, _VP]),
     "tokmix_gdn_prefill": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _F, _I, _VP,
-                                _VP]),
+                                _VP, _VP]),
     "tokmix_gdn_prefill_noalloc": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _F, _I, _VP,
                                         _VP]),
     "tokmix_gdn_prefill_split": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I,
-                                      _I, _I, _F, _I, _VP, ctypes.c_longlong, _VP, _VP]),
+                                      _I, _I, _F, _I, _VP, _VP, ctypes.c_longlong, _VP, _VP]),
     "tokmix_gdn_noalloc_status": (_I, [_VP, _I]),
     "tokmix_gdn_prefill_segmented": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I,
-                                          _I, _I, _F, _I, _I, _VP, _VP, ctypes.c_longlong, _VP, _VP]),
+                                          _I, _I, _F, _I, _VP, _I, _VP, _VP, ctypes.c_longlong, _VP, _VP]),
     "tokmix_gdn_segmented_workspace_bytes": (ctypes.c_longlong, [_VP, _I, _I, _I]),
     "tokmix_gdn_segmented_plan_bytes": (ctypes.c_longlong, [_VP, _I, _I, _I]),
     "tokmix_gdn_segmented_plan": (_I, [_VP, _I, _I, _I, _VP, ctypes.c_longlong]),
@@ -67,6 +67,13 @@ SIGNATURES = {
     "tokmix_last_error": (ctypes.c_char_p, []),
     "tokmix_version": (ctypes.c_char_p, []),
 }
+
+class GateInputs(ctypes.Structure):
+    """tokmix_gdn_gate_inputs: the raw gate projections the GDN kernels compute g and beta from."""
+
+    _fields_ = [("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("dtype", ctypes.c_int),
+                ("a_log", ctypes.c_void_p), ("dt_bias", ctypes.c_void_p)]
+
 
 _lib = None
 _lock = threading.Lock()

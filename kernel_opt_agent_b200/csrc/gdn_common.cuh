@@ -14,6 +14,38 @@ constexpr int kC = 64;    // tokens per chunk
 constexpr int kD = 128;   // head dim (keys and values)
 constexpr int kLds = 68;  // fp32 row stride of the solve matrices L and X (64 + 4: conflict-free rows)
 
+// Where a chunk's gates come from: g and beta as given, or -- when `a` is not null -- the
+// Qwen3.5 gated-delta-net gates computed from the raw projections a, b [tokens, heads_v] (bf16
+// or fp32) and the per-head A_log, dt_bias, with the same arithmetic as the separate gates pass
+// (gdn_preprocess.cu), so both routes give the same bits:
+//   g = -exp(A_log[h]) softplus(a + dt_bias[h]),   beta = sigmoid(b)
+struct GateSource {
+  const void* a;
+  const void* b;
+  const float* a_log;
+  const float* dt_bias;
+  int bf16;  // a, b are bf16 (else fp32)
+};
+
+// softplus(x) = log(1 + e^x); for x > 20, e^x exceeds 4e8 and log(1 + e^x) equals x in fp32
+__device__ __forceinline__ float gate_softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// g and beta of element idx (= token * heads_v + h)
+__device__ __forceinline__ void load_gates(const float* g, const float* beta, const GateSource& gs, size_t idx, int h,
+                                           float& gv, float& bv) {
+  if (gs.a == nullptr) {
+    gv = g[idx];
+    bv = beta[idx];
+    return;
+  }
+  const float a = gs.bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(gs.a)[idx])
+                          : static_cast<const float*>(gs.a)[idx];
+  const float b = gs.bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(gs.b)[idx])
+                          : static_cast<const float*>(gs.b)[idx];
+  gv = -expf(gs.a_log[h]) * gate_softplus(a + gs.dt_bias[h]);
+  bv = 1.0f / (1.0f + expf(-b));
+}
+
 struct ChunkParams {
   float beta[kC];  // write strength (0 for tokens past the sequence end)
   float g2[kC];    // in-chunk inclusive prefix sum of g, in log2 units

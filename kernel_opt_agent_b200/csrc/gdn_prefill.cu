@@ -87,6 +87,7 @@ struct Params {
   int num_seqs, total_tokens;
   float scale;
   uint32_t* status;
+  GateSource gates;  // a == null: g and beta as given
 };
 
 // Hand-off barriers.  Event of chunk c lives in slot c & 1 (in_full: c % 3) and completes the
@@ -485,10 +486,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n_valid = min(kC, len - c * kC);
       const int t0 = 2 * lane, t1 = 2 * lane + 1;
       const size_t base = static_cast<size_t>(tok0 + c * kC);
-      ga = t0 < n_valid ? p.g[(base + t0) * p.hv + h] : 0.0f;
-      gb = t1 < n_valid ? p.g[(base + t1) * p.hv + h] : 0.0f;
-      ba = t0 < n_valid ? p.beta[(base + t0) * p.hv + h] : 0.0f;
-      bb = t1 < n_valid ? p.beta[(base + t1) * p.hv + h] : 0.0f;
+      ga = gb = ba = bb = 0.0f;
+      if (t0 < n_valid) load_gates(p.g, p.beta, p.gates, (base + t0) * p.hv + h, h, ga, ba);
+      if (t1 < n_valid) load_gates(p.g, p.beta, p.gates, (base + t1) * p.hv + h, h, gb, bb);
     };
     if (warp == 7) load_g(0);
     unsigned long long idle_since = 0;
@@ -706,9 +706,14 @@ namespace gdn {
 static int validate_prefill_args(const char* who, const void* q, const void* k, const void* v, const float* g,
                                  const float* beta, const float* initial_state, const void* out,
                                  const float* final_state, int num_seqs, int total_tokens, int heads_k, int heads_v,
-                                 int head_dim_k, int head_dim_v, float scale, int io_dtype) {
-  if (!q || !k || !v || !g || !beta || !out || !final_state)
+                                 int head_dim_k, int head_dim_v, float scale, int io_dtype,
+                                 const tokmix_gdn_gate_inputs* gates = nullptr) {
+  if (!q || !k || !v || !out || !final_state || (gates == nullptr && (!g || !beta)))
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: null pointer argument", who);
+  if (gates != nullptr &&
+      (!gates->a || !gates->b || !gates->a_log || !gates->dt_bias ||
+       (gates->dtype != TOKMIX_DTYPE_BF16 && gates->dtype != TOKMIX_DTYPE_FP32)))
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: gates need a, b, a_log, dt_bias and a bf16 or fp32 dtype", who);
   if (num_seqs < 0 || total_tokens < 0 || heads_k <= 0 || heads_v <= 0)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: negative or zero size", who);
   if (heads_v % heads_k != 0)
@@ -732,12 +737,13 @@ extern "C" int tokmix_gdn_prefill(const void* q, const void* k, const void* v, c
                                   const float* initial_state, void* out, float* final_state,
                                   const int32_t* cu_seqlens_dev, const int32_t* seq_order_dev, int num_seqs,
                                   int total_tokens, int heads_k, int heads_v, int head_dim_k, int head_dim_v,
-                                  float scale, int io_dtype, uint32_t* status, void* stream) {
+                                  float scale, int io_dtype, const tokmix_gdn_gate_inputs* gates, uint32_t* status,
+                                  void* stream) {
   using namespace tokmix;
   using namespace tokmix::gdn;
   if (const int rc = validate_prefill_args("tokmix_gdn_prefill", q, k, v, g, beta, initial_state, out, final_state,
                                            num_seqs, total_tokens, heads_k, heads_v, head_dim_k, head_dim_v, scale,
-                                           io_dtype))
+                                           io_dtype, gates))
     return rc;
   if (cu_seqlens_dev == nullptr)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill: null pointer argument");
@@ -777,6 +783,8 @@ extern "C" int tokmix_gdn_prefill(const void* q, const void* k, const void* v, c
   p.hv = heads_v;
   p.num_seqs = num_seqs;
   p.total_tokens = total_tokens;
+  if (gates != nullptr)
+    p.gates = GateSource{gates->a, gates->b, gates->a_log, gates->dt_bias, gates->dtype == TOKMIX_DTYPE_BF16 ? 1 : 0};
   p.scale = scale;
   p.status = status;
   const int smem_bytes = kSmemBytes + 1024;
@@ -872,7 +880,7 @@ extern "C" int tokmix_gdn_prefill_noalloc(const void* q, const void* k, const vo
   na::fill_offsets<<<(batch + 1 + 255) / 256, 256, 0, s>>>(offsets, batch, seqlen, status != nullptr ? nullptr : st);
   if (const int rc = check_launch("tokmix_gdn_prefill_noalloc")) return rc;
   return tokmix_gdn_prefill(q, k, v, g, beta, initial_state, out, final_state, offsets, nullptr, batch, batch * seqlen,
-                            heads_k, heads_v, head_dim_k, head_dim_v, scale, io_dtype, st, stream);
+                            heads_k, heads_v, head_dim_k, head_dim_v, scale, io_dtype, nullptr, st, stream);
 }
 
 // Reads the library-owned status word of the current device that tokmix_gdn_prefill_noalloc

@@ -17,6 +17,7 @@
 #include <cmath>
 #include <cstdint>
 
+#include "gdn_common.cuh"
 #include "host_common.h"
 
 namespace tokmix {
@@ -69,28 +70,18 @@ __global__ void __launch_bounds__(kWarps * 32) l2norm_rows_kernel(const T* x, __
 }
 
 template <typename T>
-__device__ __forceinline__ float as_float(T x);
-template <>
-__device__ __forceinline__ float as_float<float>(float x) {
-  return x;
-}
-template <>
-__device__ __forceinline__ float as_float<__nv_bfloat16>(__nv_bfloat16 x) {
-  return __bfloat162float(x);
-}
-
-// softplus(x) = log(1 + e^x); for x > 20, e^x exceeds 4e8 and log(1 + e^x) equals x in fp32
-__device__ __forceinline__ float softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
-
-template <typename T>
 __global__ void __launch_bounds__(256) gdn_gates_kernel(const T* a, const T* b, const float* a_log,
                                                         const float* dt_bias, float* g, float* beta, long long n,
                                                         int hv) {
   const long long i = static_cast<long long>(blockIdx.x) * 256 + threadIdx.x;
   if (i >= n) return;
   const int h = static_cast<int>(i % hv);
-  g[i] = -expf(a_log[h]) * softplus(as_float<T>(a[i]) + dt_bias[h]);
-  beta[i] = 1.0f / (1.0f + expf(-as_float<T>(b[i])));
+  // the same arithmetic as the GDN kernels' own gate loads (gdn_common.cuh: load_gates)
+  gdn::GateSource gs{a, b, a_log, dt_bias, sizeof(T) == 2 ? 1 : 0};
+  float gv, bv;
+  gdn::load_gates(nullptr, nullptr, gs, static_cast<size_t>(i), h, gv, bv);
+  g[i] = gv;
+  beta[i] = bv;
 }
 
 }  // namespace preprocess

@@ -111,6 +111,7 @@ struct PrepParams {
   int total_tokens;
   float scale;
   uint32_t* status;
+  GateSource gates;  // a == null: g and beta as given
 };
 
 // A chain unit of the segmented schedule: `nchunks` chunks of sequence `seq` from its chunk
@@ -195,10 +196,9 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
   if (warp == 3) {
     const int t0 = 2 * lane, t1 = 2 * lane + 1;
     const size_t base = static_cast<size_t>(row0);
-    const float ga = t0 < n_valid ? p.g[(base + t0) * p.hv + h] : 0.0f;
-    const float gb = t1 < n_valid ? p.g[(base + t1) * p.hv + h] : 0.0f;
-    const float ba = t0 < n_valid ? p.beta[(base + t0) * p.hv + h] : 0.0f;
-    const float bb = t1 < n_valid ? p.beta[(base + t1) * p.hv + h] : 0.0f;
+    float ga = 0.0f, gb = 0.0f, ba = 0.0f, bb = 0.0f;
+    if (t0 < n_valid) load_gates(p.g, p.beta, p.gates, (base + t0) * p.hv + h, h, ga, ba);
+    if (t1 < n_valid) load_gates(p.g, p.beta, p.gates, (base + t1) * p.hv + h, h, gb, bb);
     chunk_decay_params(pc, ga, gb, ba, bb, n_valid, lane);
   }
   named_sync(bar_id, 128);
@@ -863,6 +863,19 @@ namespace tokmix {
 namespace gdn {
 namespace split {
 
+static int check_gate_inputs(const char* who, const tokmix_gdn_gate_inputs* gates) {
+  if (gates != nullptr &&
+      (!gates->a || !gates->b || !gates->a_log || !gates->dt_bias ||
+       (gates->dtype != TOKMIX_DTYPE_BF16 && gates->dtype != TOKMIX_DTYPE_FP32)))
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: gates need a, b, a_log, dt_bias and a bf16 or fp32 dtype", who);
+  return TOKMIX_OK;
+}
+
+static GateSource gate_source(const tokmix_gdn_gate_inputs* gates) {
+  if (gates == nullptr) return GateSource{};
+  return GateSource{gates->a, gates->b, gates->a_log, gates->dt_bias, gates->dtype == TOKMIX_DTYPE_BF16 ? 1 : 0};
+}
+
 // TMA maps over q, k [tokens, heads_k, 128] and v [tokens, heads_v, 128] (bf16); boxes of 64
 // columns x 1 head x 64 tokens, 128-byte swizzle.
 static bool encode_qkv_maps(const void* q, const void* k, const void* v, int total_tokens, int heads_k, int heads_v,
@@ -894,7 +907,8 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
                                         float* checkpoints, const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev,
                                         const int32_t* record_order_dev, int num_seqs, int total_tokens,
                                         int total_chunks, int heads_k, int heads_v, int head_dim_k,
-                                        int head_dim_v, float scale, int io_dtype, void* workspace,
+                                        int head_dim_v, float scale, int io_dtype,
+                                        const tokmix_gdn_gate_inputs* gates, void* workspace,
                                         long long workspace_bytes, uint32_t* status, void* stream) {
   using namespace tokmix;
   using namespace tokmix::gdn;
@@ -902,8 +916,10 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   if (num_seqs < 0 || total_tokens < 0 || total_chunks < 0 || heads_k <= 0 || heads_v <= 0)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: negative or zero size");
   if (num_seqs == 0) return TOKMIX_OK;
-  if (!q || !k || !v || !g || !beta || !out || !final_state || !cu_seqlens_dev || !chunk_base_dev || !status)
+  if (!q || !k || !v || !out || !final_state || !cu_seqlens_dev || !chunk_base_dev || !status ||
+      (gates == nullptr && (!g || !beta)))
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: null pointer argument");
+  if (const int rc = check_gate_inputs("tokmix_gdn_prefill_split", gates)) return rc;
   if (heads_v % heads_k != 0)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT,
                 "tokmix_gdn_prefill_split: heads_v (%d) must be a multiple of heads_k (%d)", heads_v, heads_k);
@@ -942,6 +958,7 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   pp.hv = heads_v;
   pp.scale = scale;
   pp.status = status;
+  pp.gates = gate_source(gates);
   ChainParams cp{};
   cp.state_in = initial_state;
   cp.state_out = final_state;
@@ -1159,8 +1176,9 @@ extern "C" int tokmix_gdn_prefill_segmented(const void* q, const void* k, const 
                                             const int32_t* chunk_base_dev, const int32_t* cu_seqlens_host,
                                             int num_seqs, int total_tokens, int total_chunks, int heads_k, int heads_v,
                                             int head_dim_k, int head_dim_v, float scale, int io_dtype,
-                                            int max_segment_chunks, const void* plan_dev, void* workspace,
-                                            long long workspace_bytes, uint32_t* status, void* stream) {
+                                            const tokmix_gdn_gate_inputs* gates, int max_segment_chunks,
+                                            const void* plan_dev, void* workspace, long long workspace_bytes,
+                                            uint32_t* status, void* stream) {
   using namespace tokmix;
   using namespace tokmix::gdn;
   using namespace tokmix::gdn::split;
@@ -1168,8 +1186,10 @@ extern "C" int tokmix_gdn_prefill_segmented(const void* q, const void* k, const 
   if (num_seqs < 0 || total_tokens < 0 || total_chunks < 0 || heads_k <= 0 || heads_v <= 0)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: negative or zero size", who);
   if (num_seqs == 0) return TOKMIX_OK;
-  if (!q || !k || !v || !g || !beta || !out || !final_state || !cu_seqlens_dev || !chunk_base_dev || !status)
+  if (!q || !k || !v || !out || !final_state || !cu_seqlens_dev || !chunk_base_dev || !status ||
+      (gates == nullptr && (!g || !beta)))
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: null pointer argument", who);
+  if (const int rc = check_gate_inputs(who, gates)) return rc;
   if (heads_v % heads_k != 0)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: heads_v (%d) must be a multiple of heads_k (%d)", who, heads_v, heads_k);
   if (head_dim_k != kD || head_dim_v != kD)
@@ -1237,6 +1257,7 @@ extern "C" int tokmix_gdn_prefill_segmented(const void* q, const void* k, const 
   pp.hv = heads_v;
   pp.scale = scale;
   pp.status = status;
+  pp.gates = gate_source(gates);
   if (total_chunks > 0) {
     const int smem = kPSmem + 1024;
     if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_prep_kernel), smem))

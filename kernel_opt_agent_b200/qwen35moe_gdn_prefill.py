@@ -29,7 +29,9 @@ Extensions over the reference module:
 * ``gates`` (keyword, default None): ``(A_log, dt_bias)`` ([Hv] each) to pass the raw gate
   projections instead of g and beta: the ``g`` and ``beta`` arguments then hold the projections
   a and b, and ``g = -exp(A_log) * softplus(a + dt_bias)``, ``beta = sigmoid(b)`` are computed on
-  the device first (``gdn_gates``), as Qwen3.5's GDN layer does before its kernel.
+  the device by the preparation of each chunk inside the prefill kernels (the same arithmetic as
+  the separate pass ``gdn_gates``, so the results are the same bits), as Qwen3.5's GDN layer does
+  before its kernel; the decode step runs the separate pass.
 * ``checkpoints`` (keyword, default False): also return the state after every 64-token chunk
   as a third output -- [B, ceil(T/64), Hv, 128, 128] fp32 for a batch, [total_chunks, Hv, 128,
   128] with cu_seqlens (sequence n's chunks from ``sum(ceil(len_m/64) for m < n)``) -- for prefix
@@ -175,8 +177,6 @@ def kernel_fn(
     segment_chunks: int | None = None,
 ) -> list[torch.Tensor]:
     nseq, hk, hv = _validate(q, k, v, g, beta, state, cu_seqlens)
-    if gates is not None:
-        g, beta = gdn_gates(g, beta, *gates)
     if scale is None:
         scale = D ** -0.5
     dev = q.device
@@ -186,8 +186,13 @@ def kernel_fn(
     if cu_seqlens is None and T == 1 and B > 0 and _mode(mode) == "auto":
         from . import qwen35moe_gdn_decode
 
+        if gates is not None:
+            g, beta = gdn_gates(g, beta, *gates)
         res = qwen35moe_gdn_decode.kernel_fn(q, k, v, g, beta, state, scale, qk_l2norm=qk_l2norm)
         return res + [res[1].unsqueeze(1).clone()] if checkpoints else res
+    gate_in = None
+    if gates is not None:  # the preparation of each chunk computes g and beta from the projections
+        gate_in, gate_keep = _gate_inputs(g, beta, gates, hv)
     if cu_seqlens is None:
         lengths = (T,) * B
     else:
@@ -203,13 +208,14 @@ def kernel_fn(
     qb = l2norm_rows(q) if qk_l2norm else q.to(torch.bfloat16).contiguous()
     kb = l2norm_rows(k) if qk_l2norm else k.to(torch.bfloat16).contiguous()
     vb = v.to(torch.bfloat16).contiguous()
-    gf = g.to(torch.float32).contiguous()
-    bf = beta.to(torch.float32).contiguous()
+    gf = g.to(torch.float32).contiguous() if gate_in is None else None
+    bf = beta.to(torch.float32).contiguous() if gate_in is None else None
     st = state.to(torch.float32).contiguous() if state is not None else None
     out = torch.empty(vb.shape, dtype=torch.bfloat16, device=dev)
     final_state = torch.empty((nseq, hv, D, D), dtype=torch.float32, device=dev)
     lib = _lib.load()
     word = _lib.status_word(dev)
+    gate_ref = ctypes.byref(gate_in) if gate_in is not None else None
     sched, seg_len = _plan(mode, lengths, hv, dev, checkpoints)
     if sched == "segmented" and segment_chunks is not None:
         if int(segment_chunks) < 1:
@@ -225,27 +231,28 @@ def kernel_fn(
             ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
             plan_t = _segment_plan(lengths, cu_host, hv, seg_len, dev)
             rc = lib.tokmix_gdn_prefill_segmented(
-                qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
+                qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), _ptr(gf), _ptr(bf),
                 st.data_ptr() if st is not None else None, out.data_ptr(), final_state.data_ptr(),
                 cu_t.data_ptr(), cb_t.data_ptr(), cu_host, nseq, total, total_chunks, hk, hv, D, D, float(scale),
-                _lib.DTYPE_BF16, seg_len, plan_t.data_ptr(), ws.data_ptr(), ws.numel(), word.data_ptr(),
+                _lib.DTYPE_BF16, gate_ref, seg_len, plan_t.data_ptr(), ws.data_ptr(), ws.numel(), word.data_ptr(),
                 _lib.stream_ptr(dev))
         elif sched != "fused":
             nbytes = int(lib.tokmix_gdn_split_workspace_bytes(total_chunks, hv))
             ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
             rec_t = _record_order(lengths, cb_host, hv, dev) if sched == "overlap" else None
             rc = lib.tokmix_gdn_prefill_split(
-                qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
+                qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), _ptr(gf), _ptr(bf),
                 st.data_ptr() if st is not None else None, out.data_ptr(), final_state.data_ptr(),
                 ck.data_ptr() if ck is not None else None, cu_t.data_ptr(), cb_t.data_ptr(), rec_t.data_ptr() if rec_t is not None else None, nseq, total,
-                total_chunks, hk, hv, D, D, float(scale), _lib.DTYPE_BF16, ws.data_ptr(), ws.numel(),
+                total_chunks, hk, hv, D, D, float(scale), _lib.DTYPE_BF16, gate_ref, ws.data_ptr(), ws.numel(),
                 word.data_ptr(), _lib.stream_ptr(dev))
         else:
             rc = lib.tokmix_gdn_prefill(
-                qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), gf.data_ptr(), bf.data_ptr(),
+                qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), _ptr(gf), _ptr(bf),
                 st.data_ptr() if st is not None else None, out.data_ptr(), final_state.data_ptr(),
                 cu_t.data_ptr(), order_t.data_ptr() if order_t is not None else None,
-                nseq, total, hk, hv, D, D, float(scale), _lib.DTYPE_BF16, word.data_ptr(), _lib.stream_ptr(dev))
+                nseq, total, hk, hv, D, D, float(scale), _lib.DTYPE_BF16, gate_ref, word.data_ptr(),
+                _lib.stream_ptr(dev))
     _lib.check(rc, "qwen35moe_gdn_prefill")
     _lib.after_launch(dev, "qwen35moe_gdn_prefill")
     if io_dtype != torch.bfloat16:
@@ -253,6 +260,26 @@ def kernel_fn(
     if ck is not None:
         return [out, final_state, ck if cu_seqlens is not None else ck.reshape(B, total_chunks // B, hv, D, D)]
     return [out, final_state]
+
+
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def _gate_inputs(a: torch.Tensor, b: torch.Tensor, gates, hv: int):
+    """The raw gate projections and per-head parameters as the kernels' gate source (and the
+    tensors that must stay alive until the launch)."""
+    a_log, dt_bias = gates
+    if a.shape != b.shape or a.dtype != b.dtype or a.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("gates: a and b must be tensors of one shape and dtype (bf16 or fp32)")
+    if tuple(a_log.shape) != (hv,) or tuple(dt_bias.shape) != (hv,):
+        raise ValueError(f"gates: A_log and dt_bias must have shape [{hv}]")
+    a, b = a.contiguous(), b.contiguous()
+    al = a_log.to(device=a.device, dtype=torch.float32).contiguous()
+    db = dt_bias.to(device=a.device, dtype=torch.float32).contiguous()
+    src = _lib.GateInputs(a.data_ptr(), b.data_ptr(), _lib.DTYPE_BF16 if a.dtype == torch.bfloat16 else _lib.DTYPE_FP32,
+                          al.data_ptr(), db.data_ptr())
+    return src, (a, b, al, db)
 
 
 def gdn_gates(a: torch.Tensor, b: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor):

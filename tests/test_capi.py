@@ -57,7 +57,8 @@ def test_gdn_rejects_bad_arguments():
     lib = _lib.load()
     p = ctypes.c_void_p(16)
     # every call below is rejected (or is a no-op) before anything is launched
-    args = [p, p, p, p, p, None, p, p, p, None, 1, 64, 16, 32, 128, 128, 0.08, 0, p, None]
+    # q k v g beta state out final cu order nseq tokens hk hv dk dv scale io gates status stream
+    args = [p, p, p, p, p, None, p, p, p, None, 1, 64, 16, 32, 128, 128, 0.08, 0, None, p, None]
     bad = list(args)
     bad[0] = None
     assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "null" in _lib.last_error()
@@ -71,8 +72,17 @@ def test_gdn_rejects_bad_arguments():
     bad[17] = 1  # fp32 io
     assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_UNSUPPORTED
     bad = list(args)
-    bad[18] = None  # status word required
+    bad[19] = None  # status word required
     assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    bad = list(args)
+    bad[3] = bad[4] = None  # g and beta missing without gate inputs
+    assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "null" in _lib.last_error()
+    gates = _lib.GateInputs(16, 16, 5, 16, 16)  # unknown dtype
+    bad[18] = ctypes.byref(gates)
+    assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "gates" in _lib.last_error()
+    gates = _lib.GateInputs(16, None, 0, 16, 16)  # b missing
+    bad[18] = ctypes.byref(gates)
+    assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "gates" in _lib.last_error()
     bad = list(args)
     bad[10] = 0  # no sequences: no-op
     assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_OK
@@ -100,14 +110,14 @@ def test_gdn_split_rejects_bad_arguments():
     need = lib.tokmix_gdn_split_workspace_bytes(32, 32)
     assert need >= 32 * 32 * 4 * 1024 and need % 16 == 0  # records plus one flag word per record
     assert lib.tokmix_gdn_split_workspace_bytes(-1, 32) == -1
-    # q k v g beta state out final checkpoints cu chunk_base order nseq tokens chunks hk hv dk dv scale io ws ws_bytes
-    # status stream
-    args = [p, p, p, p, p, None, p, p, None, p, p, None, 1, 2048, 32, 16, 32, 128, 128, 0.08, 0, p, need, p, None]
+    # q k v g beta state out final checkpoints cu chunk_base order nseq tokens chunks hk hv dk dv scale io gates ws
+    # ws_bytes status stream
+    args = [p, p, p, p, p, None, p, p, None, p, p, None, 1, 2048, 32, 16, 32, 128, 128, 0.08, 0, None, p, need, p, None]
     bad = list(args)
     bad[10] = None  # chunk_base
     assert lib.tokmix_gdn_prefill_split(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "null" in _lib.last_error()
     bad = list(args)
-    bad[22] = need - 16  # workspace too small
+    bad[23] = need - 16  # workspace too small
     assert lib.tokmix_gdn_prefill_split(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "workspace" in _lib.last_error()
     bad = list(args)
     bad[17] = 64  # head dim
@@ -209,3 +219,35 @@ def test_qkv_part_rope_rejects_bad_arguments():
     assert call(sin=None) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
     assert call(out=ctypes.c_void_p(24)) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
     assert call(seq=0) == _lib.TOKMIX_OK
+
+
+def test_gdn_segmented_rejects_bad_arguments():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    cu = (ctypes.c_int32 * 3)(0, 5000, 9000)
+    need = lib.tokmix_gdn_segmented_workspace_bytes(cu, 2, 32, 16)
+    assert need > 0 and need % 256 == 0
+    assert lib.tokmix_gdn_segmented_plan_bytes(cu, 2, 32, 16) > 0
+    assert lib.tokmix_gdn_segmented_workspace_bytes(cu, 2, 32, 0) == -1
+    backwards = (ctypes.c_int32 * 3)(0, 5000, 4000)
+    assert lib.tokmix_gdn_segmented_workspace_bytes(backwards, 2, 32, 16) == -1
+    chunks = (5000 + 63) // 64 + (4000 + 63) // 64
+    # q k v g beta state out final cu chunk_base cu_host nseq tokens chunks hk hv dk dv scale io gates seg plan ws
+    # ws_bytes status stream
+    args = [p, p, p, p, p, None, p, p, p, p, cu, 2, 9000, chunks, 16, 32, 128, 128, 0.08, 0, None, 16, None, p, need,
+            p, None]
+    bad = list(args)
+    bad[13] = chunks + 1  # chunk count disagrees with the host offsets
+    assert lib.tokmix_gdn_prefill_segmented(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    bad = list(args)
+    bad[24] = need - 256  # workspace too small
+    assert lib.tokmix_gdn_prefill_segmented(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "workspace" in _lib.last_error()
+    bad = list(args)
+    bad[21] = 0  # segment length
+    assert lib.tokmix_gdn_prefill_segmented(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    bad = list(args)
+    bad[10] = backwards
+    assert lib.tokmix_gdn_prefill_segmented(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT
+    bad = list(args)
+    bad[11] = 0  # no sequences: no-op
+    assert lib.tokmix_gdn_prefill_segmented(*bad) == _lib.TOKMIX_OK

@@ -120,7 +120,7 @@ def test_inconsistent_device_offsets_set_bad_args_bit(cuda_device):
     cu = torch.tensor([0, 64, 32], dtype=torch.int32, device=cuda_device)
     rc = lib.tokmix_gdn_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), st.data_ptr(),
                                 out.data_ptr(), final.data_ptr(), cu.data_ptr(), None, 2, 128, 2, 4, 128, 128,
-                                float(inp["scale"]), _lib.DTYPE_BF16, word.data_ptr(), stream)
+                                float(inp["scale"]), _lib.DTYPE_BF16, None, word.data_ptr(), stream)
     _lib.check(rc, "tokmix_gdn_prefill")
     torch.cuda.synchronize()
     assert int(word.item()) == 0x8
@@ -134,7 +134,7 @@ def test_inconsistent_device_offsets_set_bad_args_bit(cuda_device):
     out.zero_()
     rc = lib.tokmix_gdn_prefill_split(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(),
                                       st.data_ptr(), out.data_ptr(), final.data_ptr(), None, cu.data_ptr(), cb.data_ptr(),
-                                      None, 2, 128, 2, 2, 4, 128, 128, float(inp["scale"]), _lib.DTYPE_BF16,
+                                      None, 2, 128, 2, 2, 4, 128, 128, float(inp["scale"]), _lib.DTYPE_BF16, None,
                                       ws.data_ptr(), nbytes, word.data_ptr(), stream)
     _lib.check(rc, "tokmix_gdn_prefill_split")
     torch.cuda.synchronize()

@@ -303,3 +303,18 @@ def test_gdn_with_raw_gates_matches_oracle(cuda_device, oracle_threads, t):
     o_ref, s_ref = _oracle({**inp, "g": torch.from_numpy(g_ref), "beta": torch.from_numpy(b_ref)}, oracle_threads)
     np.testing.assert_allclose(_np(out), o_ref, **OUT_TOL)
     np.testing.assert_allclose(_np(fs), s_ref.reshape(fs.shape), **STATE_TOL)
+
+
+@pytest.mark.parametrize("mode", ["fused", "split", "overlap", "segmented"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gdn_gates_inside_the_kernels_equal_the_separate_pass(cuda_device, mode, dtype):
+    """gates=(A_log, dt_bias): the preparation of each chunk computes g and beta from the raw
+    projections with the separate pass's arithmetic, so the results are the same bits as running
+    gdn_gates first and passing its g and beta."""
+    inp = gcfg.random_inputs(1, 0, lengths=[70, 300, 1, 0, 129], seed=14, state_std=0.02, hk=2, hv=4)
+    a, b, a_log, dt_bias = _raw_gates(inp["g"].shape, 4, seed=15, dtype=dtype)
+    o1, s1 = gdn.kernel_fn(**{**inp, "g": a, "beta": b}, gates=(a_log, dt_bias), mode=mode, segment_chunks=2)
+    g, beta = gdn.gdn_gates(a, b, a_log, dt_bias)
+    o2, s2 = gdn.kernel_fn(**{**inp, "g": g, "beta": beta}, mode=mode, segment_chunks=2)
+    gdn.check_device_status(cuda_device)
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
