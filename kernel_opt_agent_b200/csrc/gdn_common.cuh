@@ -46,6 +46,71 @@ __device__ __forceinline__ void load_gates(const float* g, const float* beta, co
   bv = 1.0f / (1.0f + expf(-b));
 }
 
+// Sum of squares of four values in a fixed order (explicitly rounded, so every caller gets the
+// same bits): the per-lane step of the row L2 normalisation (qk_l2norm).
+__device__ __forceinline__ float sumsq4(float a, float b, float c, float d) {
+  return __fmaf_rn(d, d, __fmaf_rn(c, c, __fmaf_rn(b, b, __fmul_rn(a, a))));
+}
+
+// x / sqrt(sum x^2 + eps) of one bf16 row of 128 held in shared memory as the 128-byte rows of two
+// 128-byte-swizzled 64-column boxes (half0: elements 0-63, half1: 64-127; swizzle phase r7 = the
+// row's index & 7), in place.  The sum is formed exactly as the normalisation pass over global
+// memory forms it (gdn_preprocess.cu: 32 lanes take 4 consecutive elements each, then an XOR
+// butterfly over offsets 16 .. 1), so both give the same bits.  Returns the scaling factor.
+__device__ __forceinline__ float l2norm_row_sw128(uint8_t* half0, uint8_t* half1, int r7, float eps) {
+  float part[32];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint8_t* base = h ? half1 : half0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {  // 16-byte chunk j holds elements 64h + 8j .. +7
+      const uint4 w = *reinterpret_cast<const uint4*>(base + ((j ^ r7) << 4));
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+      const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.z));
+      const float2 d = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.w));
+      part[16 * h + 2 * j] = sumsq4(a.x, a.y, b.x, b.y);
+      part[16 * h + 2 * j + 1] = sumsq4(c.x, c.y, d.x, d.y);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    float nxt[32];
+#pragma unroll
+    for (int l = 0; l < 32; ++l) nxt[l] = __fadd_rn(part[l], part[l ^ off]);
+#pragma unroll
+    for (int l = 0; l < 32; ++l) part[l] = nxt[l];
+  }
+  const float inv = rsqrtf(part[0] + eps);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint8_t* base = h ? half1 : half0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint4 w = *reinterpret_cast<const uint4*>(base + ((j ^ r7) << 4));
+      uint32_t* e = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e[q]));
+        e[q] = pack_bf16x2(f.x * inv, f.y * inv);
+      }
+      *reinterpret_cast<uint4*>(base + ((j ^ r7) << 4)) = w;
+    }
+  }
+  return inv;
+}
+
+// The normalised row (as above) copied to global memory in plain order: 128 bf16, 16-byte aligned.
+__device__ __forceinline__ void copy_row_sw128(const uint8_t* half0, const uint8_t* half1, int r7, __nv_bfloat16* dst) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint8_t* base = h ? half1 : half0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      reinterpret_cast<uint4*>(dst)[8 * h + j] = *reinterpret_cast<const uint4*>(base + ((j ^ r7) << 4));
+  }
+}
+
 struct ChunkParams {
   float beta[kC];  // write strength (0 for tokens past the sequence end)
   float g2[kC];    // in-chunk inclusive prefix sum of g, in log2 units

@@ -57,9 +57,11 @@ __global__ void __launch_bounds__(kWarps * 32) l2norm_rows_kernel(const T* x, __
   if (r >= rows) return;  // whole warps leave together (r is warp-uniform)
   float f[4];
   load4<T>(x + r * kDim, lane, f);
-  float ss = f[0] * f[0] + f[1] * f[1] + f[2] * f[2] + f[3] * f[3];
+  // the order of the sum is fixed (gdn_common.cuh, l2norm_row_sw128 forms it the same way inside
+  // the GDN kernels): 4 consecutive elements per lane, then an XOR butterfly
+  float ss = gdn::sumsq4(f[0], f[1], f[2], f[3]);
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
   const float inv = rsqrtf(ss + eps);
   const __nv_bfloat162 a = __floats2bfloat162_rn(f[0] * inv, f[1] * inv);
   const __nv_bfloat162 b = __floats2bfloat162_rn(f[2] * inv, f[3] * inv);
