@@ -69,21 +69,32 @@ int tokmix_fa2_fwd(const void* q, const void* k, const void* v, void* o, int bat
                    int seqlen_q, int seqlen_kv, int head_dim, int layout, int causal, float sm_scale,
                    uint32_t* status, void* stream);
 
-/* The Qwen3.5 gated-delta-net gates from the raw projections, for the GDN prefill entry points'
- * `gates` argument: when given, the kernels compute g and beta themselves while preparing each
- * chunk (and their g, beta arguments are ignored):
- *   g = -exp(a_log[h]) * softplus(a + dt_bias[h]),  beta = sigmoid(b)      (fp32 arithmetic)
- * a, b: device [total_tokens, heads_v] in `dtype` (TOKMIX_DTYPE_BF16 or TOKMIX_DTYPE_FP32);
- * a_log, dt_bias: device fp32 [heads_v].  The arithmetic is tokmix_gdn_gates' own, so the results
- * equal those of running tokmix_gdn_gates first, bit for bit.  The reference takes g and beta
- * ready-made (kernels/qwen35moe_gdn_prefill.py:107-136). */
-typedef struct tokmix_gdn_gate_inputs {
+/* Steps before the recurrence that the GDN prefill entry points can do inside their first stage
+ * (the `gates` argument; NULL = neither).  The reference takes normalised q, k and ready g, beta
+ * (kernels/qwen35moe_gdn_prefill.py:107-136).
+ *   Gates (a != NULL): the Qwen3.5 gated-delta-net gates from the raw projections, computed while
+ *   each chunk is prepared (the g, beta arguments are then ignored):
+ *     g = -exp(a_log[h]) * softplus(a + dt_bias[h]),  beta = sigmoid(b)      (fp32 arithmetic)
+ *   a, b: device [total_tokens, heads_v] in `dtype` (TOKMIX_DTYPE_BF16 or TOKMIX_DTYPE_FP32);
+ *   a_log, dt_bias: device fp32 [heads_v].  The arithmetic is tokmix_gdn_gates' own, so the
+ *   results equal those of running tokmix_gdn_gates first, bit for bit.
+ *   q/k normalisation (qk_l2norm != 0): every q and k row becomes x / sqrt(sum x^2 + l2norm_eps)
+ *   (fp32 arithmetic, bf16 result) as it is staged for the first product, with the summation of
+ *   tokmix_l2norm_rows, so the results equal those of running tokmix_l2norm_rows on bf16 q and k
+ *   first, bit for bit.  The schedules that prepare chunks apart from their state chains
+ *   (tokmix_gdn_prefill_split, tokmix_gdn_prefill_segmented) write the normalised keys to
+ *   k_normed (device bf16 [total_tokens, heads_k, 128]) for the chains to read; the one-CTA-per-unit
+ *   kernel (tokmix_gdn_prefill) needs no such buffer (k_normed may be NULL there). */
+typedef struct tokmix_gdn_stage1 {
   const void* a;
   const void* b;
   int dtype;
   const float* a_log;
   const float* dt_bias;
-} tokmix_gdn_gate_inputs;
+  int qk_l2norm;
+  float l2norm_eps;
+  void* k_normed;
+} tokmix_gdn_stage1;
 
 /* Gated-delta-rule (GDN) prefill, chunked on the tensor cores.
  *
@@ -105,7 +116,7 @@ typedef struct tokmix_gdn_gate_inputs {
 int tokmix_gdn_prefill(const void* q, const void* k, const void* v, const float* g, const float* beta,
                        const float* initial_state, void* out, float* final_state, const int32_t* cu_seqlens_dev,
                        const int32_t* seq_order_dev, int num_seqs, int total_tokens, int heads_k, int heads_v,
-                       int head_dim_k, int head_dim_v, float scale, int io_dtype, const tokmix_gdn_gate_inputs* gates,
+                       int head_dim_k, int head_dim_v, float scale, int io_dtype, const tokmix_gdn_stage1* gates,
                        uint32_t* status, void* stream);
 
 /* Gated-delta-rule prefill for a batch of equal-length sequences that allocates nothing.
@@ -159,7 +170,7 @@ int tokmix_gdn_prefill_split(const void* q, const void* k, const void* v, const 
                              const float* initial_state, void* out, float* final_state, float* checkpoints,
                              const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev, const int32_t* record_order_dev, int num_seqs,
                              int total_tokens, int total_chunks, int heads_k, int heads_v, int head_dim_k,
-                             int head_dim_v, float scale, int io_dtype, const tokmix_gdn_gate_inputs* gates,
+                             int head_dim_v, float scale, int io_dtype, const tokmix_gdn_stage1* gates,
                              void* workspace, long long workspace_bytes, uint32_t* status, void* stream);
 
 /* Workspace size of tokmix_gdn_prefill_split in bytes (-1 for negative arguments). */
@@ -196,7 +207,7 @@ int tokmix_gdn_prefill_segmented(const void* q, const void* k, const void* v, co
                                  const int32_t* cu_seqlens_dev, const int32_t* chunk_base_dev,
                                  const int32_t* cu_seqlens_host, int num_seqs, int total_tokens, int total_chunks,
                                  int heads_k, int heads_v, int head_dim_k, int head_dim_v, float scale, int io_dtype,
-                                 const tokmix_gdn_gate_inputs* gates, int max_segment_chunks, const void* plan_dev,
+                                 const tokmix_gdn_stage1* gates, int max_segment_chunks, const void* plan_dev,
                                  void* workspace, long long workspace_bytes, uint32_t* status, void* stream);
 
 /* Workspace size of tokmix_gdn_prefill_segmented in bytes (-1 for inconsistent arguments). */

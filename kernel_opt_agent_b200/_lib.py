@@ -68,11 +68,12 @@ SIGNATURES = {
     "tokmix_version": (ctypes.c_char_p, []),
 }
 
-class GateInputs(ctypes.Structure):
-    """tokmix_gdn_gate_inputs: the raw gate projections the GDN kernels compute g and beta from."""
+class Stage1Inputs(ctypes.Structure):
+    """tokmix_gdn_stage1: the gate projections and q/k normalisation the GDN kernels do in stage 1."""
 
     _fields_ = [("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("dtype", ctypes.c_int),
-                ("a_log", ctypes.c_void_p), ("dt_bias", ctypes.c_void_p)]
+                ("a_log", ctypes.c_void_p), ("dt_bias", ctypes.c_void_p), ("qk_l2norm", ctypes.c_int),
+                ("l2norm_eps", ctypes.c_float), ("k_normed", ctypes.c_void_p)]
 
 
 _lib = None

@@ -88,6 +88,8 @@ struct Params {
   float scale;
   uint32_t* status;
   GateSource gates;  // a == null: g and beta as given
+  int l2norm;        // normalise the q and k rows as they are staged (before T1)
+  float l2norm_eps;
 };
 
 // Hand-off barriers.  Event of chunk c lives in slot c & 1 (in_full: c % 3) and completes the
@@ -599,8 +601,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lb = tmem_addr(tbase, (warp & 3) * 32, 0);
     float* Ls = reinterpret_cast<float*>(smem + kOffL);
     float* Xs = reinterpret_cast<float*>(smem + kOffX);
+    // qk_l2norm: the four warps normalise the 128 rows of chunk n's staged [K; Q] tile (thread =
+    // row) once it has landed, before T1(n) -- its first reader
+    auto normalize_slot = [&](int n) -> bool {
+      bool landed = __all_sync(0xffffffffu, mbar_wait(&bars.in_full[n % kSlots], (n / kSlots) & 1, p.status,
+                                                      kDevTimeoutTma));
+      if (landed) {
+        uint8_t* slot = smem + kOffSlots + (n % kSlots) * kSlotBytes;
+        l2norm_row_sw128(slot + tid * 128, slot + 16384 + tid * 128, tid & 7, p.l2norm_eps);
+        fence_async_smem();
+      }
+      return named_sync_and(3, 128, landed);
+    };
     bool ok = true;
-    if (tid == 0) {
+    if (p.l2norm) ok = normalize_slot(0);
+    if (tid == 0 && ok) {
       ok = mbar_wait(&bars.in_full[0], 0, p.status, kDevTimeoutTma);
       if (ok) {
         tc_fence_after();
@@ -662,6 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // every thread has read W^T out of the QW region: T1(c+1) may overwrite it
       if (!named_sync_and(3, 128, wready)) { ok = false; break; }
+      if (p.l2norm && c + 1 < N && !normalize_slot(c + 1)) { ok = false; break; }
       if (tid == 0) {
         GDN_TRACE(13, c);
         const int n = c + 1;
@@ -707,13 +723,10 @@ static int validate_prefill_args(const char* who, const void* q, const void* k, 
                                  const float* beta, const float* initial_state, const void* out,
                                  const float* final_state, int num_seqs, int total_tokens, int heads_k, int heads_v,
                                  int head_dim_k, int head_dim_v, float scale, int io_dtype,
-                                 const tokmix_gdn_gate_inputs* gates = nullptr) {
-  if (!q || !k || !v || !out || !final_state || (gates == nullptr && (!g || !beta)))
+                                 const tokmix_gdn_stage1* gates = nullptr) {
+  if (!q || !k || !v || !out || !final_state || (!stage1_gates(gates) && (!g || !beta)))
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: null pointer argument", who);
-  if (gates != nullptr &&
-      (!gates->a || !gates->b || !gates->a_log || !gates->dt_bias ||
-       (gates->dtype != TOKMIX_DTYPE_BF16 && gates->dtype != TOKMIX_DTYPE_FP32)))
-    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: gates need a, b, a_log, dt_bias and a bf16 or fp32 dtype", who);
+  if (const int rc = check_stage1(who, gates, false)) return rc;
   if (num_seqs < 0 || total_tokens < 0 || heads_k <= 0 || heads_v <= 0)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: negative or zero size", who);
   if (heads_v % heads_k != 0)
@@ -737,7 +750,7 @@ extern "C" int tokmix_gdn_prefill(const void* q, const void* k, const void* v, c
                                   const float* initial_state, void* out, float* final_state,
                                   const int32_t* cu_seqlens_dev, const int32_t* seq_order_dev, int num_seqs,
                                   int total_tokens, int heads_k, int heads_v, int head_dim_k, int head_dim_v,
-                                  float scale, int io_dtype, const tokmix_gdn_gate_inputs* gates, uint32_t* status,
+                                  float scale, int io_dtype, const tokmix_gdn_stage1* gates, uint32_t* status,
                                   void* stream) {
   using namespace tokmix;
   using namespace tokmix::gdn;
@@ -783,8 +796,12 @@ extern "C" int tokmix_gdn_prefill(const void* q, const void* k, const void* v, c
   p.hv = heads_v;
   p.num_seqs = num_seqs;
   p.total_tokens = total_tokens;
-  if (gates != nullptr)
+  if (stage1_gates(gates))
     p.gates = GateSource{gates->a, gates->b, gates->a_log, gates->dt_bias, gates->dtype == TOKMIX_DTYPE_BF16 ? 1 : 0};
+  if (stage1_l2norm(gates)) {
+    p.l2norm = 1;
+    p.l2norm_eps = gates->l2norm_eps;
+  }
   p.scale = scale;
   p.status = status;
   const int smem_bytes = kSmemBytes + 1024;

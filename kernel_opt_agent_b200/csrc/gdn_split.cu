@@ -112,6 +112,9 @@ struct PrepParams {
   float scale;
   uint32_t* status;
   GateSource gates;  // a == null: g and beta as given
+  int l2norm;        // normalise the staged q and k rows before T1; the key head's first value
+  float l2norm_eps;  //   head's record also writes the normalised keys to k_normed for the chains
+  __nv_bfloat16* k_normed;
 };
 
 // A chain unit of the segmented schedule: `nchunks` chunks of sequence `seq` from its chunk
@@ -144,6 +147,9 @@ struct ChainParams {
   int num_units, num_slots, num_seqs;
   float* seg_states;      // [num_slots, hv, 128, 128]
   __nv_bfloat16* r_out;   // [total_tokens, hv, 128]
+  // with flags (one cooperative launch) and normalised keys: the keys of chunk c are written by
+  // the record of the key head's first value head, so the loader waits for that record too
+  int wait_key_record;
 };
 
 // bulk copy global -> shared, completing on an mbarrier (one destination CTA)
@@ -205,6 +211,18 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
   PREP_TRACE(1);
   if (tid < kParamsBytes / 16)
     reinterpret_cast<uint4*>(rec + kRecParams)[tid] = reinterpret_cast<const uint4*>(smem + kPParams)[tid];
+  // --- qk_l2norm: thread = row of the staged [K; Q] tile, normalised in place once it landed
+  if (p.l2norm) {
+    const bool landed = __all_sync(0xffffffffu, mbar_wait(bar_in, in_parity, p.status, kDevTimeoutTma));
+    if (landed) {
+      uint8_t* r0p = smem + kPSlot + tid * 128;
+      l2norm_row_sw128(r0p, r0p + 16384, tid & 7, p.l2norm_eps);
+      if (tid < n_valid && h < p.hk)  // rows 0-63 are keys; one value head per key head writes them
+        copy_row_sw128(r0p, r0p + 16384, tid & 7, p.k_normed + (static_cast<size_t>(row0 + tid) * p.hk + kh) * kD);
+      fence_async_smem();
+    }
+    if (!named_sync_and(bar_id, 128, landed)) return false;
+  }
   // --- T1: [K;Q] K^T
   if (tid == 0 && mbar_wait(bar_in, in_parity, p.status, kDevTimeoutTma)) {
     tc_fence_after();
@@ -450,6 +468,9 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
         const size_t ridx = static_cast<size_t>(gc0 + c) * p.hv + h;
         const uint8_t* rec = p.ws + ridx * kRecBytes;
         if (flags != nullptr && !wait_flag(flags + ridx, p.status)) break;
+        if (flags != nullptr && p.wait_key_record && kh != h &&
+            !wait_flag(flags + static_cast<size_t>(gc0 + c) * p.hv + kh, p.status))
+          break;
         mbar_arrive_expect_tx(bar, kRecBytes + (zero_v ? 16384 : 32768));
         bulk_g2s(st, rec, kRecP, bar);  // T, W, e^G Q
         bulk_g2s(st + kRecP, rec + kRecP, kRecBytes - kRecP, bar);  // P, params
@@ -762,8 +783,8 @@ struct OverlapParams {
 // every CTA resident, so the chain CTAs' (bounded) waits are on CTAs that are running.
 __global__ void __launch_bounds__(kOverlapThreads, 1)
     gdn_overlap_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                       const __grid_constant__ CUtensorMap map_v, const PrepParams pp, const ChainParams cp,
-                       const OverlapParams op) {
+                       const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_kc,
+                       const PrepParams pp, const ChainParams cp, const OverlapParams op) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ ChainBarriers bars;
@@ -773,7 +794,7 @@ __global__ void __launch_bounds__(kOverlapThreads, 1)
   CTA_START_TRACE();
   if (static_cast<int>(blockIdx.x) < op.units) {
     const uint32_t tbase = chain_setup(bars, &tmem_base_shared);
-    if (warp < kChainThreads / 32) chain_unit(&map_k, &map_v, cp, smem, bars, tbase, blockIdx.x, op.flags);
+    if (warp < kChainThreads / 32) chain_unit(&map_kc, &map_v, cp, smem, bars, tbase, blockIdx.x, op.flags);
     tc_fence_before();
     __syncthreads();
     CTA_END_TRACE();
@@ -863,16 +884,15 @@ namespace tokmix {
 namespace gdn {
 namespace split {
 
-static int check_gate_inputs(const char* who, const tokmix_gdn_gate_inputs* gates) {
-  if (gates != nullptr &&
-      (!gates->a || !gates->b || !gates->a_log || !gates->dt_bias ||
-       (gates->dtype != TOKMIX_DTYPE_BF16 && gates->dtype != TOKMIX_DTYPE_FP32)))
-    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: gates need a, b, a_log, dt_bias and a bf16 or fp32 dtype", who);
-  return TOKMIX_OK;
+static void set_l2norm(PrepParams& pp, const tokmix_gdn_stage1* s1) {
+  if (!stage1_l2norm(s1)) return;
+  pp.l2norm = 1;
+  pp.l2norm_eps = s1->l2norm_eps;
+  pp.k_normed = static_cast<__nv_bfloat16*>(s1->k_normed);
 }
 
-static GateSource gate_source(const tokmix_gdn_gate_inputs* gates) {
-  if (gates == nullptr) return GateSource{};
+static GateSource gate_source(const tokmix_gdn_stage1* gates) {
+  if (!stage1_gates(gates)) return GateSource{};
   return GateSource{gates->a, gates->b, gates->a_log, gates->dt_bias, gates->dtype == TOKMIX_DTYPE_BF16 ? 1 : 0};
 }
 
@@ -908,7 +928,7 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
                                         const int32_t* record_order_dev, int num_seqs, int total_tokens,
                                         int total_chunks, int heads_k, int heads_v, int head_dim_k,
                                         int head_dim_v, float scale, int io_dtype,
-                                        const tokmix_gdn_gate_inputs* gates, void* workspace,
+                                        const tokmix_gdn_stage1* gates, void* workspace,
                                         long long workspace_bytes, uint32_t* status, void* stream) {
   using namespace tokmix;
   using namespace tokmix::gdn;
@@ -917,9 +937,9 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: negative or zero size");
   if (num_seqs == 0) return TOKMIX_OK;
   if (!q || !k || !v || !out || !final_state || !cu_seqlens_dev || !chunk_base_dev || !status ||
-      (gates == nullptr && (!g || !beta)))
+      (!stage1_gates(gates) && (!g || !beta)))
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "tokmix_gdn_prefill_split: null pointer argument");
-  if (const int rc = check_gate_inputs("tokmix_gdn_prefill_split", gates)) return rc;
+  if (const int rc = check_stage1("tokmix_gdn_prefill_split", gates, true)) return rc;
   if (heads_v % heads_k != 0)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT,
                 "tokmix_gdn_prefill_split: heads_v (%d) must be a multiple of heads_k (%d)", heads_v, heads_k);
@@ -945,6 +965,9 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
 
   CUtensorMap mq, mk, mv;
   if (!encode_qkv_maps(q, k, v, total_tokens, heads_k, heads_v, &mq, &mk, &mv)) return TOKMIX_ERR_INVALID_ARGUMENT;
+  CUtensorMap mkc = mk;  // the chains' keys: the normalised copy when the preparation normalises
+  if (stage1_l2norm(gates) && !encode_qkv_maps(q, gates->k_normed, v, total_tokens, heads_k, heads_v, &mq, &mkc, &mv))
+    return TOKMIX_ERR_INVALID_ARGUMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   PrepParams pp{};
   pp.g = g;
@@ -959,6 +982,7 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   pp.scale = scale;
   pp.status = status;
   pp.gates = gate_source(gates);
+  set_l2norm(pp, gates);
   ChainParams cp{};
   cp.state_in = initial_state;
   cp.state_out = final_state;
@@ -972,6 +996,7 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   cp.total_tokens = total_tokens;
   cp.total_chunks = total_chunks;
   cp.num_seqs = num_seqs;  // units == null: one whole-sequence unit per (sequence, head)
+  cp.wait_key_record = stage1_l2norm(gates) ? 1 : 0;
   cp.status = status;
   const long long records = static_cast<long long>(total_chunks) * heads_v;
   // --- one cooperative launch when the chains leave SMs free for the preparation CTAs
@@ -1000,7 +1025,7 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
       attr[0].val.cooperative = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      if (cudaLaunchKernelEx(&cfg, gdn_overlap_kernel, mq, mk, mv, pp, cp, op) == cudaSuccess)
+      if (cudaLaunchKernelEx(&cfg, gdn_overlap_kernel, mq, mk, mv, mkc, pp, cp, op) == cudaSuccess)
         return check_launch("tokmix_gdn_prefill_split (overlapped)");
       cudaGetLastError();  // not launchable cooperatively here: two launches instead
     } else {
@@ -1018,7 +1043,7 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
   const int smem = kCSmem + 1024;
   if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_chain_kernel), smem))
     return check_launch("tokmix_gdn_prefill_split: cudaFuncSetAttribute (chain)");
-  gdn_chain_kernel<<<static_cast<unsigned>(units), kChainThreads, smem, s>>>(mk, mv, cp);
+  gdn_chain_kernel<<<static_cast<unsigned>(units), kChainThreads, smem, s>>>(mkc, mv, cp);
   return check_launch("tokmix_gdn_prefill_split (chain)");
 }
 
@@ -1176,7 +1201,7 @@ extern "C" int tokmix_gdn_prefill_segmented(const void* q, const void* k, const 
                                             const int32_t* chunk_base_dev, const int32_t* cu_seqlens_host,
                                             int num_seqs, int total_tokens, int total_chunks, int heads_k, int heads_v,
                                             int head_dim_k, int head_dim_v, float scale, int io_dtype,
-                                            const tokmix_gdn_gate_inputs* gates, int max_segment_chunks,
+                                            const tokmix_gdn_stage1* gates, int max_segment_chunks,
                                             const void* plan_dev, void* workspace, long long workspace_bytes,
                                             uint32_t* status, void* stream) {
   using namespace tokmix;
@@ -1187,9 +1212,9 @@ extern "C" int tokmix_gdn_prefill_segmented(const void* q, const void* k, const 
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: negative or zero size", who);
   if (num_seqs == 0) return TOKMIX_OK;
   if (!q || !k || !v || !out || !final_state || !cu_seqlens_dev || !chunk_base_dev || !status ||
-      (gates == nullptr && (!g || !beta)))
+      (!stage1_gates(gates) && (!g || !beta)))
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: null pointer argument", who);
-  if (const int rc = check_gate_inputs(who, gates)) return rc;
+  if (const int rc = check_stage1(who, gates, true)) return rc;
   if (heads_v % heads_k != 0)
     return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: heads_v (%d) must be a multiple of heads_k (%d)", who, heads_v, heads_k);
   if (head_dim_k != kD || head_dim_v != kD)
@@ -1214,6 +1239,9 @@ extern "C" int tokmix_gdn_prefill_segmented(const void* q, const void* k, const 
 
   CUtensorMap mq, mk, mv;
   if (!encode_qkv_maps(q, k, v, total_tokens, heads_k, heads_v, &mq, &mk, &mv)) return TOKMIX_ERR_INVALID_ARGUMENT;
+  CUtensorMap mkc = mk;  // the chains' keys: the normalised copy when the preparation normalises
+  if (stage1_l2norm(gates) && !encode_qkv_maps(q, gates->k_normed, v, total_tokens, heads_k, heads_v, &mq, &mkc, &mv))
+    return TOKMIX_ERR_INVALID_ARGUMENT;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   auto* r_out = reinterpret_cast<__nv_bfloat16*>(ws + plan.off_r);
   auto* seg_states = reinterpret_cast<float*>(ws + plan.off_states);
@@ -1258,6 +1286,7 @@ extern "C" int tokmix_gdn_prefill_segmented(const void* q, const void* k, const 
   pp.scale = scale;
   pp.status = status;
   pp.gates = gate_source(gates);
+  set_l2norm(pp, gates);
   if (total_chunks > 0) {
     const int smem = kPSmem + 1024;
     if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_prep_kernel), smem))
@@ -1289,7 +1318,7 @@ extern "C" int tokmix_gdn_prefill_segmented(const void* q, const void* k, const 
     const int smem = kCSmem + 1024;
     if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_chain_kernel), smem))
       return check_launch("tokmix_gdn_prefill_segmented: cudaFuncSetAttribute (chain)");
-    gdn_chain_kernel<<<static_cast<unsigned>(plan.units.size() * heads_v), kChainThreads, smem, s>>>(mk, mv, cp);
+    gdn_chain_kernel<<<static_cast<unsigned>(plan.units.size() * heads_v), kChainThreads, smem, s>>>(mkc, mv, cp);
     if (const int rc = check_launch("tokmix_gdn_prefill_segmented (chain)")) return rc;
   }
   if (!plan.combine.empty()) {

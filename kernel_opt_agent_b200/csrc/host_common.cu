@@ -1,6 +1,8 @@
 // host_common.cu -- error reporting, tensor-map encoding and device queries for the C ABI.
 #include "host_common.h"
 
+#include <cmath>
+
 #include <mutex>
 #include <set>
 #include <utility>
@@ -105,6 +107,24 @@ int check_device() {
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
   if (major != 10 || minor != 0)
     return fail(TOKMIX_ERR_DEVICE, "libtokmix is built for sm_100a (B200); device %d is sm_%d%d", dev, major, minor);
+  return TOKMIX_OK;
+}
+
+}  // namespace tokmix
+
+namespace tokmix {
+
+int check_stage1(const char* who, const tokmix_gdn_stage1* s1, bool needs_k_normed) {
+  if (s1 == nullptr) return TOKMIX_OK;
+  if (stage1_gates(s1) && (!s1->b || !s1->a_log || !s1->dt_bias ||
+                           (s1->dtype != TOKMIX_DTYPE_BF16 && s1->dtype != TOKMIX_DTYPE_FP32)))
+    return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: gates need a, b, a_log, dt_bias and a bf16 or fp32 dtype", who);
+  if (stage1_l2norm(s1)) {
+    if (!(s1->l2norm_eps > 0.0f) || !std::isfinite(s1->l2norm_eps))
+      return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: l2norm_eps must be positive and finite", who);
+    if (needs_k_normed && (s1->k_normed == nullptr || reinterpret_cast<uintptr_t>(s1->k_normed) % 16 != 0))
+      return fail(TOKMIX_ERR_INVALID_ARGUMENT, "%s: qk_l2norm needs a 16-byte aligned k_normed buffer", who);
+  }
   return TOKMIX_OK;
 }
 

@@ -40,4 +40,11 @@ bool ensure_smem_attr(const void* func, int bytes);
 // TOKMIX_OK if the current device is a compute capability 10.0 part, else sets the error.
 int check_device();
 
+// The GDN stage-1 options (tokmix_gdn_stage1): whether gates / q-k normalisation are requested,
+// and their checks -- gates need a, b, a_log, dt_bias and a bf16 or fp32 dtype; normalisation a
+// positive finite eps and, for the schedules that need it, the normalised-key buffer.
+inline bool stage1_gates(const tokmix_gdn_stage1* s1) { return s1 != nullptr && s1->a != nullptr; }
+inline bool stage1_l2norm(const tokmix_gdn_stage1* s1) { return s1 != nullptr && s1->qk_l2norm != 0; }
+int check_stage1(const char* who, const tokmix_gdn_stage1* s1, bool needs_k_normed);
+
 }  // namespace tokmix

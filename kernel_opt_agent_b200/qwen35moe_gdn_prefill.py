@@ -22,10 +22,12 @@ Extensions over the reference module:
 * ``cu_seqlens`` (keyword): variable-length sequences packed along T with q.shape[0] == 1 and
   one initial state per sequence (state [N,Hv,128,128]); ``state=None`` means zero states.
 * any Hk dividing Hv (the reference fixes Hk=16, Hv=32).
-* ``qk_l2norm`` (keyword, default False): L2-normalise q and k per (token, head) on the device
-  first, ``x / sqrt(sum x^2 + 1e-6)`` in fp32 (``l2norm_rows``), as the workloads' generators do
-  before calling the reference; the result is the kernels' bf16 operand, so with fp32 inputs the
-  normalisation replaces the conversion pass.
+* ``qk_l2norm`` (keyword, default False): L2-normalise q and k per (token, head),
+  ``x / sqrt(sum x^2 + 1e-6)`` in fp32, as the workloads' generators do before calling the
+  reference.  bf16 q, k are normalised inside stage 1, as each chunk's rows are staged for the
+  first product (the split-family schedules keep a normalised copy of k for their chains); fp32
+  q, k by the separate pass ``l2norm_rows``, which also converts them to the kernels' bf16 operand.
+  Both give the same bits.
 * ``gates`` (keyword, default None): ``(A_log, dt_bias)`` ([Hv] each) to pass the raw gate
   projections instead of g and beta: the ``g`` and ``beta`` arguments then hold the projections
   a and b, and ``g = -exp(A_log) * softplus(a + dt_bias)``, ``beta = sigmoid(b)`` are computed on
@@ -190,9 +192,16 @@ def kernel_fn(
             g, beta = gdn_gates(g, beta, *gates)
         res = qwen35moe_gdn_decode.kernel_fn(q, k, v, g, beta, state, scale, qk_l2norm=qk_l2norm)
         return res + [res[1].unsqueeze(1).clone()] if checkpoints else res
-    gate_in = None
-    if gates is not None:  # the preparation of each chunk computes g and beta from the projections
+    # stage 1 inside the kernels: the gates from the raw projections, and the q/k normalisation
+    # of bf16 inputs (fp32 inputs are normalised by the separate pass, which also converts them)
+    norm_inside = qk_l2norm and q.dtype == torch.bfloat16
+    gate_in, gate_keep = None, ()
+    if gates is not None:
         gate_in, gate_keep = _gate_inputs(g, beta, gates, hv)
+    if norm_inside:
+        gate_in = gate_in if gate_in is not None else _lib.Stage1Inputs()
+        gate_in.qk_l2norm = 1
+        gate_in.l2norm_eps = QK_L2NORM_EPS
     if cu_seqlens is None:
         lengths = (T,) * B
     else:
@@ -205,11 +214,11 @@ def kernel_fn(
             return [out, fs, ck if cu_seqlens is not None else ck.reshape(B, 0, hv, D, D)]
         return [out, fs]
     cu_t, order_t, cb_t, total_chunks, cb_host = _device_meta(lengths, dev)
-    qb = l2norm_rows(q) if qk_l2norm else q.to(torch.bfloat16).contiguous()
-    kb = l2norm_rows(k) if qk_l2norm else k.to(torch.bfloat16).contiguous()
+    qb = l2norm_rows(q) if qk_l2norm and not norm_inside else q.to(torch.bfloat16).contiguous()
+    kb = l2norm_rows(k) if qk_l2norm and not norm_inside else k.to(torch.bfloat16).contiguous()
     vb = v.to(torch.bfloat16).contiguous()
-    gf = g.to(torch.float32).contiguous() if gate_in is None else None
-    bf = beta.to(torch.float32).contiguous() if gate_in is None else None
+    gf = g.to(torch.float32).contiguous() if gates is None else None
+    bf = beta.to(torch.float32).contiguous() if gates is None else None
     st = state.to(torch.float32).contiguous() if state is not None else None
     out = torch.empty(vb.shape, dtype=torch.bfloat16, device=dev)
     final_state = torch.empty((nseq, hv, D, D), dtype=torch.float32, device=dev)
@@ -222,6 +231,10 @@ def kernel_fn(
             raise ValueError("segment_chunks must be positive")
         seg_len = int(segment_chunks)
     ck = torch.empty((total_chunks, hv, D, D), dtype=torch.float32, device=dev) if checkpoints else None
+    k_normed = None
+    if norm_inside and sched != "fused":  # the preparation writes the normalised keys for the chains
+        k_normed = torch.empty_like(kb)
+        gate_in.k_normed = k_normed.data_ptr()
     with torch.cuda.device(dev):
         if sched == "segmented":
             cu_host = _host_offsets(lengths)
@@ -277,7 +290,7 @@ def _gate_inputs(a: torch.Tensor, b: torch.Tensor, gates, hv: int):
     a, b = a.contiguous(), b.contiguous()
     al = a_log.to(device=a.device, dtype=torch.float32).contiguous()
     db = dt_bias.to(device=a.device, dtype=torch.float32).contiguous()
-    src = _lib.GateInputs(a.data_ptr(), b.data_ptr(), _lib.DTYPE_BF16 if a.dtype == torch.bfloat16 else _lib.DTYPE_FP32,
+    src = _lib.Stage1Inputs(a.data_ptr(), b.data_ptr(), _lib.DTYPE_BF16 if a.dtype == torch.bfloat16 else _lib.DTYPE_FP32,
                           al.data_ptr(), db.data_ptr())
     return src, (a, b, al, db)
 

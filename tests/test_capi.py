@@ -77,10 +77,10 @@ def test_gdn_rejects_bad_arguments():
     bad = list(args)
     bad[3] = bad[4] = None  # g and beta missing without gate inputs
     assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "null" in _lib.last_error()
-    gates = _lib.GateInputs(16, 16, 5, 16, 16)  # unknown dtype
+    gates = _lib.Stage1Inputs(16, 16, 5, 16, 16)  # unknown dtype
     bad[18] = ctypes.byref(gates)
     assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "gates" in _lib.last_error()
-    gates = _lib.GateInputs(16, None, 0, 16, 16)  # b missing
+    gates = _lib.Stage1Inputs(16, None, 0, 16, 16)  # b missing
     bad[18] = ctypes.byref(gates)
     assert lib.tokmix_gdn_prefill(*bad) == _lib.TOKMIX_ERR_INVALID_ARGUMENT and "gates" in _lib.last_error()
     bad = list(args)

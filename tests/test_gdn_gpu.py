@@ -318,3 +318,23 @@ def test_gdn_gates_inside_the_kernels_equal_the_separate_pass(cuda_device, mode,
     o2, s2 = gdn.kernel_fn(**{**inp, "g": g, "beta": beta}, mode=mode, segment_chunks=2)
     gdn.check_device_status(cuda_device)
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
+
+
+@pytest.mark.parametrize("mode", ["fused", "split", "overlap", "segmented"])
+def test_gdn_qk_l2norm_inside_the_kernels_equals_the_separate_pass(cuda_device, mode):
+    """qk_l2norm=True on bf16 q, k: the rows are normalised as they are staged inside stage 1
+    (with the separate pass's summation order), so the results are the same bits as running
+    l2norm_rows first; with the gates computed inside stage 1 too."""
+    inp = _raw_qk_inputs(2, 300, seed=61, hk=2, hv=4)
+    o1, s1 = gdn.kernel_fn(**inp, qk_l2norm=True, mode=mode, segment_chunks=2)
+    ref = {**inp, "q": gdn.l2norm_rows(inp["q"]), "k": gdn.l2norm_rows(inp["k"])}
+    o2, s2 = gdn.kernel_fn(**ref, mode=mode, segment_chunks=2)
+    gdn.check_device_status(cuda_device)
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+    a, b, a_log, dt_bias = _raw_gates(inp["g"].shape, 4, seed=62)
+    o3, s3 = gdn.kernel_fn(**{**inp, "g": a, "beta": b}, gates=(a_log, dt_bias), qk_l2norm=True, mode=mode,
+                           segment_chunks=2)
+    g, beta = gdn.gdn_gates(a, b, a_log, dt_bias)
+    o4, s4 = gdn.kernel_fn(**{**ref, "g": g, "beta": beta}, mode=mode, segment_chunks=2)
+    gdn.check_device_status(cuda_device)
+    assert torch.equal(o3, o4) and torch.equal(s3, s4)
