@@ -186,26 +186,30 @@ __global__ void __launch_bounds__(kCorrThreads, 1)
     }
   }
   __syncwarp();
+  // the thread's output row is read while the operands load and the product runs
+  uint4* orow = reinterpret_cast<uint4*>(out + (static_cast<size_t>(ci.tok0 + t) * hv + h) * kD);
+  uint4 o[16];
+  if (t < ci.ntok) {
+#pragma unroll
+    for (int q = 0; q < 16; ++q) o[q] = orow[q];
+  }
   const bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_mma, 0, status, kDevTimeoutMma));
   if (ok) {
     tc_fence_after();
-    __nv_bfloat16* orow = out + (static_cast<size_t>(ci.tok0 + t) * hv + h) * kD;
-#pragma unroll 1
-    for (int c = 0; c < kD; c += 32) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {  // 32 columns at a time
       uint32_t d[32];
-      tmem_ld32(tmem_addr(tbase, warp * 32, c), d);
+      tmem_ld32(tmem_addr(tbase, warp * 32, 32 * c), d);
       if (t < ci.ntok) {
-        uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          uint4 o4 = dst[q];
-          uint32_t* w = reinterpret_cast<uint32_t*>(&o4);
+          uint32_t* w = reinterpret_cast<uint32_t*>(&o[4 * c + q]);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[e]));
             w[e] = pack_bf16x2(f.x + __uint_as_float(d[8 * q + 2 * e]), f.y + __uint_as_float(d[8 * q + 2 * e + 1]));
           }
-          dst[q] = o4;
+          orow[4 * c + q] = o[4 * c + q];
         }
       }
     }

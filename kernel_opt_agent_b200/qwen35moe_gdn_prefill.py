@@ -73,6 +73,7 @@ _SPLIT_MAX_WORKSPACE = 8 << 30  # bytes; larger problems use the one-launch sche
 # for 7364; beside the chains of the overlapped launch: 1.51 ms for the 14,728 records of a 4-GPU
 # varlen slice), the overlapped launch's start-up, and the gap between launches.
 _US_FUSED_CHUNK = 8.5
+_US_FUSED_CHUNK_WAVES = 10.2  # per chunk and unit when the units run in several waves (varlen, one GPU: 4.07 ms)
 _US_CHAIN_CHUNK = 2.7
 _US_PREP_RECORD = 19.0
 _US_PREP_RECORD_OVERLAP = 24.0
@@ -465,11 +466,21 @@ def _plan_uncached(mode: str, lengths: tuple[int, ...], hv: int, dev: torch.devi
         if mode == "segmented":
             return mode, seg if seg is not None else max(max_chunks, 1)
         return mode, 0
-    if not checkpoints and (units >= sms or
-                            _lib.load().tokmix_gdn_split_workspace_bytes(total_chunks, hv) > _SPLIT_MAX_WORKSPACE):
-        return "fused", 0
+    too_big = _lib.load().tokmix_gdn_split_workspace_bytes(total_chunks, hv) > _SPLIT_MAX_WORKSPACE
     if units >= sms:
-        return "split", 0
+        # several waves of units: the one-CTA-per-unit kernel (longest first), or every record
+        # prepared first and the chains run longest first (the segmented launch without cuts)
+        if checkpoints:
+            return "split", 0
+        if too_big:
+            return "fused", 0
+        work = total_chunks * hv
+        fused = max(max_chunks * _US_FUSED_CHUNK, work * _US_FUSED_CHUNK_WAVES / sms)
+        lpt = (total_chunks * hv * _US_PREP_RECORD / (3 * sms) + _US_SPLIT_GAP +
+               max(max_chunks, work / sms) * _US_SEG_CHAIN_CHUNK)
+        return ("segmented", max(max_chunks, 1)) if lpt < fused else ("fused", 0)
+    if not checkpoints and too_big:
+        return "fused", 0
     records = total_chunks * hv
     # ties go to the earlier entry: the single fused launch first
     cands = ([] if checkpoints else ["fused"]) + (["overlap"] if units + 8 <= sms else []) + ["split"]

@@ -40,13 +40,20 @@ def test_hybrid_attention_long_sequences_sampled_rows(cuda_device, s):
         np.testing.assert_allclose(out[0, h, i].float().cpu().numpy(), ref, **TOL, err_msg=str((h, i)))
 
 
+_ORACLE_CACHE = {}
+
+
+@pytest.mark.parametrize("mode", ["auto", "fused"])
 @pytest.mark.parametrize("b,t", [(16, 4096), (5, 65536)])
-def test_hybrid_gdn_matches_oracle(cuda_device, oracle_threads, b, t):
+def test_hybrid_gdn_matches_oracle(cuda_device, oracle_threads, b, t, mode):
+    """More units than SMs: the one-CTA-per-unit kernel in waves, and the schedule "auto" picks
+    (the record-fed chains run longest first when that is predicted faster)."""
     inp = gcfg.random_inputs(b, t, seed=b * t, state_std=0.02)
-    assert gdn.schedule(inp["q"], inp["v"]) == "fused"
-    out, fs = gdn.kernel_fn(**inp)
+    out, fs = gdn.kernel_fn(**inp, mode=mode)
     gdn.check_device_status(cuda_device)
-    o_ref, s_ref = oracle.gdn_recurrent(*(_np(inp[x]) for x in ("q", "k", "v", "g", "beta")), _np(inp["state"]),
-                                        inp["scale"], nthreads=oracle_threads)
-    np.testing.assert_allclose(_np(out), o_ref, **TOL)
+    if (b, t) not in _ORACLE_CACHE:
+        _ORACLE_CACHE[(b, t)] = oracle.gdn_recurrent(*(_np(inp[x]) for x in ("q", "k", "v", "g", "beta")),
+                                                     _np(inp["state"]), inp["scale"], nthreads=oracle_threads)
+    o_ref, s_ref = _ORACLE_CACHE[(b, t)]
+    np.testing.assert_allclose(_np(out), o_ref, **TOL, err_msg=gdn.schedule(inp["q"], inp["v"], mode=mode))
     np.testing.assert_allclose(_np(fs), s_ref, **STATE_TOL)
