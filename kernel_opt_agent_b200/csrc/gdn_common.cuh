@@ -290,13 +290,22 @@ __device__ __forceinline__ void scale_row_copy(const uint8_t* src_box0_row, int 
   }
 }
 
+// Row layout of the 64x64 fp32 matrix X of the solve (a template parameter of the functions that
+// use it).  at(r, c) is the address of X[r][c]; for c a multiple of 4, X[r][c..c+3] are contiguous
+// and 16-byte aligned.
+struct PaddedRows {  // rows of kLds floats
+  float* p;
+  __device__ __forceinline__ float* at(int r, int c) const { return p + r * kLds + c; }
+};
+
 // X = (I + L)^-1 (unit lower triangular, fp32), 128 threads meeting at named barrier `bar`, by
 // recursive doubling over 16x16 blocks: the four diagonal blocks D_b by forward substitution
 // (one column per thread of the second half of the group); the two 32x32 diagonal blocks E_0,
 // E_1 from X[2p+1, 2p] = -D_{2p+1} L[2p+1, 2p] D_{2p}; the lower 32x32 block as -E_1 L[1, 0] E_0.
 // Products are staged in X's strictly upper blocks, which nothing else reads; the diagonal
 // blocks hold explicit zeros above their diagonal.  Ends with a barrier: X is complete.
-__device__ __forceinline__ void solve_inverse(const float* Ls, float* Xs, int tid, int bar) {
+template <class XM>
+__device__ __forceinline__ void solve_inverse(const float* Ls, XM X, int tid, int bar) {
   if (tid >= 64) {
     const int b = (tid - 64) >> 4, j = tid & 15;
     const float* lb16 = Ls + 16 * b * kLds + 16 * b;
@@ -310,7 +319,7 @@ __device__ __forceinline__ void solve_inverse(const float* Ls, float* Xs, int ti
       for (int i = s + 1; i < 16; ++i) acc[i] = fmaf(-lb16[i * kLds + s], xs, acc[i]);
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) Xs[(16 * b + i) * kLds + 16 * b + j] = acc[i];
+    for (int i = 0; i < 16; ++i) *X.at(16 * b + i, 16 * b + j) = acc[i];
   }
   named_sync(bar, 128);
   {  // pairs p: X[R + rr][C + c4..c4+3], R = 16(2p+1), C = 32p
@@ -320,25 +329,25 @@ __device__ __forceinline__ void solve_inverse(const float* Ls, float* Xs, int ti
 #pragma unroll
     for (int k = 0; k < 16; ++k) {  // Y = L[R.., C..] D_{2p}
       const float l = Ls[(R + rr) * kLds + C + k];
-      const float4 d = *reinterpret_cast<const float4*>(Xs + (C + k) * kLds + C + c4);
+      const float4 d = *reinterpret_cast<const float4*>(X.at(C + k, C + c4));
       y.x = fmaf(l, d.x, y.x);
       y.y = fmaf(l, d.y, y.y);
       y.z = fmaf(l, d.z, y.z);
       y.w = fmaf(l, d.w, y.w);
     }
-    *reinterpret_cast<float4*>(Xs + (C + rr) * kLds + R + c4) = y;  // staged in block (2p, 2p+1)
+    *reinterpret_cast<float4*>(X.at(C + rr, R + c4)) = y;  // staged in block (2p, 2p+1)
     named_sync(bar, 128);
     float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int m = 0; m < 16; ++m) {  // X[R.., C..] = -D_{2p+1} Y
-      const float dm = Xs[(R + rr) * kLds + R + m];
-      const float4 ym = *reinterpret_cast<const float4*>(Xs + (C + m) * kLds + R + c4);
+      const float dm = *X.at(R + rr, R + m);
+      const float4 ym = *reinterpret_cast<const float4*>(X.at(C + m, R + c4));
       z.x = fmaf(dm, ym.x, z.x);
       z.y = fmaf(dm, ym.y, z.y);
       z.z = fmaf(dm, ym.z, z.z);
       z.w = fmaf(dm, ym.w, z.w);
     }
-    *reinterpret_cast<float4*>(Xs + (R + rr) * kLds + C + c4) = make_float4(-z.x, -z.y, -z.z, -z.w);
+    *reinterpret_cast<float4*>(X.at(R + rr, C + c4)) = make_float4(-z.x, -z.y, -z.z, -z.w);
   }
   named_sync(bar, 128);
   {  // lower 32x32 block.  Thread: row r of 32, columns 4q..4q+3 and 16+4q..16+4q+3.
@@ -348,29 +357,28 @@ __device__ __forceinline__ void solve_inverse(const float* Ls, float* Xs, int ti
 #pragma unroll
     for (int k = 0; k < 32; ++k) {  // Y = L[32.., 0..32] E_0   (E_0 block (0,1) is not read)
       const float l = lrow[k];
-      const float4 xa = *reinterpret_cast<const float4*>(Xs + k * kLds + q4);
+      const float4 xa = *reinterpret_cast<const float4*>(X.at(k, q4));
       ya.x = fmaf(l, xa.x, ya.x);
       ya.y = fmaf(l, xa.y, ya.y);
       ya.z = fmaf(l, xa.z, ya.z);
       ya.w = fmaf(l, xa.w, ya.w);
       if (k >= 16) {
-        const float4 xb = *reinterpret_cast<const float4*>(Xs + k * kLds + 16 + q4);
+        const float4 xb = *reinterpret_cast<const float4*>(X.at(k, 16 + q4));
         yb.x = fmaf(l, xb.x, yb.x);
         yb.y = fmaf(l, xb.y, yb.y);
         yb.z = fmaf(l, xb.z, yb.z);
         yb.w = fmaf(l, xb.w, yb.w);
       }
     }
-    *reinterpret_cast<float4*>(Xs + r * kLds + 32 + q4) = ya;  // staged in rows 0-31, cols 32-63
-    *reinterpret_cast<float4*>(Xs + r * kLds + 48 + q4) = yb;
+    *reinterpret_cast<float4*>(X.at(r, 32 + q4)) = ya;  // staged in rows 0-31, cols 32-63
+    *reinterpret_cast<float4*>(X.at(r, 48 + q4)) = yb;
     named_sync(bar, 128);
     float4 za = make_float4(0.f, 0.f, 0.f, 0.f), zb = za;
-    const float* erow = Xs + (32 + r) * kLds + 32;
 #pragma unroll
     for (int m = 0; m < 16; ++m) {  // X[32.., 0..32] = -E_1 Y   (rows 32-47: D_2 only)
-      const float e = erow[m];
-      const float4 a = *reinterpret_cast<const float4*>(Xs + m * kLds + 32 + q4);
-      const float4 b = *reinterpret_cast<const float4*>(Xs + m * kLds + 48 + q4);
+      const float e = *X.at(32 + r, 32 + m);
+      const float4 a = *reinterpret_cast<const float4*>(X.at(m, 32 + q4));
+      const float4 b = *reinterpret_cast<const float4*>(X.at(m, 48 + q4));
       za.x = fmaf(e, a.x, za.x);
       za.y = fmaf(e, a.y, za.y);
       za.z = fmaf(e, a.z, za.z);
@@ -383,9 +391,9 @@ __device__ __forceinline__ void solve_inverse(const float* Ls, float* Xs, int ti
     if (r >= 16) {  // warp-uniform: rows 48-63 also take X[3, 2] and D_3
 #pragma unroll
       for (int m = 16; m < 32; ++m) {
-        const float e = erow[m];
-        const float4 a = *reinterpret_cast<const float4*>(Xs + m * kLds + 32 + q4);
-        const float4 b = *reinterpret_cast<const float4*>(Xs + m * kLds + 48 + q4);
+        const float e = *X.at(32 + r, 32 + m);
+        const float4 a = *reinterpret_cast<const float4*>(X.at(m, 32 + q4));
+        const float4 b = *reinterpret_cast<const float4*>(X.at(m, 48 + q4));
         za.x = fmaf(e, a.x, za.x);
         za.y = fmaf(e, a.y, za.y);
         za.z = fmaf(e, a.z, za.z);
@@ -396,8 +404,8 @@ __device__ __forceinline__ void solve_inverse(const float* Ls, float* Xs, int ti
         zb.w = fmaf(e, b.w, zb.w);
       }
     }
-    *reinterpret_cast<float4*>(Xs + (32 + r) * kLds + q4) = make_float4(-za.x, -za.y, -za.z, -za.w);
-    *reinterpret_cast<float4*>(Xs + (32 + r) * kLds + 16 + q4) = make_float4(-zb.x, -zb.y, -zb.z, -zb.w);
+    *reinterpret_cast<float4*>(X.at(32 + r, q4)) = make_float4(-za.x, -za.y, -za.z, -za.w);
+    *reinterpret_cast<float4*>(X.at(32 + r, 16 + q4)) = make_float4(-zb.x, -zb.y, -zb.z, -zb.w);
   }
   named_sync(bar, 128);
 }
@@ -405,14 +413,15 @@ __device__ __forceinline__ void solve_inverse(const float* Ls, float* Xs, int ti
 // T = X diag(beta) and TG = T diag(e^G) as MN-major ([s][t]) hi/lo bf16 tiles (hi at tile, lo at
 // tile + lo_off; shared or global memory), 128 threads: thread = (row s, token half).  Entries
 // above the diagonal are 0.
-__device__ __forceinline__ void write_t_tiles(const float* Xs, const ChunkParams& pc, int tid, uint8_t* t_tile,
+template <class XM>
+__device__ __forceinline__ void write_t_tiles(XM X, const ChunkParams& pc, int tid, uint8_t* t_tile,
                                               uint8_t* tg_tile, int t_lo_off = 8192, int tg_lo_off = 8192) {
   const int s = tid & 63, half = tid >> 6;
   float xv[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     const int t = 32 * half + i;
-    xv[i] = t >= s ? Xs[t * kLds + s] : 0.0f;
+    xv[i] = t >= s ? *X.at(t, s) : 0.0f;
   }
   const float w0 = pc.beta[s];
   const float w1 = w0 * pc.eg[s];
@@ -429,8 +438,8 @@ __device__ __forceinline__ void write_t_tiles(const float* Xs, const ChunkParams
 }
 
 // Row k of W^T (64 tokens, fp32 raw bits) -> row k of the -W hi/lo tiles ([k][t], hi at w_tile,
-// lo at w_tile + 16384)
-__device__ __forceinline__ void w_row(const uint32_t (&row)[64], int k, uint8_t* w_tile) {
+// lo at w_tile + lo_off)
+__device__ __forceinline__ void w_row(const uint32_t (&row)[64], int k, uint8_t* w_tile, int lo_off = 16384) {
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     uint32_t hi[16], lo[16];
@@ -438,7 +447,7 @@ __device__ __forceinline__ void w_row(const uint32_t (&row)[64], int k, uint8_t*
     for (int j = 0; j < 16; ++j)
       split_pack(-__uint_as_float(row[32 * half + 2 * j]), -__uint_as_float(row[32 * half + 2 * j + 1]), hi[j], lo[j]);
     store_half_row_sw128(w_tile, k, half, hi);
-    store_half_row_sw128(w_tile + 16384, k, half, lo);
+    store_half_row_sw128(w_tile + lo_off, k, half, lo);
   }
 }
 

@@ -637,14 +637,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (tid == 64) GDN_TRACE(35, c);
       if (!named_sync_and(3, 128, ready && ok)) { ok = false; break; }
       if (tid == 0) GDN_TRACE(9, c);
-      solve_inverse(Ls, Xs, tid, 3);
+      solve_inverse(Ls, PaddedRows{Xs}, tid, 3);
       if (tid == 0) GDN_TRACE(10, c);
       // --- T = X diag(beta) and T diag(e^G) as MN-major hi/lo tiles (row s, tokens t of one
       //     half).  The T tiles were last read by TV(c-1), the W tiles by the state terms(c-1).
       const bool free_tiles = (c == 0) || wait_c_warp(bars.x_ready, c - 1, p.status, kDevTimeoutMma);
       if (!named_sync_and(3, 128, free_tiles)) { ok = false; break; }
       if (tid == 0) GDN_TRACE(22, c);
-      write_t_tiles(Xs, params[c & 1], tid, smem + kOffT, smem + kOffL);  // T diag(e^G) over the dead L
+      write_t_tiles(PaddedRows{Xs}, params[c & 1], tid, smem + kOffT, smem + kOffL);  // T diag(e^G) over the dead L
       if (tid == 0) GDN_TRACE(27, c);
       fence_async_smem();
       named_sync(3, 128);

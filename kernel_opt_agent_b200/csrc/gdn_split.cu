@@ -42,7 +42,13 @@ constexpr int kPL = 32768;                    // L fp32 (row stride kLds); then 
 constexpr int kPX = kPL + 64 * kLds * 4;      // X = (I + L)^-1 fp32
 constexpr int kPParams = kPX + 64 * kLds * 4;
 constexpr int kPSmem = kPParams + kParamsBytes;
-static_assert(kPL % 1024 == 0 && 3 * (kPSmem + 1024 + 64) <= 228 * 1024, "prep layout: three CTAs per SM");
+constexpr int kPrepCtasPerSm = 3;
+static_assert(kPL % 1024 == 0 && kPX % 16 == 0 && kPrepCtasPerSm * (kPSmem + 1024 + 64) <= 228 * 1024,
+              "prep layout: three CTAs per SM");
+// The record leaves shared memory by bulk copies, each tile staged as its exact image in a region
+// that is dead by then: e^G Q in place in the Q rows; T hi | lo in the Q rows once that copy has
+// read them; after T2, -W hi in L, -W lo in X and P in the K rows of box 0.
+constexpr int kPQ0 = kPSlot + 8192, kPQ1 = kPSlot + 24576;  // the Q rows of boxes 0 and 1 (8 KB each)
 
 // ---- chain kernel
 constexpr int kChainThreads = 320;            // warps 0-7 passes, 8 loader, 9 MMA issuer
@@ -60,6 +66,13 @@ constexpr int kTrChunks = 64, kTrEvents = 16;
 __device__ unsigned long long g_split_trace[kTrEvents * kTrChunks];
 __device__ unsigned long long g_cta_end[1024];    // %globaltimer at the end of each CTA
 __device__ unsigned long long g_cta_start[1024];  // %globaltimer at the start of each CTA
+__device__ unsigned long long g_rec_start[2048];  // %globaltimer: overlapped launch, record rid begun
+__device__ unsigned long long g_rec_end[2048];    // ... and published
+__device__ unsigned long long g_chain_issue[64];  // ... chain CTA 0's loader: chunk c's copies issued
+#define OVL_TRACE(arr, i, n)                                      \
+  do {                                                            \
+    if ((i) >= 0 && (i) < (n)) arr[(i)] = global_timer_ns();       \
+  } while (0)
 #define SPLIT_TRACE(ev, c)                                                                               \
   do {                                                                                                   \
     if (blockIdx.x == 0 && (c) < kTrChunks) g_split_trace[(ev) * kTrChunks + (c)] = clock64();          \
@@ -67,6 +80,9 @@ __device__ unsigned long long g_cta_start[1024];  // %globaltimer at the start o
 #else
 #define SPLIT_TRACE(ev, c) \
   do {                     \
+  } while (0)
+#define OVL_TRACE(arr, i, n) \
+  do {                       \
   } while (0)
 #endif
 #ifdef TOKMIX_GDN_TRACE
@@ -160,6 +176,18 @@ __device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t 
                : "memory");
 }
 
+// bulk copy shared -> global in the issuing thread's bulk group (both addresses 16-byte aligned,
+// bytes a multiple of 16); bulk_commit closes the group, bulk_wait_read waits until every committed
+// group has read its shared memory, bulk_wait until their global writes are done
+__device__ __forceinline__ void bulk_s2g(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // One record: the preparation of chunk gc of value head h by a group of 128 threads (group-local
 // `tid`; the group's warp w must sit on TMEM lane quadrant w).  `smem` is the group's 1024-byte
 // aligned region of kPSmem bytes, `tbase` its 64 TMEM columns, `bar_id` its named barrier;
@@ -189,7 +217,7 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
   const int kh = h % p.hk;
   ChunkParams& pc = *reinterpret_cast<ChunkParams*>(smem + kPParams);
   float* Ls = reinterpret_cast<float*>(smem + kPL);
-  float* Xs = reinterpret_cast<float*>(smem + kPX);
+  const PaddedRows X{reinterpret_cast<float*>(smem + kPX)};
   uint8_t* rec = p.ws + (static_cast<size_t>(gc) * p.hv + h) * kRecBytes;
 
   if (tid == 0) {
@@ -209,8 +237,6 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
   }
   named_sync(bar_id, 128);
   PREP_TRACE(1);
-  if (tid < kParamsBytes / 16)
-    reinterpret_cast<uint4*>(rec + kRecParams)[tid] = reinterpret_cast<const uint4*>(smem + kPParams)[tid];
   // --- qk_l2norm: thread = row of the staged [K; Q] tile, normalised in place once it landed
   if (p.l2norm) {
     const bool landed = __all_sync(0xffffffffu, mbar_wait(bar_in, in_parity, p.status, kDevTimeoutTma));
@@ -234,33 +260,44 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
     umma_commit(bar_mma);
     PREP_TRACE(2);
   }
-  // --- read-out: rows 0-63 (K K^T) -> L, rows 64-127 (Q K^T) -> P and e^G-scaled Q
+  // --- read-out: rows 0-63 (K K^T) -> L; the Q rows scaled in place to scale e^G Q, which a bulk
+  //     copy stores.  Q K^T stays in TMEM columns 0-63 until P is formed at the end.
   bool ok = __all_sync(0xffffffffu, mbar_wait(bar_mma, 0, p.status, kDevTimeoutMma));
   PREP_TRACE(3);
   if (ok) {
-    tc_fence_after();
-    uint32_t row[64];
-    tmem_ld64(tmem_addr(tbase, warp * 32, 0), row);
     if (tid < 64) {
+      tc_fence_after();
+      uint32_t row[64];
+      tmem_ld64(tmem_addr(tbase, warp * 32, 0), row);
       l_row(row, pc, tid, Ls);
     } else {
       const int t = tid - 64;
-      p_row(row, pc, t, p.scale, rec + kRecP);
-      scale_row_copy(smem + kPSlot + 8192 + t * 128, 16384, rec + kRecQ + t * 128, 8192, pc.eg[t] * p.scale);
+      scale_row_inplace(smem + kPQ0 + t * 128, kPQ1 - kPQ0, pc.eg[t] * p.scale);
     }
   }
+  fence_async_smem();  // the scaled Q rows -> the bulk copy
   tc_fence_before();
   ok = named_sync_and(bar_id, 128, ok);
   if (!ok) return false;
+  if (tid == 0) {
+    bulk_s2g(rec + kRecQ, smem + kPQ0, 8192);
+    bulk_s2g(rec + kRecQ + 8192, smem + kPQ1, 8192);
+    bulk_commit();
+  }
   PREP_TRACE(4);
-  solve_inverse(Ls, Xs, tid, bar_id);
+  solve_inverse(Ls, X, tid, bar_id);
   PREP_TRACE(5);
-  write_t_tiles(Xs, pc, tid, rec + kRecT, smem + kPL);  // T to the record, T diag(e^G) over the dead L
+  if (tid == 0) bulk_wait_read();  // the Q rows are free for the T tiles
+  named_sync(bar_id, 128);
+  write_t_tiles(X, pc, tid, smem + kPQ0, smem + kPL, kPQ1 - kPQ0);  // T -> the Q rows, T diag(e^G) over the dead L
   fence_async_smem();
   named_sync(bar_id, 128);
   PREP_TRACE(6);
-  // --- T2: W^T = K^T (TG_hi + TG_lo)^T
+  // --- T2: W^T = K^T (TG_hi + TG_lo)^T into TMEM columns 64-127; the T tiles leave meanwhile
   if (tid == 0) {
+    bulk_s2g(rec + kRecT, smem + kPQ0, 8192);
+    bulk_s2g(rec + kRecT + 8192, smem + kPQ1, 8192);
+    bulk_commit();
     tc_fence_after();
     const uint32_t id = make_idesc(128, 64, 1, 1, 1);
     const uint32_t kt = smem_u32(smem + kPSlot), tg = smem_u32(smem + kPL);
@@ -268,26 +305,39 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
     for (int part = 0; part < 2; ++part)
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
-        umma_bf16_ss(tbase, make_sdesc_sw128(kt + kk * 2048, 16384, 1024),
+        umma_bf16_ss(tbase + 64, make_sdesc_sw128(kt + kk * 2048, 16384, 1024),
                      make_sdesc_sw128(tg + part * 8192 + kk * 2048, 16384, 1024), id, (part > 0 || kk > 0) ? 1u : 0u);
     umma_commit(bar_mma);
     PREP_TRACE(7);
   }
+  // --- -W hi | lo -> the dead L | X, P -> the dead K rows of box 0 (T2 has read K, TG, X)
   ok = __all_sync(0xffffffffu, mbar_wait(bar_mma, 1, p.status, kDevTimeoutMma));
   PREP_TRACE(8);
   if (ok) {
     tc_fence_after();
     uint32_t row[64];
-    tmem_ld64(tmem_addr(tbase, warp * 32, 0), row);
-    w_row(row, tid, rec + kRecW);
+    tmem_ld64(tmem_addr(tbase, warp * 32, 64), row);
+    w_row(row, tid, smem + kPL, kPX - kPL);
+    if (tid >= 64) {
+      tmem_ld64(tmem_addr(tbase, warp * 32, 0), row);
+      p_row(row, pc, tid - 64, p.scale, smem + kPSlot);
+    }
   }
+  fence_async_smem();
   tc_fence_before();
-  ok = named_sync_and(bar_id, 128, ok);  // every TMEM read and smem use of this record is done
+  ok = named_sync_and(bar_id, 128, ok);  // every TMEM read and staged tile of this record is done
+  if (ok && tid == 0) {
+    bulk_s2g(rec + kRecW, smem + kPL, 16384);
+    bulk_s2g(rec + kRecW + 16384, smem + kPX, 16384);
+    bulk_s2g(rec + kRecP, smem + kPSlot, 8192);
+    bulk_s2g(rec + kRecParams, smem + kPParams, kParamsBytes);
+    bulk_commit();
+  }
   PREP_TRACE(9);
   return ok;
 }
 
-__global__ void __launch_bounds__(kPrepThreads, 3)
+__global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
     gdn_prep_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                     const PrepParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -304,7 +354,7 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
     tma_prefetch_desc(&map_k);
   }
   if (warp == 0) {
-    tmem_alloc(&tmem_base_shared, 64);
+    tmem_alloc(&tmem_base_shared, 128);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -312,11 +362,12 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
   tc_fence_after();
   const uint32_t tbase = tmem_base_shared;
   prep_record(&map_q, &map_k, p, blockIdx.x, blockIdx.y, smem, &bar_in, 0, &bar_mma, tbase, tid, 1);
+  if (tid == 0) bulk_wait();  // the record's bulk copies have read shared memory and written it out
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tbase, 64);
+    tmem_dealloc(tbase, 128);
   }
 }
 
@@ -478,6 +529,7 @@ __device__ __forceinline__ void chain_unit(const CUtensorMap* map_k, const CUten
           tma_load_3d(st + kSK + bx * 8192, map_k, bar, bx * 64, kh, tok0 + c * kC);
           if (!zero_v) tma_load_3d(st + kSV + bx * 8192, map_v, bar, bx * 64, h, tok0 + c * kC);
         }
+        if (blockIdx.x == 0) OVL_TRACE(g_chain_issue, c, 64);
         issued = c + 1;
       }
       for (int c = max(0, issued - 2); c < issued; ++c) mbar_drain(&bars.full[c & 1], (c >> 1) & 1);
@@ -816,13 +868,13 @@ __global__ void __launch_bounds__(kOverlapThreads, 1)
     tma_prefetch_desc(&map_k);
   }
   if (warp == 0) {
-    tmem_alloc(&tmem_base_shared, 256);
+    tmem_alloc(&tmem_base_shared, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tbase = tmem_base_shared + 64 * grp;
+  const uint32_t tbase = tmem_base_shared + 128 * grp;
   // Slot (group, CTA) takes records grp * nprep + cta, + stride, ...: the first records -- the
   // chains' first chunk -- land one per SM, on groups 0; all groups start at once.
   const int nprep = gridDim.x - op.units;
@@ -837,19 +889,29 @@ __global__ void __launch_bounds__(kOverlapThreads, 1)
       continue;
     }
     const int gc = rid / pp.hv, h = rid - gc * pp.hv;
+    if (tid == 0) OVL_TRACE(g_rec_start, rid, 2048);
     ok = prep_record(&map_q, &map_k, pp, gc, h, smem + grp * kPSmemA, &pbar[grp][0], k & 1, &pbar[grp][1], tbase, tid,
                      1 + grp);
-    if (ok && tid == 0) {  // every thread's record stores precede prep_record's final group barrier
-      __threadfence();
-      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(op.flags + rid), "r"(1u) : "memory");
+    if (tid == 0) {
+      // the record's bulk copies are written out (and have read the group's shared memory, which
+      // the next record's loads overwrite); the direct stores of k_normed precede prep_record's
+      // final group barrier
+      bulk_wait();
+      if (ok) {
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence();
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(op.flags + rid), "r"(1u) : "memory");
+        OVL_TRACE(g_rec_end, rid, 2048);
+      }
     }
+    named_sync(1 + grp, 128);  // no thread writes the next record's parameters before the copies read them
   }
   tc_fence_before();
   __syncthreads();
   CTA_END_TRACE();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem_base_shared, 256);
+    tmem_dealloc(tmem_base_shared, 512);
   }
 }
 
@@ -867,6 +929,15 @@ extern "C" int tokmix_gdn_split_cta_start_read(unsigned long long* host, int n) 
   using namespace tokmix::gdn::split;
   const int count = n < 1024 ? n : 1024;
   return cudaMemcpyFromSymbol(host, g_cta_start, sizeof(unsigned long long) * count) == cudaSuccess ? count : -1;
+}
+extern "C" int tokmix_gdn_overlap_trace_read(unsigned long long* host, int n) {
+  using namespace tokmix::gdn::split;
+  if (n < 2048 * 2 + 64) return -1;
+  if (cudaMemcpyFromSymbol(host, g_rec_start, sizeof(unsigned long long) * 2048) != cudaSuccess ||
+      cudaMemcpyFromSymbol(host + 2048, g_rec_end, sizeof(unsigned long long) * 2048) != cudaSuccess ||
+      cudaMemcpyFromSymbol(host + 4096, g_chain_issue, sizeof(unsigned long long) * 64) != cudaSuccess)
+    return -1;
+  return 2048 * 2 + 64;
 }
 extern "C" int tokmix_gdn_prep_trace_read(unsigned long long* host, int n) {
   using namespace tokmix::gdn::split;
