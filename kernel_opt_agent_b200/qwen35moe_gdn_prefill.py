@@ -64,18 +64,21 @@ KERNEL_TYPE = "qwen35moe_gdn_prefill"
 D = 128
 H_K = 16
 H_V = 32
-_SPLIT_MAX_WORKSPACE = 8 << 30  # bytes; larger problems use the one-launch schedule
+# bytes; larger problems use the one-launch schedule.  75 KB per (chunk, value head): 24 GiB covers a
+# batch of 16 sequences of 16384 tokens at 32 value heads (9.8 GB), an eighth of a B200's memory.
+_SPLIT_MAX_WORKSPACE = 24 << 30
 # Costs measured on a B200 (microseconds), from which "auto" predicts each schedule's time when
 # every unit fits on the SMs at once: a chunk of the fused kernel's chain (preparation inside the
 # CTA; 277 us / 32 chunks at B1 T2048, 2.9 ms / 347 chunks on a varlen slice), a chunk of the chain
 # fed from prepared records (split B1 T2048: 140 us = 44 preparation + 32 chunks + gap), one
-# preparation record with three preparation groups per SM (alone: 49 us for 1024 records, 308 us
-# for 7364; beside the chains of the overlapped launch: 1.51 ms for the 14,728 records of a 4-GPU
-# varlen slice), the overlapped launch's start-up, and the gap between launches.
+# preparation record with three preparation groups per SM (alone: 288 us for 7364 records; beside
+# the chains of the overlapped launch, whose first round of records runs in lockstep: 27 us for the
+# first records, 18 us each after that), the overlapped launch's start-up, and the gap between
+# launches.
 _US_FUSED_CHUNK = 8.5
 _US_FUSED_CHUNK_WAVES = 10.2  # per chunk and unit when the units run in several waves (varlen, one GPU: 4.07 ms)
 _US_CHAIN_CHUNK = 2.7
-_US_PREP_RECORD = 19.0
+_US_PREP_RECORD = 17.5
 _US_PREP_RECORD_OVERLAP = 24.0
 _US_OVERLAP_START = 20.0
 _US_SPLIT_GAP = 10.0
