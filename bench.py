@@ -28,7 +28,8 @@ torch.cuda.synchronize(); each step is timed with CUDA events on the launching s
 L2 cache (126 MB) is flushed by writing a 256 MB buffer between steps when the step's inputs fit
 in L2.  The step time is the max over ranks.  `e2e` repeats the headline step through the public
 plugin call from pinned host buffers, host->device copies of the inputs and device->host copies
-of the outputs inside the timed region.
+of the outputs inside the timed region, as a serving loop runs them: each step's uploads overlap
+the previous step's kernel and read-back (two copy streams, two input buffers).
 """
 
 from __future__ import annotations
@@ -218,6 +219,67 @@ def time_steps(step_fn, steps, warmup, device, flush: bool, collective: bool = T
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_s = sum(per) / 1e3
     return (max_over_ranks(total_s, device) if collective else total_s), per
+
+
+PIPELINE_NOTE = ("each step uploads its inputs and reads back its results; step i+1's uploads run beside step "
+                 "i's kernel and read-back (two copy streams, two input buffers)")
+
+
+def time_pipelined(upload, compute, download, steps, warmup, device, collective: bool = True):
+    """End-to-end steps as a serving loop runs them: step i's uploads (host -> device, on one copy
+    stream, into input buffer i % 2) run beside step i-1's kernel and step i-2's read-back (device ->
+    host, on a second copy stream), ordered by events; every step still uploads its own inputs and
+    reads back its own results.  upload(b) and download(b, outs) issue copies on the current stream
+    (set to the copy stream by the caller), compute(b) runs the kernel on the device's current
+    stream and returns the output tensors.  Returns the max-over-ranks seconds of the K timed steps:
+    from an event the first upload waits on to the end of the last read-back."""
+    s_c = torch.cuda.current_stream(device)
+    s_up, s_dn = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    comp_done = [None, None]
+
+    def run(n, first_wait=None):
+        last = None
+        for i in range(n):
+            b = i & 1
+            with torch.cuda.stream(s_up):
+                if i == 0 and first_wait is not None:
+                    s_up.wait_event(first_wait)
+                if comp_done[b] is not None:  # the kernel that last read buffer b is done
+                    s_up.wait_event(comp_done[b])
+                upload(b)
+            up = torch.cuda.Event()
+            up.record(s_up)
+            s_c.wait_event(up)
+            outs = compute(b)
+            done = torch.cuda.Event()
+            done.record(s_c)
+            comp_done[b] = done
+            s_dn.wait_event(done)
+            with torch.cuda.stream(s_dn):
+                for t in outs:
+                    t.record_stream(s_dn)
+                download(b, outs)
+            last = torch.cuda.Event(enable_timing=True)
+            last.record(s_dn)
+        return last
+
+    run(warmup)
+    torch.cuda.synchronize(device)
+    if collective:
+        barrier()
+    torch.cuda.synchronize(device)
+    start = torch.cuda.Event(enable_timing=True)
+    start.record(s_c)
+    end_dn = run(steps, first_wait=start)
+    s_c.wait_event(end_dn)
+    end = torch.cuda.Event(enable_timing=True)
+    end.record(s_c)
+    torch.cuda.synchronize(device)
+    if collective:
+        barrier()
+    torch.cuda.synchronize(device)
+    total_s = start.elapsed_time(end) / 1e3
+    return max_over_ranks(total_s, device) if collective else total_s
 
 
 # ----------------------------------------------------------------------------- workloads
@@ -413,23 +475,28 @@ def sdpa_comparators(inp, flops, steps, warmup, device):
 
 
 def e2e_fa2(device, inp, steps, warmup, flops_total):
-    """FA2 step through the public plugin call from pinned host memory: q, k, v host->device,
-    kernel_fn, the output device->host, all inside the timed region."""
+    """FA2 step through the public plugin call from pinned host memory: every step uploads q, k, v,
+    runs kernel_fn and reads back the output, pipelined as a serving loop runs it (time_pipelined)."""
     host = {n: inp[n].cpu().pin_memory() for n in ("q", "k", "v")}
-    dev_bufs = {n: torch.empty_like(t, device=device) for n, t in host.items()}
-    out_host = torch.empty(host["q"].shape, dtype=torch.bfloat16).pin_memory()
+    dev_bufs = [{n: torch.empty_like(t, device=device) for n, t in host.items()} for _ in range(2)]
+    out_host = [torch.empty(host["q"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = out_host.numel() * 2
+    d2h = out_host[0].numel() * 2
 
-    def step():
-        for n, t in dev_bufs.items():
+    def upload(b):
+        for n, t in dev_bufs[b].items():
             t.copy_(host[n], non_blocking=True)
-        out = fa2.kernel_fn(dev_bufs["q"], dev_bufs["k"], dev_bufs["v"], causal=True, sm_scale=inp["sm_scale"])
-        out_host.copy_(out, non_blocking=True)
 
-    total_s, _ = time_steps(step, steps, warmup, device, flush=False)
+    def compute(b):
+        d = dev_bufs[b]
+        return (fa2.kernel_fn(d["q"], d["k"], d["v"], causal=True, sm_scale=inp["sm_scale"]),)
+
+    def download(b, outs):
+        out_host[b].copy_(outs[0], non_blocking=True)
+
+    total_s = time_pipelined(upload, compute, download, steps, warmup, device)
     return {"value": flops_total * steps / total_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": total_s / steps * 1e3}
+            "d2h_bytes_per_step": d2h, "ms_per_step": total_s / steps * 1e3, "pipelined": PIPELINE_NOTE}
 
 
 def cpu_fa2_sample(s=8192, d=128, group=4, repeats=1):
@@ -536,26 +603,34 @@ ONE_GPU_WORKLOADS = list(ROW_OPS) + ["fa2_d256_b16_s4096"]
 
 
 def e2e_gdn_b1(device, rank, world, steps, warmup, inp):
-    """Headline step through the public plugin call from pinned host memory."""
+    """Headline step through the public plugin call from pinned host memory: every step uploads
+    its inputs, runs kernel_fn and reads back the output and final state, pipelined as a serving
+    loop runs it (time_pipelined)."""
     host = {k: (v.cpu().pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
-    dev_bufs = {k: torch.empty_like(v, device=device) for k, v in host.items() if isinstance(v, torch.Tensor)}
-    out_host = torch.empty((1, 2048, HV, D), dtype=torch.bfloat16).pin_memory()
-    st_host = torch.empty((1, HV, D, D), dtype=torch.float32).pin_memory()
+    dev_bufs = [{k: torch.empty_like(v, device=device) for k, v in host.items() if isinstance(v, torch.Tensor)}
+                for _ in range(2)]
+    out_host = [torch.empty((1, 2048, HV, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    st_host = [torch.empty((1, HV, D, D), dtype=torch.float32).pin_memory() for _ in range(2)]
     h2d = sum(v.numel() * v.element_size() for v in host.values() if isinstance(v, torch.Tensor))
-    d2h = out_host.numel() * 2 + st_host.numel() * 4
+    d2h = out_host[0].numel() * 2 + st_host[0].numel() * 4
 
-    def step():
-        for k, v in dev_bufs.items():
+    def upload(b):
+        for k, v in dev_bufs[b].items():
             v.copy_(host[k], non_blocking=True)
-        args = dict(dev_bufs)
+
+    def compute(b):
+        args = dict(dev_bufs[b])
         args["scale"] = host["scale"]
         out, fs = gdn.kernel_fn(**args)
-        out_host.copy_(out, non_blocking=True)
-        st_host.copy_(fs, non_blocking=True)
+        return out, fs
 
-    total_s, _ = time_steps(step, steps, warmup, device, flush=True)
+    def download(b, outs):
+        out_host[b].copy_(outs[0], non_blocking=True)
+        st_host[b].copy_(outs[1], non_blocking=True)
+
+    total_s = time_pipelined(upload, compute, download, steps, warmup, device)
     return {"value": 2048 * world * steps / total_s / 1e6, "unit": "Mtok/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": total_s / steps * 1e3}
+            "d2h_bytes_per_step": d2h, "ms_per_step": total_s / steps * 1e3, "pipelined": PIPELINE_NOTE}
 
 
 # ----------------------------------------------------------------------------- CPU baseline

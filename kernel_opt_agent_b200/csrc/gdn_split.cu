@@ -275,6 +275,7 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
       scale_row_inplace(smem + kPQ0 + t * 128, kPQ1 - kPQ0, pc.eg[t] * p.scale);
     }
   }
+  PREP_TRACE(12);
   fence_async_smem();  // the scaled Q rows -> the bulk copy
   tc_fence_before();
   ok = named_sync_and(bar_id, 128, ok);
@@ -323,9 +324,11 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
       p_row(row, pc, tid - 64, p.scale, smem + kPSlot);
     }
   }
+  PREP_TRACE(10);
   fence_async_smem();
   tc_fence_before();
   ok = named_sync_and(bar_id, 128, ok);  // every TMEM read and staged tile of this record is done
+  PREP_TRACE(11);
   if (ok && tid == 0) {
     bulk_s2g(rec + kRecW, smem + kPL, 16384);
     bulk_s2g(rec + kRecW + 16384, smem + kPX, 16384);
