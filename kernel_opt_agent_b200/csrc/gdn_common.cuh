@@ -219,12 +219,11 @@ __device__ __forceinline__ void l_row(const uint32_t (&row)[64], const ChunkPara
   }
 }
 
-// Row t of P = scale exp(G_t - G_s) (q_t . k_s), s <= t, from row t of Q K^T -> the P tile
-// ([t][s] bf16, 128-byte swizzle)
-__device__ __forceinline__ void p_row(const uint32_t (&row)[64], const ChunkParams& pc, int t, float scale,
-                                      uint8_t* p_tile) {
+// Row t of P = scale exp(G_t - G_s) (q_t . k_s), s <= t, from row t of Q K^T, as 32 packed bf16
+// pairs (p_row below stores it)
+__device__ __forceinline__ void p_row_pack(const uint32_t (&row)[64], const ChunkParams& pc, int t, float scale,
+                                           uint32_t (&prow)[32]) {
   const float gt = pc.g2[t];
-  uint32_t prow[32];
 #pragma unroll
   for (int j = 0; j < 32; j += 2) {
     const int s0 = 2 * j;
@@ -236,6 +235,13 @@ __device__ __forceinline__ void p_row(const uint32_t (&row)[64], const ChunkPara
     prow[j] = pack_bf16x2(p0, p1);
     prow[j + 1] = pack_bf16x2(p2, p3);
   }
+}
+
+// Row t of P (above) -> the P tile ([t][s] bf16, 128-byte swizzle)
+__device__ __forceinline__ void p_row(const uint32_t (&row)[64], const ChunkParams& pc, int t, float scale,
+                                      uint8_t* p_tile) {
+  uint32_t prow[32];
+  p_row_pack(row, pc, t, scale, prow);
   store_row_sw128(p_tile, t, prow);
 }
 
@@ -298,16 +304,22 @@ struct PaddedRows {  // rows of kLds floats
   __device__ __forceinline__ float* at(int r, int c) const { return p + r * kLds + c; }
 };
 
+struct NoSideWork {
+  __device__ __forceinline__ void operator()(int) const {}
+};
+
 // X = (I + L)^-1 (unit lower triangular, fp32), 128 threads meeting at named barrier `bar`, by
 // recursive doubling over 16x16 blocks: the four diagonal blocks D_b by forward substitution
-// (one column per thread of the second half of the group); the two 32x32 diagonal blocks E_0,
+// (one column per thread of threads [d_lo, d_lo + 64); the other 64 threads run side(tid)
+// meanwhile, which must not touch L or X); the two 32x32 diagonal blocks E_0,
 // E_1 from X[2p+1, 2p] = -D_{2p+1} L[2p+1, 2p] D_{2p}; the lower 32x32 block as -E_1 L[1, 0] E_0.
 // Products are staged in X's strictly upper blocks, which nothing else reads; the diagonal
 // blocks hold explicit zeros above their diagonal.  Ends with a barrier: X is complete.
-template <class XM>
-__device__ __forceinline__ void solve_inverse(const float* Ls, XM X, int tid, int bar) {
-  if (tid >= 64) {
-    const int b = (tid - 64) >> 4, j = tid & 15;
+template <class XM, class Side = NoSideWork>
+__device__ __forceinline__ void solve_inverse(const float* Ls, XM X, int tid, int bar, int d_lo = 64,
+                                              Side side = Side{}) {
+  if (tid >= d_lo && tid < d_lo + 64) {
+    const int b = (tid - d_lo) >> 4, j = tid & 15;
     const float* lb16 = Ls + 16 * b * kLds + 16 * b;
     float acc[16];
 #pragma unroll
@@ -320,6 +332,8 @@ __device__ __forceinline__ void solve_inverse(const float* Ls, XM X, int tid, in
     }
 #pragma unroll
     for (int i = 0; i < 16; ++i) *X.at(16 * b + i, 16 * b + j) = acc[i];
+  } else {
+    side(tid);
   }
   named_sync(bar, 128);
   {  // pairs p: X[R + rr][C + c4..c4+3], R = 16(2p+1), C = 32p

@@ -86,13 +86,21 @@ __device__ unsigned long long g_chain_issue[64];  // ... chain CTA 0's loader: c
   } while (0)
 #endif
 #ifdef TOKMIX_GDN_TRACE
-// prep phases of CTAs (x < 8, y = 0) of the two-launch schedule, by thread 0 (SM clock)
+// prep phases of the records of chunks [X0, X0 + 8) and value head Y prepared by the preparation
+// launch (named barrier 1), by thread 0 (SM clock)
+#ifndef TOKMIX_PREP_TRACE_Y
+#define TOKMIX_PREP_TRACE_Y 0
+#endif
+#ifndef TOKMIX_PREP_TRACE_X0
+#define TOKMIX_PREP_TRACE_X0 0
+#endif
 constexpr int kPrepTrCtas = 8, kPrepTrEvents = 16;
 __device__ unsigned long long g_prep_trace[kPrepTrCtas * kPrepTrEvents];
 #define PREP_TRACE(ev)                                                                         \
   do {                                                                                         \
-    if (gridDim.y > 1 && blockIdx.y == 0 && blockIdx.x < kPrepTrCtas && tid == 0)              \
-      g_prep_trace[blockIdx.x * kPrepTrEvents + (ev)] = clock64();                             \
+    if (bar_id == 1 && h == TOKMIX_PREP_TRACE_Y && gc >= TOKMIX_PREP_TRACE_X0 &&                      \
+        gc < TOKMIX_PREP_TRACE_X0 + kPrepTrCtas && tid == 0)                                           \
+      g_prep_trace[(gc - TOKMIX_PREP_TRACE_X0) * kPrepTrEvents + (ev)] = clock64();               \
   } while (0)
 #else
 #define PREP_TRACE(ev) \
@@ -286,7 +294,15 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
     bulk_commit();
   }
   PREP_TRACE(4);
-  solve_inverse(Ls, X, tid, bar_id);
+  // the solve's diagonal blocks on warps 0-1; meanwhile warps 2-3 (TMEM lanes 64-127) form their
+  // row of P from Q K^T, kept in registers until the K rows are free after T2
+  uint32_t prow[32];
+  solve_inverse(Ls, X, tid, bar_id, 0, [&](int t) {
+    tc_fence_after();
+    uint32_t row[64];
+    tmem_ld64(tmem_addr(tbase, warp * 32, 0), row);
+    p_row_pack(row, pc, t - 64, p.scale, prow);
+  });
   PREP_TRACE(5);
   if (tid == 0) bulk_wait_read();  // the Q rows are free for the T tiles
   named_sync(bar_id, 128);
@@ -319,10 +335,7 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
     uint32_t row[64];
     tmem_ld64(tmem_addr(tbase, warp * 32, 64), row);
     w_row(row, tid, smem + kPL, kPX - kPL);
-    if (tid >= 64) {
-      tmem_ld64(tmem_addr(tbase, warp * 32, 0), row);
-      p_row(row, pc, tid - 64, p.scale, smem + kPSlot);
-    }
+    if (tid >= 64) store_row_sw128(smem + kPSlot, tid - 64, prow);
   }
   PREP_TRACE(10);
   fence_async_smem();
@@ -340,9 +353,13 @@ __device__ __forceinline__ bool prep_record(const CUtensorMap* map_q, const CUte
   return ok;
 }
 
+// Persistent: CTA i prepares records i, i + gridDim.x, ... of the `records` = total chunks x heads_v
+// records in chunk-major order (record r = chunk r / hv, value head r % hv, so the value heads of a
+// key head, which load the same q and k rows, are prepared together).  Barriers, TMEM and the
+// tensor maps are set up once per CTA.
 __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
     gdn_prep_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                    const PrepParams p) {
+                    const PrepParams p, int records) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar_in, bar_mma;
@@ -364,8 +381,16 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = tmem_base_shared;
-  prep_record(&map_q, &map_k, p, blockIdx.x, blockIdx.y, smem, &bar_in, 0, &bar_mma, tbase, tid, 1);
-  if (tid == 0) bulk_wait();  // the record's bulk copies have read shared memory and written it out
+  uint32_t k = 0;
+  for (int r = blockIdx.x; r < records; r += gridDim.x, ++k) {
+    const int gc = r / p.hv, h = r - gc * p.hv;
+    const bool ok = prep_record(&map_q, &map_k, p, gc, h, smem, &bar_in, k & 1, &bar_mma, tbase, tid, 1);
+    // the record's bulk copies have read shared memory before the next record's loads and
+    // parameter writes reuse it (their global writes complete on their own, before the launch ends)
+    if (tid == 0) bulk_wait_read();
+    named_sync(1, kPrepThreads);
+    if (!ok) break;
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -1110,8 +1135,9 @@ extern "C" int tokmix_gdn_prefill_split(const void* q, const void* k, const void
     const int smem = kPSmem + 1024;
     if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_prep_kernel), smem))
       return check_launch("tokmix_gdn_prefill_split: cudaFuncSetAttribute (prep)");
-    gdn_prep_kernel<<<dim3(static_cast<unsigned>(total_chunks), static_cast<unsigned>(heads_v)), kPrepThreads, smem, s>>>(
-        mq, mk, pp);
+    const int records = total_chunks * heads_v;
+    const int grid = std::min(records, kPrepCtasPerSm * std::max(1, device_sm_count()));
+    gdn_prep_kernel<<<grid, kPrepThreads, smem, s>>>(mq, mk, pp, records);
     if (const int rc = check_launch("tokmix_gdn_prefill_split (prep)")) return rc;
   }
   const int smem = kCSmem + 1024;
@@ -1365,8 +1391,9 @@ extern "C" int tokmix_gdn_prefill_segmented(const void* q, const void* k, const 
     const int smem = kPSmem + 1024;
     if (!ensure_smem_attr(reinterpret_cast<const void*>(&gdn_prep_kernel), smem))
       return check_launch("tokmix_gdn_prefill_segmented: cudaFuncSetAttribute (prep)");
-    gdn_prep_kernel<<<dim3(static_cast<unsigned>(total_chunks), static_cast<unsigned>(heads_v)), kPrepThreads, smem, s>>>(
-        mq, mk, pp);
+    const int records = total_chunks * heads_v;
+    const int grid = std::min(records, kPrepCtasPerSm * std::max(1, device_sm_count()));
+    gdn_prep_kernel<<<grid, kPrepThreads, smem, s>>>(mq, mk, pp, records);
     if (const int rc = check_launch("tokmix_gdn_prefill_segmented (prep)")) return rc;
   }
   ChainParams cp{};
