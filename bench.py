@@ -221,8 +221,29 @@ def time_steps(step_fn, steps, warmup, device, flush: bool, collective: bool = T
     return (max_over_ranks(total_s, device) if collective else total_s), per
 
 
-PIPELINE_NOTE = ("each step uploads its inputs and reads back its results; step i+1's uploads run beside step "
-                 "i's kernel and read-back (two copy streams, two input buffers)")
+def stage_arenas(tensors, device):
+    """A step's inputs staged in one pinned host buffer (filled with `tensors`' values) and two
+    device buffers of the same layout, so that a step uploads them with one copy; returns (host
+    buffer, [device buffers], views) where views(buffer) gives the tensors as views of a buffer
+    (256-byte aligned)."""
+    offsets, total = {}, 0
+    for k, v in tensors.items():
+        offsets[k] = total
+        total += -(-v.numel() * v.element_size() // 256) * 256
+
+    def views(arena):
+        return {k: arena[offsets[k]:offsets[k] + v.numel() * v.element_size()].view(v.dtype).view(v.shape)
+                for k, v in tensors.items()}
+
+    host_arena = torch.empty(total, dtype=torch.uint8).pin_memory()
+    for k, v in views(host_arena).items():
+        v.copy_(tensors[k].cpu())
+    return host_arena, [torch.empty(total, dtype=torch.uint8, device=device) for _ in range(2)], views
+
+
+PIPELINE_NOTE = ("each step uploads its inputs (staged in one pinned buffer: one copy) and reads back its "
+                 "results; step i+1's upload runs beside step i's kernel and read-back (two copy streams, two "
+                 "input buffers)")
 
 
 def time_pipelined(upload, compute, download, steps, warmup, device, collective: bool = True):
@@ -477,15 +498,15 @@ def sdpa_comparators(inp, flops, steps, warmup, device):
 def e2e_fa2(device, inp, steps, warmup, flops_total):
     """FA2 step through the public plugin call from pinned host memory: every step uploads q, k, v,
     runs kernel_fn and reads back the output, pipelined as a serving loop runs it (time_pipelined)."""
-    host = {n: inp[n].cpu().pin_memory() for n in ("q", "k", "v")}
-    dev_bufs = [{n: torch.empty_like(t, device=device) for n, t in host.items()} for _ in range(2)]
-    out_host = [torch.empty(host["q"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    tensors = {n: inp[n] for n in ("q", "k", "v")}
+    host_arena, dev_arena, views = stage_arenas(tensors, device)
+    dev_bufs = [views(a) for a in dev_arena]
+    out_host = [torch.empty(tensors["q"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    h2d = sum(t.numel() * t.element_size() for t in tensors.values())
     d2h = out_host[0].numel() * 2
 
     def upload(b):
-        for n, t in dev_bufs[b].items():
-            t.copy_(host[n], non_blocking=True)
+        dev_arena[b].copy_(host_arena, non_blocking=True)
 
     def compute(b):
         d = dev_bufs[b]
@@ -606,22 +627,8 @@ def e2e_gdn_b1(device, rank, world, steps, warmup, inp):
     """Headline step through the public plugin call from pinned host memory: every step uploads
     its inputs, runs kernel_fn and reads back the output and final state, pipelined as a serving
     loop runs it (time_pipelined)."""
-    # a step's inputs staged in one pinned host buffer and uploaded with one copy (views of it are
-    # the tensors; 256-byte aligned)
     tensors = {k: v for k, v in inp.items() if isinstance(v, torch.Tensor)}
-    offsets, total = {}, 0
-    for k, v in tensors.items():
-        offsets[k] = total
-        total += -(-v.numel() * v.element_size() // 256) * 256
-    host_arena = torch.empty(total, dtype=torch.uint8).pin_memory()
-    dev_arena = [torch.empty(total, dtype=torch.uint8, device=device) for _ in range(2)]
-
-    def views(arena):
-        return {k: arena[offsets[k]:offsets[k] + v.numel() * v.element_size()].view(v.dtype).view(v.shape)
-                for k, v in tensors.items()}
-
-    for k, v in views(host_arena).items():
-        v.copy_(tensors[k].cpu())
+    host_arena, dev_arena, views = stage_arenas(tensors, device)
     dev_bufs = [views(a) for a in dev_arena]
     host = {"scale": inp["scale"]}
     out_host = [torch.empty((1, 2048, HV, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
