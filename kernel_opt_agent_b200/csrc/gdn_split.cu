@@ -2,16 +2,17 @@
 // units, where one CTA per unit would leave most SMs idle and put a long per-chunk preparation
 // path in front of every step of the state chain.
 //
-//   1. gdn_prep_kernel: one CTA per (chunk, value head), all chunks at once, three CTAs per SM.
-//      Decay sums, Q K^T / K K^T (tcgen05), the read-out of L, P and e^G-scaled Q, the triangular
-//      solve, T and T diag(e^G), W = T diag(e^G) K (tcgen05).  The threads that produce the chunk's
-//      MMA operands write them straight to one record of kRecBytes in a workspace (L2-resident
-//      for the sizes this mode is used at), already in the 128-byte-swizzled shared-memory layout
-//      the chain kernel feeds to the tensor core.
+//   1. gdn_prep_kernel: every (chunk, value head) record, persistent CTAs (three per SM) taking
+//      records in chunk-major order.  Decay sums, Q K^T / K K^T (tcgen05), the read-out of L, P
+//      and e^G-scaled Q, the triangular solve, T and T diag(e^G), W = T diag(e^G) K (tcgen05).
+//      Each of the chunk's MMA operands is staged in shared memory as its image in the
+//      128-byte-swizzled layout the chain kernel feeds to the tensor core, and bulk-copied to one
+//      record of kRecBytes in a workspace.
 //   2. gdn_chain_kernel: one CTA per (sequence, value head).  A loader warp streams each chunk's
 //      record (bulk copies) and its K, V tiles (TMA) into a two-stage ring; the state chain and
 //      the output pass are those of gdn_prefill.cu without any preparation work.
-// Results equal gdn_prefill.cu's up to fp32 summation order (same operands, same splits).
+// Results equal gdn_prefill.cu's bit for bit: the same operands and splits, and every TMEM
+// accumulator receives its MMAs in the same order.
 #include <cuda_runtime.h>
 
 #include <algorithm>
