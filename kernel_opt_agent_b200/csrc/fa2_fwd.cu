@@ -63,6 +63,7 @@ struct Params {
   int pair_heads;              // 1: a pair is two heads of one GQA group; 0: two query tiles of one head
   int n_qtiles;                // ceil(sq / 128)
   int head_units;              // pairs of heads (pair_heads) or heads
+  int units;                   // work units (tile pairs), heaviest first
   uint32_t* status;
 };
 
@@ -71,6 +72,14 @@ struct TileInfo {
   int q0;       // first query row
   int n_kv;     // number of kv tiles this tile visits (0 = inactive)
 };
+
+// The r-th unit of this CTA in a persistent launch: units are heaviest first, and rounds of
+// gridDim.x units go to the CTAs in alternating directions, so that every CTA's total stays
+// within one unit of the others'.
+__device__ __forceinline__ int unit_of_round(int r) {
+  const int pos = (r & 1) ? static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
+  return r * static_cast<int>(gridDim.x) + pos;
+}
 
 __device__ __forceinline__ void decode_unit(const Params& p, int u, int& b, int& kvh, TileInfo (&t)[2]) {
   const int per_row = p.batch * p.head_units;
@@ -106,6 +115,11 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& b, int&
   }
 }
 
+// Persistent: CTA c takes its work units (tile pairs) round by round (unit_of_round), so barriers
+// and TMEM are set up once per CTA and the next unit's Q load
+// and first S MMAs run while the softmax warps finish the previous unit's epilogue.  Barrier
+// phases carry over from unit to unit: the K/V ring by a running key-tile count g, bar_s/bar_p
+// by each tile slot's running step count, bar_q, bar_qfree, bar_o and bar_ofree by unit.
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     fa2_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
@@ -113,20 +127,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = Layout<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar_q, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_s[2], bar_p[2], bar_o[2];
+  __shared__ uint64_t bar_q, bar_qfree, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_s[2], bar_p[2],
+      bar_o[2], bar_ofree[2];
   __shared__ uint64_t bar_drain;
   __shared__ uint32_t tmem_base_shared;
 
   const int warp = warp_id();
   const int lane = lane_id();
-  int b, kvh;
-  TileInfo tile[2];
-  decode_unit(p, blockIdx.x, b, kvh, tile);
-  const int nmax = max(tile[0].n_kv, tile[1].n_kv);
 
   if (threadIdx.x == 0) {
     cta_abort_flag() = 0u;
     mbar_init(&bar_q, 1);
+    mbar_init(&bar_qfree, 1);
     mbar_init(&bar_drain, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_kfull[i], 1);
@@ -136,6 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar_s[i], 1);
       mbar_init(&bar_p[i], 128);
       mbar_init(&bar_o[i], 1);
+      mbar_init(&bar_ofree[i], 128);
     }
     fence_barrier_init();
   }
@@ -154,36 +167,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&map_q);
       tma_prefetch_desc(&map_k);
       tma_prefetch_desc(&map_v);
-      uint32_t qbytes = 0;
-      for (int i = 0; i < 2; ++i) qbytes += tile[i].n_kv > 0 ? L::kTileBytes : 0;
-      mbar_arrive_expect_tx(&bar_q, qbytes);
-      for (int i = 0; i < 2; ++i) {
-        if (tile[i].n_kv == 0) continue;
-        uint8_t* dst = smem + (i == 0 ? L::kQ0 : L::kQ1);
-        for (int bx = 0; bx < D / 64; ++bx)
-          tma_load_4d(dst + bx * L::kBoxBytes, &map_q, &bar_q, bx * 64, tile[i].q0, tile[i].head, b);
-      }
-      int issued = 0;
-      for (int j = 0; j < nmax; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&bar_kempty[st], ((j >> 1) - 1) & 1, p.status, kDevTimeoutPipe)) break;
-        mbar_arrive_expect_tx(&bar_kfull[st], L::kTileBytes);
-        for (int bx = 0; bx < D / 64; ++bx)
-          tma_load_4d(smem + L::kK + st * L::kTileBytes + bx * L::kBoxBytes, &map_k, &bar_kfull[st], bx * 64,
-                      j * kBN, kvh, b);
-        if (j >= 2 && !mbar_wait(&bar_vempty[st], ((j >> 1) - 1) & 1, p.status, kDevTimeoutPipe)) break;
-        mbar_arrive_expect_tx(&bar_vfull[st], L::kTileBytes);
-        for (int bx = 0; bx < D / 64; ++bx)
-          tma_load_4d(smem + L::kV + st * L::kTileBytes + bx * L::kBoxBytes, &map_v, &bar_vfull[st], bx * 64,
-                      j * kBN, kvh, b);
-        issued = j + 1;
+      bool ok = true;
+      int g = 0, it = 0;                          // key tiles and units begun
+      int q_issued = 0, k_issued = 0, v_issued = 0;  // loads issued, for the drain
+      for (int r = 0; ok; ++r, ++it) {
+        const int u = unit_of_round(r);
+        if (u >= p.units) break;
+        int b, kvh;
+        TileInfo tile[2];
+        decode_unit(p, u, b, kvh, tile);
+        const int nmax = max(tile[0].n_kv, tile[1].n_kv);
+        // Q of this unit once the previous unit's last S MMAs have read the Q tiles
+        if (it > 0 && !mbar_wait(&bar_qfree, (it - 1) & 1, p.status, kDevTimeoutPipe)) break;
+        uint32_t qbytes = 0;
+        for (int i = 0; i < 2; ++i) qbytes += tile[i].n_kv > 0 ? L::kTileBytes : 0;
+        mbar_arrive_expect_tx(&bar_q, qbytes);
+        for (int i = 0; i < 2; ++i) {
+          if (tile[i].n_kv == 0) continue;
+          uint8_t* dst = smem + (i == 0 ? L::kQ0 : L::kQ1);
+          for (int bx = 0; bx < D / 64; ++bx)
+            tma_load_4d(dst + bx * L::kBoxBytes, &map_q, &bar_q, bx * 64, tile[i].q0, tile[i].head, b);
+        }
+        q_issued = it + 1;
+        for (int j = 0; j < nmax; ++j, ++g) {
+          const int st = g & 1;
+          if (g >= 2 && !mbar_wait(&bar_kempty[st], ((g >> 1) - 1) & 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bar_kfull[st], L::kTileBytes);
+          for (int bx = 0; bx < D / 64; ++bx)
+            tma_load_4d(smem + L::kK + st * L::kTileBytes + bx * L::kBoxBytes, &map_k, &bar_kfull[st], bx * 64,
+                        j * kBN, kvh, b);
+          k_issued = g + 1;
+          if (g >= 2 && !mbar_wait(&bar_vempty[st], ((g >> 1) - 1) & 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bar_vfull[st], L::kTileBytes);
+          for (int bx = 0; bx < D / 64; ++bx)
+            tma_load_4d(smem + L::kV + st * L::kTileBytes + bx * L::kBoxBytes, &map_v, &bar_vfull[st], bx * 64,
+                        j * kBN, kvh, b);
+          v_issued = g + 1;
+        }
       }
       // before the CTA retires, let the last loads land (bounded; a no-op on the normal path)
-      mbar_drain(&bar_q, 0);
-      for (int j = max(0, issued - 2); j < issued; ++j) {
-        mbar_drain(&bar_kfull[j & 1], (j >> 1) & 1);
-        mbar_drain(&bar_vfull[j & 1], (j >> 1) & 1);
-      }
+      if (q_issued > 0) mbar_drain(&bar_q, (q_issued - 1) & 1);
+      for (int t = max(0, k_issued - 2); t < k_issued; ++t) mbar_drain(&bar_kfull[t & 1], (t >> 1) & 1);
+      for (int t = max(0, v_issued - 2); t < v_issued; ++t) mbar_drain(&bar_vfull[t & 1], (t >> 1) & 1);
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------------ MMA issuer
@@ -211,44 +236,68 @@ __global__ void __launch_bounds__(kThreads, 1)
                        (accumulate || kk > 0) ? 1u : 0u);
         }
       };
-      bool ok = mbar_wait(&bar_q, 0, p.status, kDevTimeoutTma);
-      if (ok) ok = mbar_wait(&bar_kfull[0], 0, p.status, kDevTimeoutTma);
-      if (ok) {
+      bool ok = true;
+      int g = 0, it = 0;         // key tiles of earlier units; units begun
+      int steps[2] = {0, 0};     // each tile slot's steps in earlier units (bar_s, bar_p phases)
+      int outs[2] = {0, 0};      // earlier units in which the slot was active (bar_o, bar_ofree phases)
+      for (int r = 0; ok; ++r, ++it) {
+        const int u = unit_of_round(r);
+        if (u >= p.units) break;
+        int b, kvh;
+        TileInfo tile[2];
+        decode_unit(p, u, b, kvh, tile);
+        const int nmax = max(tile[0].n_kv, tile[1].n_kv);
+        ok = mbar_wait(&bar_q, it & 1, p.status, kDevTimeoutTma) &&
+             mbar_wait(&bar_kfull[g & 1], (g >> 1) & 1, p.status, kDevTimeoutTma);
+        if (!ok) break;
         tc_fence_after();
+        // S(0): S_i's columns were last read by the previous unit's PV_i, issued earlier by this thread
         for (int i = 0; i < 2; ++i) {
           if (tile[i].n_kv > 0) {
-            issue_s(i, 0);
+            issue_s(i, g & 1);
             umma_commit(&bar_s[i]);
           }
         }
-        umma_commit(&bar_kempty[0]);
-      }
-      for (int j = 0; ok && j < nmax; ++j) {
-        const int st = j & 1;
-        const int jn = j + 1;
-        const int stn = jn & 1;
-        if (!mbar_wait(&bar_vfull[st], (j >> 1) & 1, p.status, kDevTimeoutTma)) break;
-        tc_fence_after();
-        bool k_ready = false;
-        for (int i = 0; i < 2 && ok; ++i) {
-          if (j >= tile[i].n_kv) continue;
-          if (!mbar_wait(&bar_p[i], j & 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
+        umma_commit(&bar_kempty[g & 1]);
+        if (nmax == 1) umma_commit(&bar_qfree);  // no later S of this unit reads Q
+        for (int j = 0; ok && j < nmax; ++j) {
+          const int gj = g + j, st = gj & 1, gn = gj + 1, stn = gn & 1;
+          if (!mbar_wait(&bar_vfull[st], (gj >> 1) & 1, p.status, kDevTimeoutTma)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(i, st, j > 0);
-          if (j == tile[i].n_kv - 1) umma_commit(&bar_o[i]);
-          if (jn < tile[i].n_kv) {
-            if (!k_ready) {
-              if (!mbar_wait(&bar_kfull[stn], (jn >> 1) & 1, p.status, kDevTimeoutTma)) { ok = false; break; }
-              tc_fence_after();
-              k_ready = true;
+          bool k_ready = false;
+          for (int i = 0; i < 2 && ok; ++i) {
+            if (j >= tile[i].n_kv) continue;
+            if (!mbar_wait(&bar_p[i], (steps[i] + j) & 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
+            // PV(0) overwrites O: the softmax warps have read the previous unit's O out of it
+            if (j == 0 && outs[i] > 0 && !mbar_wait(&bar_ofree[i], (outs[i] - 1) & 1, p.status, kDevTimeoutPipe)) {
+              ok = false;
+              break;
             }
-            issue_s(i, stn);
-            umma_commit(&bar_s[i]);
+            tc_fence_after();
+            issue_pv(i, st, j > 0);
+            if (j == tile[i].n_kv - 1) umma_commit(&bar_o[i]);
+            if (j + 1 < tile[i].n_kv) {
+              if (!k_ready) {
+                if (!mbar_wait(&bar_kfull[stn], (gn >> 1) & 1, p.status, kDevTimeoutTma)) { ok = false; break; }
+                tc_fence_after();
+                k_ready = true;
+              }
+              issue_s(i, stn);
+              umma_commit(&bar_s[i]);
+            }
+          }
+          if (!ok) break;
+          umma_commit(&bar_vempty[st]);
+          if (k_ready) umma_commit(&bar_kempty[stn]);
+          if (j == nmax - 2) umma_commit(&bar_qfree);  // the unit's last S MMAs are issued
+        }
+        for (int i = 0; i < 2; ++i) {
+          if (tile[i].n_kv > 0) {
+            steps[i] += tile[i].n_kv;
+            ++outs[i];
           }
         }
-        if (!ok) break;
-        umma_commit(&bar_vempty[st]);
-        if (k_ready) umma_commit(&bar_kempty[stn]);
+        g += nmax;
       }
       // every MMA issued by this thread completes before TMEM is released (bounded)
       umma_commit(&bar_drain);
@@ -259,105 +308,127 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ softmax warpgroups
     const int i = warp >> 2;
     const int qrow_local = (warp & 3) * 32 + lane;
-    const int qrow = tile[i].q0 + qrow_local;
-    const int n_kv = tile[i].n_kv;
     const uint32_t lane_base = tmem_addr(tbase, (warp & 3) * 32, 0);
     const uint32_t col_s = i == 0 ? L::kColS0 : L::kColS1;
     const uint32_t col_o = i == 0 ? L::kColO0 : L::kColO1;
     const float c = p.scale_log2;
-    float m = -INFINITY;
-    float l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      // tcgen05.ld/st are warp-collective: the whole warp continues or stops together
-      if (!__all_sync(0xffffffffu, mbar_wait(&bar_s[i], j & 1, p.status, kDevTimeoutMma))) { ok = false; break; }
-      tc_fence_after();
-      uint32_t raw[128];
-      tmem_ld64(lane_base + col_s, *reinterpret_cast<uint32_t(*)[64]>(&raw[0]));
-      tmem_ld64(lane_base + col_s + 64, *reinterpret_cast<uint32_t(*)[64]>(&raw[64]));
-      float s[128];
-#pragma unroll
-      for (int cc = 0; cc < 128; ++cc) s[cc] = __uint_as_float(raw[cc]);
-      const int kv0 = j * kBN;
-      const bool need_mask = (p.causal && kv0 + kBN - 1 > tile[i].q0) || (kv0 + kBN > p.skv);
-      if (need_mask) {
-        const int lim = (p.causal ? min(qrow + 1, p.skv) : p.skv) - kv0;
-#pragma unroll
-        for (int cc = 0; cc < 128; ++cc)
-          if (cc >= lim) s[cc] = -INFINITY;
-      }
-      float mx;
-      {  // four independent chains of three-input maxima over the 128 columns
-        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
-#pragma unroll
-        for (int cc = 0; cc < 128; cc += 8) {
-          m0 = max3f(m0, s[cc], s[cc + 1]);
-          m1 = max3f(m1, s[cc + 2], s[cc + 3]);
-          m2 = max3f(m2, s[cc + 4], s[cc + 5]);
-          m3 = max3f(m3, s[cc + 6], s[cc + 7]);
+    int steps = 0, outs = 0;  // this slot's steps and active units so far (barrier phases)
+    for (int r = 0; ok; ++r) {
+      const int u = unit_of_round(r);
+      if (u >= p.units) break;
+      int b, kvh;
+      TileInfo tile[2];
+      decode_unit(p, u, b, kvh, tile);
+      const int n_kv = tile[i].n_kv;
+      if (n_kv == 0) continue;  // the slot has no tile in this unit
+      const int qrow = tile[i].q0 + qrow_local;
+      float m = -INFINITY;
+      float l = 0.0f;
+      for (int j = 0; j < n_kv; ++j) {
+        // tcgen05.ld/st are warp-collective: the whole warp continues or stops together
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar_s[i], (steps + j) & 1, p.status, kDevTimeoutMma))) {
+          ok = false;
+          break;
         }
-        mx = max3f(m0, m1, fmaxf(m2, m3));
+        tc_fence_after();
+        uint32_t raw[128];
+        tmem_ld64(lane_base + col_s, *reinterpret_cast<uint32_t(*)[64]>(&raw[0]));
+        tmem_ld64(lane_base + col_s + 64, *reinterpret_cast<uint32_t(*)[64]>(&raw[64]));
+        float s[128];
+  #pragma unroll
+        for (int cc = 0; cc < 128; ++cc) s[cc] = __uint_as_float(raw[cc]);
+        const int kv0 = j * kBN;
+        const bool need_mask = (p.causal && kv0 + kBN - 1 > tile[i].q0) || (kv0 + kBN > p.skv);
+        if (need_mask) {
+          const int lim = (p.causal ? min(qrow + 1, p.skv) : p.skv) - kv0;
+  #pragma unroll
+          for (int cc = 0; cc < 128; ++cc)
+            if (cc >= lim) s[cc] = -INFINITY;
+        }
+        float mx;
+        {  // four independent chains of three-input maxima over the 128 columns
+          float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+  #pragma unroll
+          for (int cc = 0; cc < 128; cc += 8) {
+            m0 = max3f(m0, s[cc], s[cc + 1]);
+            m1 = max3f(m1, s[cc + 2], s[cc + 3]);
+            m2 = max3f(m2, s[cc + 4], s[cc + 5]);
+            m3 = max3f(m3, s[cc + 6], s[cc + 7]);
+          }
+          mx = max3f(m0, m1, fmaxf(m2, m3));
+        }
+        const float mx_scaled = mx * c;
+        // Lazy rescale: a row moves its running max only when it grew by more than 2^8.  The
+        // decision is per row, the O read-modify-write is done by the whole warp (alpha = 1 for
+        // rows that keep their max) because tcgen05.ld/st are warp-collective.
+        const bool grow = mx_scaled > m + kRescaleThreshold;
+        float alpha = 1.0f;
+        if (grow) {
+          alpha = ex2_approx(m - mx_scaled);
+          m = mx_scaled;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+          // O holds sum_{<j} P V; PV(j-1) is complete because S(j) was committed after it.
+  #pragma unroll 1
+          for (int dc = 0; dc < D; dc += 32) {
+            uint32_t o_raw[32];
+            tmem_ld32(lane_base + col_o + dc, o_raw);
+  #pragma unroll
+            for (int e = 0; e < 32; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * alpha);
+            tmem_st32(lane_base + col_o + dc, o_raw);
+          }
+        }
+        l *= alpha;
+        float rowsum = 0.0f;
+  #pragma unroll
+        for (int chunk = 0; chunk < 4; ++chunk) {
+          uint32_t packed[16];
+  #pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = ex2_approx(fmaf(s[chunk * 32 + 2 * e], c, -m));
+            const float p1 = ex2_approx(fmaf(s[chunk * 32 + 2 * e + 1], c, -m));
+            rowsum += p0 + p1;
+            packed[e] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(lane_base + col_s + chunk * 16, packed);
+        }
+        l += rowsum;
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bar_p[i]);
       }
-      const float mx_scaled = mx * c;
-      // Lazy rescale: a row moves its running max only when it grew by more than 2^8.  The
-      // decision is per row, the O read-modify-write is done by the whole warp (alpha = 1 for
-      // rows that keep their max) because tcgen05.ld/st are warp-collective.
-      const bool grow = mx_scaled > m + kRescaleThreshold;
-      float alpha = 1.0f;
-      if (grow) {
-        alpha = ex2_approx(m - mx_scaled);
-        m = mx_scaled;
+      if (!ok) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_o[i], outs & 1, p.status, kDevTimeoutMma))) {
+        ok = false;
+        break;
       }
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // O holds sum_{<j} P V; PV(j-1) is complete because S(j) was committed after it.
-#pragma unroll 1
+      {
+        tc_fence_after();
+        const float inv_l = 1.0f / l;
+        __nv_bfloat16* orow = p.o + static_cast<long long>(b) * p.o_sb + static_cast<long long>(tile[i].head) * p.o_sh +
+                              static_cast<long long>(qrow) * p.o_ss;
+  #pragma unroll 1
         for (int dc = 0; dc < D; dc += 32) {
           uint32_t o_raw[32];
           tmem_ld32(lane_base + col_o + dc, o_raw);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * alpha);
-          tmem_st32(lane_base + col_o + dc, o_raw);
+          uint32_t packed[16];
+  #pragma unroll
+          for (int e = 0; e < 16; ++e)
+            packed[e] = pack_bf16x2(__uint_as_float(o_raw[2 * e]) * inv_l, __uint_as_float(o_raw[2 * e + 1]) * inv_l);
+          if (qrow < p.sq) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + dc);
+  #pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4)
+              dst[v4] = make_uint4(packed[4 * v4], packed[4 * v4 + 1], packed[4 * v4 + 2], packed[4 * v4 + 3]);
+          }
         }
       }
-      l *= alpha;
-      float rowsum = 0.0f;
-#pragma unroll
-      for (int chunk = 0; chunk < 4; ++chunk) {
-        uint32_t packed[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float p0 = ex2_approx(fmaf(s[chunk * 32 + 2 * e], c, -m));
-          const float p1 = ex2_approx(fmaf(s[chunk * 32 + 2 * e + 1], c, -m));
-          rowsum += p0 + p1;
-          packed[e] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(lane_base + col_s + chunk * 16, packed);
-      }
-      l += rowsum;
-      tmem_wait_st();
+      // the O columns are read (tcgen05.ld waited): the next unit's PV may overwrite them
       tc_fence_before();
-      mbar_arrive(&bar_p[i]);
-    }
-    if (ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&bar_o[i], 0, p.status, kDevTimeoutMma))) {
-      tc_fence_after();
-      const float inv_l = 1.0f / l;
-      __nv_bfloat16* orow = p.o + static_cast<long long>(b) * p.o_sb + static_cast<long long>(tile[i].head) * p.o_sh +
-                            static_cast<long long>(qrow) * p.o_ss;
-#pragma unroll 1
-      for (int dc = 0; dc < D; dc += 32) {
-        uint32_t o_raw[32];
-        tmem_ld32(lane_base + col_o + dc, o_raw);
-        uint32_t packed[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          packed[e] = pack_bf16x2(__uint_as_float(o_raw[2 * e]) * inv_l, __uint_as_float(o_raw[2 * e + 1]) * inv_l);
-        if (qrow < p.sq) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + dc);
-#pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4)
-            dst[v4] = make_uint4(packed[4 * v4], packed[4 * v4 + 1], packed[4 * v4 + 2], packed[4 * v4 + 3]);
-        }
-      }
+      mbar_arrive(&bar_ofree[i]);
+      steps += n_kv;
+      ++outs;
     }
   }
 
@@ -423,10 +494,12 @@ int launch(const void* q, const void* k, const void* v, void* o, int batch, int 
   if (units <= 0) return TOKMIX_OK;
   if (units > 0x7FFFFFFFll) return fail(TOKMIX_ERR_UNSUPPORTED, "tokmix_fa2_fwd: too many tiles (%lld)", units);
 
+  p.units = static_cast<int>(units);
   const int smem_bytes = L::kBytes + 1024;
   if (!ensure_smem_attr(reinterpret_cast<const void*>(&fa2_fwd_kernel<D>), smem_bytes))
     return check_launch("tokmix_fa2_fwd: cudaFuncSetAttribute");
-  fa2_fwd_kernel<D><<<static_cast<unsigned>(units), kThreads, smem_bytes, stream>>>(mq, mk, mv, p);
+  const int grid = static_cast<int>(std::min<long long>(units, std::max(1, device_sm_count())));
+  fa2_fwd_kernel<D><<<static_cast<unsigned>(grid), kThreads, smem_bytes, stream>>>(mq, mk, mv, p);
   return check_launch("tokmix_fa2_fwd");
 }
 
