@@ -532,32 +532,42 @@ static_assert(kBytes + 1024 <= 227 * 1024, "d256 shared memory budget");
 __device__ __forceinline__ uint32_t col_s(int st) { return st ? 128u : 0u; }  // S buffer st
 constexpr uint32_t kColO = 256;
 
+// The unit u of the head_dim-256 launch: one 128-row query tile of one (batch, head), the heaviest
+// (last) causal tiles first
+__device__ __forceinline__ void decode_d256(const Params& p, int u, int& b, int& head, int& kvh, int& q0, int& n_kv) {
+  const int per_row = p.batch * p.hq;
+  const int rev = u / per_row;
+  const int rem = u - rev * per_row;
+  b = rem / p.hq;
+  head = rem - b * p.hq;
+  kvh = head / (p.hq / p.hkv);
+  q0 = (p.n_qtiles - 1 - rev) * kBM;
+  const int kv_tiles_all = (p.skv + kBN - 1) / kBN;
+  n_kv = p.causal ? min(kv_tiles_all, (q0 + kBM - 1) / kBN + 1) : kv_tiles_all;
+}
+
+// Persistent like fa2_fwd_kernel: CTA c takes its units round by round (unit_of_round); the
+// steps of all its units form one sequence g (S buffer g & 1, K and V tile g), so barrier phases
+// carry over; the next unit's Q loads once the current unit's last S is issued (bar_qfree) and
+// its first PV waits until the softmax warps have read the previous O out (bar_ofree).
 __global__ void __launch_bounds__(kThreads, 1)
     fa2_fwd_d256_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar_q, bar_kfull, bar_kempty, bar_vfull, bar_vempty, bar_s[2], bar_p[2], bar_pv[2];
-  __shared__ uint64_t bar_o, bar_drain;
+  __shared__ uint64_t bar_q, bar_qfree, bar_kfull, bar_kempty, bar_vfull, bar_vempty, bar_s[2], bar_p[2], bar_pv[2];
+  __shared__ uint64_t bar_o, bar_ofree, bar_drain;
   __shared__ uint32_t tmem_base_shared;
 
   const int warp = warp_id();
   const int lane = lane_id();
-  // unit -> (query tile, batch, head); the heaviest (last) causal tiles first
-  const int per_row = p.batch * p.hq;
-  const int rev = blockIdx.x / per_row;
-  const int rem = blockIdx.x - rev * per_row;
-  const int b = rem / p.hq;
-  const int head = rem - b * p.hq;
-  const int kvh = head / (p.hq / p.hkv);
-  const int q0 = (p.n_qtiles - 1 - rev) * kBM;
-  const int kv_tiles_all = (p.skv + kBN - 1) / kBN;
-  const int n_kv = p.causal ? min(kv_tiles_all, (q0 + kBM - 1) / kBN + 1) : kv_tiles_all;
 
   if (threadIdx.x == 0) {
     cta_abort_flag() = 0u;
     mbar_init(&bar_q, 1);
+    mbar_init(&bar_qfree, 1);
     mbar_init(&bar_o, 1);
+    mbar_init(&bar_ofree, 128);
     mbar_init(&bar_drain, 1);
     mbar_init(&bar_kfull, 1);
     mbar_init(&bar_kempty, 1);
@@ -581,34 +591,50 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kWarpTma) {
     // ------------------------------------------------------------------ TMA producers
-    // K(j) waits for S(j-1) to release the K buffer, V(j) for PV(j-1) (kempty / vempty complete
-    // once per tile, so the release of tile j-1 is phase (j-1) & 1)
+    // K(g) waits for S(g-1) to release the K buffer, V(g) for PV(g-1) (kempty / vempty complete
+    // once per tile, so the release of tile g-1 is phase (g-1) & 1)
     if (lane == 0) {
       tma_prefetch_desc(&map_q);
       tma_prefetch_desc(&map_k);
-      mbar_arrive_expect_tx(&bar_q, kQBytes);
-      for (int bx = 0; bx < kD / 64; ++bx) tma_load_4d(smem + kQ + bx * kQBox, &map_q, &bar_q, bx * 64, q0, head, b);
-      int issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        if (j >= 1 && !mbar_wait(&bar_kempty, (j - 1) & 1, p.status, kDevTimeoutPipe)) break;
-        mbar_arrive_expect_tx(&bar_kfull, kKVBytes);
-        for (int bx = 0; bx < kD / 64; ++bx)
-          tma_load_4d(smem + kK + bx * kKVBox, &map_k, &bar_kfull, bx * 64, j * kBN, kvh, b);
-        issued = j + 1;
+      bool ok = true;
+      int g = 0, q_issued = 0, k_issued = 0;
+      for (int r = 0; ok; ++r) {
+        const int u = unit_of_round(r);
+        if (u >= p.units) break;
+        int b, head, kvh, q0, n_kv;
+        decode_d256(p, u, b, head, kvh, q0, n_kv);
+        if (r > 0 && !mbar_wait(&bar_qfree, (r - 1) & 1, p.status, kDevTimeoutPipe)) break;
+        mbar_arrive_expect_tx(&bar_q, kQBytes);
+        for (int bx = 0; bx < kD / 64; ++bx) tma_load_4d(smem + kQ + bx * kQBox, &map_q, &bar_q, bx * 64, q0, head, b);
+        q_issued = r + 1;
+        for (int j = 0; j < n_kv; ++j, ++g) {
+          if (g >= 1 && !mbar_wait(&bar_kempty, (g - 1) & 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bar_kfull, kKVBytes);
+          for (int bx = 0; bx < kD / 64; ++bx)
+            tma_load_4d(smem + kK + bx * kKVBox, &map_k, &bar_kfull, bx * 64, j * kBN, kvh, b);
+          k_issued = g + 1;
+        }
       }
-      mbar_drain(&bar_q, 0);
-      if (issued > 0) mbar_drain(&bar_kfull, (issued - 1) & 1);
+      if (q_issued > 0) mbar_drain(&bar_q, (q_issued - 1) & 1);
+      if (k_issued > 0) mbar_drain(&bar_kfull, (k_issued - 1) & 1);
     } else if (lane == 1) {
       tma_prefetch_desc(&map_v);
-      int issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        if (j >= 1 && !mbar_wait(&bar_vempty, (j - 1) & 1, p.status, kDevTimeoutPipe)) break;
-        mbar_arrive_expect_tx(&bar_vfull, kKVBytes);
-        for (int bx = 0; bx < kD / 64; ++bx)
-          tma_load_4d(smem + kV + bx * kKVBox, &map_v, &bar_vfull, bx * 64, j * kBN, kvh, b);
-        issued = j + 1;
+      bool ok = true;
+      int g = 0, v_issued = 0;
+      for (int r = 0; ok; ++r) {
+        const int u = unit_of_round(r);
+        if (u >= p.units) break;
+        int b, head, kvh, q0, n_kv;
+        decode_d256(p, u, b, head, kvh, q0, n_kv);
+        for (int j = 0; j < n_kv; ++j, ++g) {
+          if (g >= 1 && !mbar_wait(&bar_vempty, (g - 1) & 1, p.status, kDevTimeoutPipe)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bar_vfull, kKVBytes);
+          for (int bx = 0; bx < kD / 64; ++bx)
+            tma_load_4d(smem + kV + bx * kKVBox, &map_v, &bar_vfull, bx * 64, j * kBN, kvh, b);
+          v_issued = g + 1;
+        }
       }
-      if (issued > 0) mbar_drain(&bar_vfull, (issued - 1) & 1);
+      if (v_issued > 0) mbar_drain(&bar_vfull, (v_issued - 1) & 1);
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------------ MMA issuer
@@ -618,39 +644,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t qa = smem_u32(smem + kQ);
       const uint32_t ka = smem_u32(smem + kK);
       const uint32_t va = smem_u32(smem + kV);
-      // S(j) = Q K(j)^T into S buffer j & 1, once K(j) is in; releases the K buffer
-      auto issue_s = [&](int j) -> bool {
-        if (!mbar_wait(&bar_kfull, j & 1, p.status, kDevTimeoutTma)) return false;
+      // S(g) = Q K(g)^T into S buffer g & 1, once K(g) is in; releases the K buffer
+      auto issue_s = [&](int g) -> bool {
+        if (!mbar_wait(&bar_kfull, g & 1, p.status, kDevTimeoutTma)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          umma_bf16_ss(tbase + col_s(j & 1), make_sdesc_sw128(qa + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024),
+          umma_bf16_ss(tbase + col_s(g & 1), make_sdesc_sw128(qa + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024),
                        make_sdesc_sw128(ka + (kk >> 2) * kKVBox + (kk & 3) * 32, 16, 1024), idesc_s,
                        kk > 0 ? 1u : 0u);
-        umma_commit(&bar_s[j & 1]);
+        umma_commit(&bar_s[g & 1]);
         umma_commit(&bar_kempty);
         return true;
       };
-      bool ok = mbar_wait(&bar_q, 0, p.status, kDevTimeoutTma) && (n_kv == 0 || issue_s(0));
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j & 1;
-        // S(j+1) first: it runs while the softmax warps work on S(j)
-        if (j + 1 < n_kv && !issue_s(j + 1)) {
-          ok = false;
-          break;
-        }
-        ok = mbar_wait(&bar_vfull, j & 1, p.status, kDevTimeoutTma) &&
-             mbar_wait(&bar_p[st], (j >> 1) & 1, p.status, kDevTimeoutPipe);
-        if (!ok) break;
-        tc_fence_after();
-        // O (+)= P(j) V(j): P read from TMEM (bf16 over S buffer j & 1), V MN-major in smem
+      bool ok = true;
+      int gbase = 0;  // steps of earlier units
+      for (int r = 0; ok; ++r) {
+        const int u = unit_of_round(r);
+        if (u >= p.units) break;
+        int b, head, kvh, q0, n_kv;
+        decode_d256(p, u, b, head, kvh, q0, n_kv);
+        ok = mbar_wait(&bar_q, r & 1, p.status, kDevTimeoutTma) && issue_s(gbase);
+        if (ok && n_kv == 1) umma_commit(&bar_qfree);  // no later S of this unit reads Q
+        for (int j = 0; ok && j < n_kv; ++j) {
+          const int g = gbase + j, st = g & 1;
+          // S(g+1) first: it runs while the softmax warps work on S(g)
+          if (j + 1 < n_kv) {
+            if (!issue_s(g + 1)) {
+              ok = false;
+              break;
+            }
+            if (j + 2 == n_kv) umma_commit(&bar_qfree);  // the unit's last S is issued
+          }
+          ok = mbar_wait(&bar_vfull, g & 1, p.status, kDevTimeoutTma) &&
+               mbar_wait(&bar_p[st], (g >> 1) & 1, p.status, kDevTimeoutPipe);
+          // PV(0) overwrites O: the softmax warps have read the previous unit's O out of it
+          if (ok && j == 0 && r > 0) ok = mbar_wait(&bar_ofree, (r - 1) & 1, p.status, kDevTimeoutPipe);
+          if (!ok) break;
+          tc_fence_after();
+          // O (+)= P(g) V(g): P read from TMEM (bf16 over S buffer g & 1), V MN-major in smem
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          umma_bf16_ts(tbase + kColO, tbase + col_s(st) + 8 * kk, make_sdesc_sw128(va + kk * 2048, kKVBox, 1024),
-                       idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&bar_pv[st]);
-        umma_commit(&bar_vempty);
-        if (j == n_kv - 1) umma_commit(&bar_o);
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            umma_bf16_ts(tbase + kColO, tbase + col_s(st) + 8 * kk, make_sdesc_sw128(va + kk * 2048, kKVBox, 1024),
+                         idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&bar_pv[st]);
+          umma_commit(&bar_vempty);
+          if (j == n_kv - 1) umma_commit(&bar_o);
+        }
+        gbase += n_kv;
       }
       umma_commit(&bar_drain);
       mbar_drain(&bar_drain, 0);
@@ -659,106 +700,122 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------------ softmax warps 0-3
     const int qrow_local = warp * 32 + lane;
-    const int qrow = q0 + qrow_local;
     const uint32_t lane_base = tmem_addr(tbase, warp * 32, 0);
     const float c = p.scale_log2;
-    float m = -INFINITY;
-    float l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int st = j & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&bar_s[st], (j >> 1) & 1, p.status, kDevTimeoutMma))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t raw[128];
-      tmem_ld64(lane_base + col_s(st), *reinterpret_cast<uint32_t(*)[64]>(&raw[0]));
-      tmem_ld64(lane_base + col_s(st) + 64, *reinterpret_cast<uint32_t(*)[64]>(&raw[64]));
-      float s[128];
-#pragma unroll
-      for (int cc = 0; cc < 128; ++cc) s[cc] = __uint_as_float(raw[cc]);
-      const int kv0 = j * kBN;
-      if ((p.causal && kv0 + kBN - 1 > q0) || (kv0 + kBN > p.skv)) {
-        const int lim = (p.causal ? min(qrow + 1, p.skv) : p.skv) - kv0;
-#pragma unroll
-        for (int cc = 0; cc < 128; ++cc)
-          if (cc >= lim) s[cc] = -INFINITY;
-      }
-      float mx;
-      {  // four independent chains of three-input maxima over the 128 columns
-        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
-#pragma unroll
-        for (int cc = 0; cc < 128; cc += 8) {
-          m0 = max3f(m0, s[cc], s[cc + 1]);
-          m1 = max3f(m1, s[cc + 2], s[cc + 3]);
-          m2 = max3f(m2, s[cc + 4], s[cc + 5]);
-          m3 = max3f(m3, s[cc + 6], s[cc + 7]);
-        }
-        mx = max3f(m0, m1, fmaxf(m2, m3));
-      }
-      const float mx_scaled = mx * c;
-      const bool grow = mx_scaled > m + kRescaleThreshold;
-      float alpha = 1.0f;
-      if (grow) {
-        alpha = ex2_approx(m - mx_scaled);
-        m = mx_scaled;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // O holds sum_{<j} P V once PV(j-1) has completed
-        if (!__all_sync(0xffffffffu, mbar_wait(&bar_pv[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status, kDevTimeoutMma))) {
+    int gbase = 0;  // steps of earlier units
+    for (int r = 0; ok; ++r) {
+      const int u = unit_of_round(r);
+      if (u >= p.units) break;
+      int b, head, kvh, q0, n_kv;
+      decode_d256(p, u, b, head, kvh, q0, n_kv);
+      const int qrow = q0 + qrow_local;
+      float m = -INFINITY;
+      float l = 0.0f;
+      for (int j = 0; j < n_kv; ++j) {
+        const int g = gbase + j, st = g & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar_s[st], (g >> 1) & 1, p.status, kDevTimeoutMma))) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll 1
+        uint32_t raw[128];
+        tmem_ld64(lane_base + col_s(st), *reinterpret_cast<uint32_t(*)[64]>(&raw[0]));
+        tmem_ld64(lane_base + col_s(st) + 64, *reinterpret_cast<uint32_t(*)[64]>(&raw[64]));
+        float s[128];
+  #pragma unroll
+        for (int cc = 0; cc < 128; ++cc) s[cc] = __uint_as_float(raw[cc]);
+        const int kv0 = j * kBN;
+        if ((p.causal && kv0 + kBN - 1 > q0) || (kv0 + kBN > p.skv)) {
+          const int lim = (p.causal ? min(qrow + 1, p.skv) : p.skv) - kv0;
+  #pragma unroll
+          for (int cc = 0; cc < 128; ++cc)
+            if (cc >= lim) s[cc] = -INFINITY;
+        }
+        float mx;
+        {  // four independent chains of three-input maxima over the 128 columns
+          float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+  #pragma unroll
+          for (int cc = 0; cc < 128; cc += 8) {
+            m0 = max3f(m0, s[cc], s[cc + 1]);
+            m1 = max3f(m1, s[cc + 2], s[cc + 3]);
+            m2 = max3f(m2, s[cc + 4], s[cc + 5]);
+            m3 = max3f(m3, s[cc + 6], s[cc + 7]);
+          }
+          mx = max3f(m0, m1, fmaxf(m2, m3));
+        }
+        const float mx_scaled = mx * c;
+        const bool grow = mx_scaled > m + kRescaleThreshold;
+        float alpha = 1.0f;
+        if (grow) {
+          alpha = ex2_approx(m - mx_scaled);
+          m = mx_scaled;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+          // O holds sum_{<j} P V once PV(j-1) has completed
+          if (!__all_sync(0xffffffffu, mbar_wait(&bar_pv[(g - 1) & 1], ((g - 1) >> 1) & 1, p.status, kDevTimeoutMma))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+  #pragma unroll 1
+          for (int dc = 0; dc < kD; dc += 32) {
+            uint32_t o_raw[32];
+            tmem_ld32(lane_base + kColO + dc, o_raw);
+  #pragma unroll
+            for (int e = 0; e < 32; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * alpha);
+            tmem_st32(lane_base + kColO + dc, o_raw);
+          }
+        }
+        l *= alpha;
+        float rowsum = 0.0f;
+  #pragma unroll
+        for (int chunk = 0; chunk < 4; ++chunk) {
+          uint32_t packed[16];
+  #pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = ex2_approx(fmaf(s[chunk * 32 + 2 * e], c, -m));
+            const float p1 = ex2_approx(fmaf(s[chunk * 32 + 2 * e + 1], c, -m));
+            rowsum += p0 + p1;
+            packed[e] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(lane_base + col_s(st) + chunk * 16, packed);
+        }
+        l += rowsum;
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bar_p[st]);
+      }
+      if (!ok) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_o, r & 1, p.status, kDevTimeoutMma))) {
+        ok = false;
+        break;
+      }
+      {
+        tc_fence_after();
+        const float inv_l = 1.0f / l;
+        __nv_bfloat16* orow = p.o + static_cast<long long>(b) * p.o_sb + static_cast<long long>(head) * p.o_sh +
+                              static_cast<long long>(qrow) * p.o_ss;
+  #pragma unroll 1
         for (int dc = 0; dc < kD; dc += 32) {
           uint32_t o_raw[32];
           tmem_ld32(lane_base + kColO + dc, o_raw);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o_raw[e] = __float_as_uint(__uint_as_float(o_raw[e]) * alpha);
-          tmem_st32(lane_base + kColO + dc, o_raw);
+          uint32_t packed[16];
+  #pragma unroll
+          for (int e = 0; e < 16; ++e)
+            packed[e] = pack_bf16x2(__uint_as_float(o_raw[2 * e]) * inv_l, __uint_as_float(o_raw[2 * e + 1]) * inv_l);
+          if (qrow < p.sq) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + dc);
+  #pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4)
+              dst[v4] = make_uint4(packed[4 * v4], packed[4 * v4 + 1], packed[4 * v4 + 2], packed[4 * v4 + 3]);
+          }
         }
       }
-      l *= alpha;
-      float rowsum = 0.0f;
-#pragma unroll
-      for (int chunk = 0; chunk < 4; ++chunk) {
-        uint32_t packed[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float p0 = ex2_approx(fmaf(s[chunk * 32 + 2 * e], c, -m));
-          const float p1 = ex2_approx(fmaf(s[chunk * 32 + 2 * e + 1], c, -m));
-          rowsum += p0 + p1;
-          packed[e] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(lane_base + col_s(st) + chunk * 16, packed);
-      }
-      l += rowsum;
-      tmem_wait_st();
+      // the O columns are read (tcgen05.ld waited): the next unit's PV may overwrite them
       tc_fence_before();
-      mbar_arrive(&bar_p[st]);
-    }
-    if (ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&bar_o, 0, p.status, kDevTimeoutMma))) {
-      tc_fence_after();
-      const float inv_l = 1.0f / l;
-      __nv_bfloat16* orow = p.o + static_cast<long long>(b) * p.o_sb + static_cast<long long>(head) * p.o_sh +
-                            static_cast<long long>(qrow) * p.o_ss;
-#pragma unroll 1
-      for (int dc = 0; dc < kD; dc += 32) {
-        uint32_t o_raw[32];
-        tmem_ld32(lane_base + kColO + dc, o_raw);
-        uint32_t packed[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          packed[e] = pack_bf16x2(__uint_as_float(o_raw[2 * e]) * inv_l, __uint_as_float(o_raw[2 * e + 1]) * inv_l);
-        if (qrow < p.sq) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + dc);
-#pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4)
-            dst[v4] = make_uint4(packed[4 * v4], packed[4 * v4 + 1], packed[4 * v4 + 2], packed[4 * v4 + 3]);
-        }
-      }
+      mbar_arrive(&bar_ofree);
+      gbase += n_kv;
     }
   }
 
@@ -819,7 +876,9 @@ int launch(const void* q, const void* k, const void* v, void* o, int batch, int 
   const int smem_bytes = kBytes + 1024;
   if (!ensure_smem_attr(reinterpret_cast<const void*>(&fa2_fwd_d256_kernel), smem_bytes))
     return check_launch("tokmix_fa2_fwd: cudaFuncSetAttribute");
-  fa2_fwd_d256_kernel<<<static_cast<unsigned>(units), kThreads, smem_bytes, stream>>>(mq, mk, mv, p);
+  p.units = static_cast<int>(units);
+  const int grid = static_cast<int>(std::min<long long>(units, std::max(1, device_sm_count())));
+  fa2_fwd_d256_kernel<<<static_cast<unsigned>(grid), kThreads, smem_bytes, stream>>>(mq, mk, mv, p);
   return check_launch("tokmix_fa2_fwd (head_dim 256)");
 }
 
