@@ -5,7 +5,8 @@
 // (:1121-1258).  Maths: references/flash_attention_2.py:27-41, i.e. torch SDPA with
 // is_causal=causal and scale=sm_scale.
 //
-// Design (one CTA = one "pair" of 128-row query tiles that read the same keys/values):
+// Design (a work unit = one "pair" of 128-row query tiles that read the same keys/values; the
+// launch is persistent, one CTA per SM walking its units heaviest first):
 //   * pair = two query heads of one GQA group at the same query rows (heads_q/heads_kv even),
 //     or two consecutive query tiles of one head (plain multi-head attention).  The K/V tiles
 //     are loaded once per pair and used by both tiles' MMAs.
@@ -23,7 +24,7 @@
 //     end divides O by l and stores the bf16 row.
 // TMEM columns: S_0 [0,128)  O_0 [128,128+D)  S_1 [256,384)  O_1 [384,384+D).
 // Every wait is bounded (sm100.cuh): a stuck pipeline sets a status bit and the CTA drains.
-// head_dim 256 has its own kernel (namespace d256 below): one query tile per CTA, S double-buffered.
+// head_dim 256 has its own kernel (namespace d256 below): one query tile per unit, S double-buffered.
 #include <cuda_runtime.h>
 
 #include <algorithm>
