@@ -505,8 +505,8 @@ int launch(const void* q, const void* k, const void* v, void* o, int batch, int 
 }
 
 // ---------------------------------------------------------------------------------------------
-// head_dim 256.  Two tiles' S and O (2 x (128 + 256) TMEM columns) do not fit in TMEM, so one CTA
-// takes one 128-row query tile and double-buffers S instead: the tensor core computes S(j+1)
+// head_dim 256.  Two tiles' S and O (2 x (128 + 256) TMEM columns) do not fit in TMEM, so a work
+// unit is one 128-row query tile, and S is double-buffered instead: the tensor core computes S(j+1)
 // while the softmax warps work on S(j).  Keys come in tiles of 128 (S(j) is one N=128 product
 // per 16-column step of Q, PV(j) a K=128 product), with K(j) and V(j) single-buffered (64 KB
 // each; Q 64 KB: 192 KB of shared memory).  Order of the MMAs: S(0) | S(1) PV(0) | S(2) PV(1) |
